@@ -1,0 +1,146 @@
+"""Region bundles (the reference's artifact layout, docs/artifacts.md:174-190:
+kernels/<id>.launch.json + swap_table.json + patch/wrappers.py) for the
+targets, and the generator that writes them.
+
+`python -m metal_autotune_b200.bundles` rewrites the committed bundles.
+"""
+from __future__ import annotations
+
+import json
+import math
+import shutil
+from pathlib import Path
+
+from ..autotuner_runtime.kernels import KernelSpec, write_spec
+
+HERE = Path(__file__).resolve().parent
+WRAPPERS = HERE / "qwen3_wrappers.py"
+
+QMM_GROUP, QMM_BITS = 64, 4
+
+
+def _ws(n_total: str, kind: int):
+    return {"workspace": {"query": "mt_qmm_workspace_bytes",
+                          "args": [{"expr": "in0.shape[0]"}, {"expr": n_total}, {"expr": "in0.shape[1]"},
+                                   {"int": QMM_BITS}, {"int": kind}]}}
+
+
+def qwen3_specs(eps: float = 1e-6, rope_theta: float = 1e6, head_dim: int = 128) -> list[KernelSpec]:
+    """Shape-generic specs of every Qwen3 region (2-D [tokens, features] activations)."""
+    S = []
+    S.append(KernelSpec(
+        kernel_id="rms_norm", name="mt_rms_norm", input_names=("in0", "in1"), output_names=("out0",),
+        cuda={"symbol": "mt_rms_norm", "args": [
+            {"in": 0}, {"in": 1}, {"float": eps}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in0.shape[1]"},
+            {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]"),), output_dtypes=("in0",), reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="qkv_qmm", name="mt_quantized_matmul_multi", input_names=tuple(f"in{i}" for i in range(10)),
+        output_names=("out0", "out1", "out2"),
+        cuda={"symbol": "mt_quantized_matmul_multi", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"in": 3}, {"out": 0}, {"expr": "in1.shape[0]"},
+            {"in": 4}, {"in": 5}, {"in": 6}, {"out": 1}, {"expr": "in4.shape[0]"},
+            {"in": 7}, {"in": 8}, {"in": 9}, {"out": 2}, {"expr": "in7.shape[0]"},
+            {"expr": "in0.shape[0]"}, {"expr": "in0.shape[1]"}, {"int": QMM_GROUP}, {"int": QMM_BITS},
+            {"dtype": "in0"}, _ws("in1.shape[0] + in4.shape[0] + in7.shape[0]", 0), {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in1.shape[0]"), ("in0.shape[0]", "in4.shape[0]"),
+                       ("in0.shape[0]", "in7.shape[0]")),
+        output_dtypes=("in0", "in0", "in0"), fallback_predicate="in0.shape[1] % 64 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="qk_norm_rope_cache", name="mt_qk_norm_rope_cache", input_names=tuple(f"in{i}" for i in range(7)),
+        output_names=("out0",),
+        cuda={"symbol": "mt_qk_norm_rope_cache", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"expr": "in0.shape[1]"}, {"expr": "in1.shape[1]"}, {"in": 3},
+            {"in": 4}, {"float": eps}, {"out": 0}, {"in": 5}, {"in": 6}, {"expr": "in0.shape[0]"},
+            {"expr": f"in0.shape[1] // {head_dim}"}, {"expr": f"in1.shape[1] // {head_dim}"}, {"int": head_dim},
+            {"expr": "in5.shape[1]"}, {"scalar": "offset"}, {"float": rope_theta}, {"dtype": "in0"},
+            {"stream": True}]},
+        output_shapes=((f"in0.shape[1] // {head_dim}", "in0.shape[0]", str(head_dim)),), output_dtypes=("in0",),
+        fallback_predicate=f"in0.shape[1] % {head_dim} != 0 or in5.shape[2] != {head_dim}", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="sdpa_causal_gqa", name="mt_sdpa", input_names=("in0", "in1", "in2"), output_names=("out0",),
+        cuda={"symbol": "mt_sdpa", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"int": 1}, {"expr": "in0.shape[0]"},
+            {"expr": "in1.shape[0]"}, {"expr": "in0.shape[1]"}, {"scalar": "kv_len"}, {"expr": "in0.shape[2]"},
+            {"float": 1.0 / math.sqrt(head_dim)}, {"int": 1}, {"scalar": "offset"},
+            {"int": 0}, {"expr": "in0.shape[1] * in0.shape[2]"}, {"expr": "in0.shape[2]"},
+            {"int": 0}, {"expr": "in1.shape[1] * in1.shape[2]"}, {"expr": "in1.shape[2]"},
+            {"int": 0}, {"expr": "in2.shape[1] * in2.shape[2]"}, {"expr": "in2.shape[2]"},
+            {"int": 0}, {"expr": "in0.shape[2]"}, {"expr": "in0.shape[0] * in0.shape[2]"},
+            {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[1]", "in0.shape[0] * in0.shape[2]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[2] != 128 and in0.shape[2] != 64", reassociates=True))
+    for kid in ("o_proj_residual", "down_proj_residual"):
+        S.append(KernelSpec(
+            kernel_id=kid, name="mt_quantized_matmul_residual", input_names=tuple(f"in{i}" for i in range(5)),
+            output_names=("out0",),
+            cuda={"symbol": "mt_quantized_matmul_residual", "args": [
+                {"in": 0}, {"in": 1}, {"in": 2}, {"in": 3}, {"in": 4}, {"out": 0}, {"expr": "in0.shape[0]"},
+                {"expr": "in1.shape[0]"}, {"expr": "in0.shape[1]"}, {"int": QMM_GROUP}, {"int": QMM_BITS},
+                {"dtype": "in0"}, _ws("in1.shape[0]", 0), {"stream": True}]},
+            output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",),
+            fallback_predicate="in0.shape[1] % 64 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="gate_up_swiglu", name="mt_quantized_matmul_swiglu", input_names=tuple(f"in{i}" for i in range(7)),
+        output_names=("out0",),
+        cuda={"symbol": "mt_quantized_matmul_swiglu", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"in": 3}, {"in": 4}, {"in": 5}, {"in": 6}, {"out": 0},
+            {"expr": "in0.shape[0]"}, {"expr": "in1.shape[0]"}, {"expr": "in0.shape[1]"}, {"int": QMM_GROUP},
+            {"int": QMM_BITS}, {"dtype": "in0"}, _ws("2 * in1.shape[0]", 1), {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[1] % 64 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="quantized_embedding", name="mt_quantized_embedding", input_names=("in0", "in1", "in2", "in3"),
+        output_names=("out0",),
+        cuda={"symbol": "mt_quantized_embedding", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"in": 3}, {"out": 0}, {"expr": "in0.shape[0]"},
+            {"expr": "in1.shape[0]"}, {"expr": f"in1.shape[1] * {32 // QMM_BITS}"}, {"int": QMM_GROUP},
+            {"int": QMM_BITS}, {"dtype": "in2"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", f"in1.shape[1] * {32 // QMM_BITS}"),), output_dtypes=("in2",)))
+    S.append(KernelSpec(
+        kernel_id="lm_head", name="mt_quantized_matmul", input_names=("in0", "in1", "in2", "in3"),
+        output_names=("out0",),
+        cuda={"symbol": "mt_quantized_matmul", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"in": 3}, {"out": 0}, {"expr": "in0.shape[0]"},
+            {"expr": "in1.shape[0]"}, {"expr": "in0.shape[1]"}, {"int": QMM_GROUP}, {"int": QMM_BITS},
+            {"dtype": "in0"}, _ws("in1.shape[0]", 0), {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[1] % 64 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="logits_pick", name="mt_logits_pick", input_names=("in0",),
+        output_names=("out0", "out1", "out2"),
+        cuda={"symbol": "mt_logits_pick", "args": [
+            {"in": 0}, {"expr": "in0.shape[0] * in0.shape[1]"}, {"dtype": "in0"}, {"out": 0}, {"out": 1},
+            {"out": 2}, {"stream": True}]},
+        output_shapes=(("1",), ("1",), ("1",)), output_dtypes=("int32", "float32", "float32"),
+        fallback_predicate="in0.shape[0] != 1"))
+    return S
+
+
+LAYER_KERNELS = ["rms_norm", "qkv_qmm", "qk_norm_rope_cache", "sdpa_causal_gqa", "o_proj_residual",
+                 "gate_up_swiglu", "down_proj_residual"]
+ROOT_KERNELS = ["quantized_embedding", "rms_norm", "lm_head", "logits_pick"]
+
+
+def write_qwen3_bundle(directory: str | Path, n_layers: int) -> Path:
+    d = Path(directory)
+    (d / "kernels").mkdir(parents=True, exist_ok=True)
+    (d / "patch").mkdir(exist_ok=True)
+    for spec in qwen3_specs():
+        write_spec(d / "kernels", spec)
+    table = [{"scope_path": f"layers.{i}", "wrapper_class": "W_qwen3_layer", "kernel_ids": LAYER_KERNELS}
+             for i in range(n_layers)]
+    table.append({"scope_path": "", "wrapper_class": "W_qwen3_root", "kernel_ids": ROOT_KERNELS})
+    (d / "swap_table.json").write_text(json.dumps(table, indent=1) + "\n")
+    shutil.copyfile(WRAPPERS, d / "patch" / "wrappers.py")
+    (d / "bundle.json").write_text(json.dumps({"target": "qwen3", "layers": n_layers}, indent=1) + "\n")
+    return d
+
+
+def main() -> None:
+    write_qwen3_bundle(HERE / "qwen3_4b", 36)
+    write_qwen3_bundle(HERE / "qwen3_tiny", 2)
+
+
+if __name__ == "__main__":
+    main()

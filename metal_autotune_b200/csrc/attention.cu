@@ -1,0 +1,285 @@
+// Causal GQA scaled-dot-product attention, flash-style (online softmax).
+//
+// One CTA = 4 warps = 64 query rows of one (batch, head); each warp owns 16
+// rows. K/V blocks of 64 keys are double-buffered in shared memory with
+// cp.async (XOR-swizzled 16-byte chunks so ldmatrix is conflict-free).
+// S = Q K^T and O += P V run on mma.sync m16n8k16 (bf16/fp16 in, fp32
+// accumulate); softmax statistics stay in fp32 registers, P is rounded to
+// the input type for the P V product. Causal blocks past the diagonal are
+// never loaded. At the Qwen3 prefill size (L = 128, 32 heads) the whole op
+// is a few microseconds and latency-bound.
+#include "mt_common.cuh"
+
+namespace mt {
+
+struct SdpaParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t qs_b, qs_h, qs_l, ks_b, ks_h, ks_l, vs_b, vs_h, vs_l, os_b, os_h, os_l;
+  int Hq, Hkv, Lq, Lk;
+  int64_t q_offset;
+  float scale_log2;  // scale * log2(e)
+  int causal;
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = smem_addr(dst);
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <int DT>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (DT == MT_BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (DT == MT_BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// byte offset of 16-byte chunk c of row r in a tile whose rows are D*2 bytes
+template <int D>
+__device__ __forceinline__ int swz(int r, int c) {
+  return r * (D * 2) + ((c ^ (r & 7)) << 4);
+}
+
+template <int DT, int D>
+__global__ void __launch_bounds__(128) sdpa_kernel(const SdpaParams p) {
+  using T = typename Elem<DT>::T;
+  constexpr int BQ = 64, BKV = 64;
+  constexpr int CH = D / 8;  // 16-byte chunks per row
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint8_t* sq = sm;
+  uint8_t* sk = sm + BQ * D * 2;           // 2 buffers
+  uint8_t* sv = sk + 2 * BKV * D * 2;      // 2 buffers
+
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q0 = qb * BQ;
+  const T* qg = static_cast<const T*>(p.q) + b * p.qs_b + h * p.qs_h;
+  const T* kg = static_cast<const T*>(p.k) + b * p.ks_b + kvh * p.ks_h;
+  const T* vg = static_cast<const T*>(p.v) + b * p.vs_b + kvh * p.vs_h;
+
+  griddep_wait();
+  // keys this block can see: causal limit of its last query row
+  int kend = p.Lk;
+  if (p.causal) {
+    const int64_t lim = p.q_offset + q0 + BQ;  // exclusive
+    if (lim < kend) kend = static_cast<int>(lim < 0 ? 0 : lim);
+  }
+  const int nkb = (kend + BKV - 1) / BKV;
+
+  for (int i = tid; i < BQ * CH; i += 128) {
+    const int r = i / CH, c = i % CH;
+    const bool ok = q0 + r < p.Lq;
+    cp_async16(sq + swz<D>(r, c), qg + static_cast<int64_t>(ok ? q0 + r : 0) * p.qs_l + c * 8, ok);
+  }
+  auto load_kv = [&](int kb, int buf) {
+    for (int i = tid; i < BKV * CH; i += 128) {
+      const int r = i / CH, c = i % CH;
+      const int key = kb * BKV + r;
+      const bool ok = key < p.Lk;
+      const int kk = ok ? key : 0;
+      cp_async16(sk + buf * BKV * D * 2 + swz<D>(r, c), kg + static_cast<int64_t>(kk) * p.ks_l + c * 8, ok);
+      cp_async16(sv + buf * BKV * D * 2 + swz<D>(r, c), vg + static_cast<int64_t>(kk) * p.vs_l + c * 8, ok);
+    }
+  };
+  if (nkb > 0) load_kv(0, 0);
+  cp_async_commit();
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  const int g = lane >> 2, t4 = lane & 3;
+  const int row0 = q0 + warp * 16 + g;  // rows row0 and row0 + 8
+
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int buf = kb & 1;
+    if (kb + 1 < nkb) load_kv(kb + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+
+    const uint32_t qbase = smem_addr(sq);
+    const uint32_t kbase = smem_addr(sk + buf * BKV * D * 2);
+    const uint32_t vbase = smem_addr(sv + buf * BKV * D * 2);
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4];
+      {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kk * 2 + (lane >> 4);
+        ldsm_x4(qbase + swz<D>(r, c), a[0], a[1], a[2], a[3]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 8; nt += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = nt * 8 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4(kbase + swz<D>(r, c), b0, b1, b2, b3);
+        mma16816<DT>(s[nt], a, b0, b1);
+        mma16816<DT>(s[nt + 1], a, b2, b3);
+      }
+    }
+    // scale, mask, online softmax
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kb * BKV + nt * 8 + 2 * t4 + (e & 1);
+        const int qi = row0 + (e >> 1) * 8;
+        float v = s[nt][e] * p.scale_log2;
+        const bool ok = key < p.Lk && (!p.causal || key <= p.q_offset + qi);
+        v = ok ? v : -INFINITY;
+        s[nt][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float corr[2], base[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float mnew = fmaxf(m_r[r], mx[r]);
+      base[r] = mnew == -INFINITY ? 0.f : mnew;
+      corr[r] = exp2f(m_r[r] - base[r]);
+      m_r[r] = mnew;
+    }
+    float rs[2] = {0.f, 0.f};
+    uint32_t pa[4][4];  // P as A fragments, 4 chunks of 16 keys
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float p0 = exp2f(s[nt][0] - base[0]);
+      const float p1 = exp2f(s[nt][1] - base[0]);
+      const float p2 = exp2f(s[nt][2] - base[1]);
+      const float p3 = exp2f(s[nt][3] - base[1]);
+      rs[0] += p0 + p1;
+      rs[1] += p2 + p3;
+      const int ch = nt >> 1, hi = nt & 1;
+      pa[ch][hi * 2 + 0] = pack2<DT>(p0, p1);
+      pa[ch][hi * 2 + 1] = pack2<DT>(p2, p3);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+      l_r[r] = l_r[r] * corr[r] + rs[r];
+    }
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt) {
+      o[dt][0] *= corr[0];
+      o[dt][1] *= corr[0];
+      o[dt][2] *= corr[1];
+      o[dt][3] *= corr[1];
+    }
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      // A fragment order: (row g, k lo), (row g+8, k lo), (row g, k hi), (row g+8, k hi)
+      const uint32_t a[4] = {pa[ch][0], pa[ch][1], pa[ch][2], pa[ch][3]};
+#pragma unroll
+      for (int dt = 0; dt < D / 8; dt += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = ch * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = dt + (lane >> 4);
+        ldsm_x4_t(vbase + swz<D>(r, c), b0, b1, b2, b3);
+        mma16816<DT>(o[dt], a, b0, b1);
+        mma16816<DT>(o[dt + 1], a, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  griddep_launch();
+  T* og = static_cast<T*>(p.o) + b * p.os_b + h * p.os_h;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int qi = row0 + r * 8;
+    if (qi >= p.Lq) continue;
+    const float inv = l_r[r] > 0.f ? 1.f / l_r[r] : 0.f;
+    T* dst = og + static_cast<int64_t>(qi) * p.os_l;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt) {
+      const int d = dt * 8 + 2 * t4;
+      const uint32_t packed = pack2<DT>(o[dt][2 * r] * inv, o[dt][2 * r + 1] * inv);
+      *reinterpret_cast<uint32_t*>(dst + d) = packed;
+    }
+  }
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" int mt_sdpa(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv,
+                       int64_t Lq, int64_t Lk, int64_t D, float scale, int causal, int64_t q_offset, int64_t qs_b,
+                       int64_t qs_h, int64_t qs_l, int64_t ks_b, int64_t ks_h, int64_t ks_l, int64_t vs_b,
+                       int64_t vs_h, int64_t vs_l, int64_t os_b, int64_t os_h, int64_t os_l, int dtype,
+                       mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(q && k && v && o, "mt_sdpa: null pointer");
+  MT_CHECK_ARG(D == 64 || D == 128, "mt_sdpa: head_dim %lld, only 64 and 128 are built", (long long)D);
+  MT_CHECK_ARG(dtype == MT_BF16 || dtype == MT_F16, "mt_sdpa: dtype must be bf16 or f16");
+  MT_CHECK_ARG(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, "mt_sdpa: Hq=%lld must be a multiple of Hkv=%lld",
+               (long long)Hq, (long long)Hkv);
+  MT_CHECK_ARG(Lq >= 0 && Lk >= 0 && Lq < (1 << 30) && Lk < (1 << 30), "mt_sdpa: bad lengths");
+  MT_CHECK_ARG(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(o, 4) && qs_l % 8 == 0 &&
+                   ks_l % 8 == 0 && vs_l % 8 == 0 && qs_h % 8 == 0 && ks_h % 8 == 0 && vs_h % 8 == 0 &&
+                   qs_b % 8 == 0 && ks_b % 8 == 0 && vs_b % 8 == 0 && os_l % 2 == 0,
+               "mt_sdpa: q/k/v rows must be 16-byte aligned");
+  if (B == 0 || Lq == 0) return MT_OK;
+  SdpaParams p = {q, k, v, o, qs_b, qs_h, qs_l, ks_b, ks_h, ks_l, vs_b, vs_h, vs_l, os_b, os_h, os_l,
+                  (int)Hq, (int)Hkv, (int)Lq, (int)Lk, q_offset, scale * 1.4426950408889634f, causal};
+  const dim3 grid(static_cast<unsigned>((Lq + 63) / 64), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  const size_t smem = static_cast<size_t>(64 * D * 2) * 5;
+  auto run = [&](auto kern) -> int {
+    MT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    return launch(kern, grid, dim3(128), smem, (cudaStream_t)stream, p);
+  };
+  if (dtype == MT_BF16) return D == 128 ? run(sdpa_kernel<MT_BF16, 128>) : run(sdpa_kernel<MT_BF16, 64>);
+  return D == 128 ? run(sdpa_kernel<MT_F16, 128>) : run(sdpa_kernel<MT_F16, 64>);
+}

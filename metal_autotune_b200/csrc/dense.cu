@@ -1,0 +1,69 @@
+// fp32 dense linear (+bias, +GELU) for the GELU-MLP region (tiny MLP).
+//
+// Bit-reproducible: each output accumulates k = 0..K-1 in order with one
+// fused multiply-add per term, adds the bias once, then applies GELU with
+// the shared fixed-sequence erf (mt_math.h). Tiles of 32 x 32 outputs stage
+// x and w through shared memory; the accumulation order is unchanged by the
+// tiling. The tiny MLP is launch-bound (33.5 MFLOP), so this favours
+// exactness over tensor cores (TF32 would change every product).
+#include "mt_common.cuh"
+#include "mt_math.h"
+
+namespace mt {
+
+__global__ void __launch_bounds__(256) linear_f32_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                         const float* __restrict__ bias, float* __restrict__ y,
+                                                         int M, int N, int K, int act) {
+  __shared__ float xs[32][33];
+  __shared__ float wsm[32][33];
+  griddep_wait();
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    for (int i = ty; i < 32; i += 8) {
+      const int m = m0 + i, n = n0 + i, k = k0 + tx;
+      xs[i][tx] = (m < M && k < K) ? x[static_cast<int64_t>(m) * K + k] : 0.f;
+      wsm[i][tx] = (n < N && k < K) ? w[static_cast<int64_t>(n) * K + k] : 0.f;
+    }
+    __syncthreads();
+    const int kmax = K - k0 < 32 ? K - k0 : 32;
+    for (int kk = 0; kk < kmax; ++kk) {
+      const float wv = wsm[tx][kk];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = fmaf(xs[ty + 8 * i][kk], wv, acc[i]);
+    }
+    __syncthreads();
+  }
+  const int n = n0 + tx;
+  if (n < N) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = m0 + ty + 8 * i;
+      if (m >= M) continue;
+      float v = acc[i];
+      if (bias) v = __fadd_rn(v, bias[n]);
+      if (act == 1) v = mt_gelu_f32(v);
+      y[static_cast<int64_t>(m) * N + n] = v;
+    }
+  }
+  griddep_launch();
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" int mt_linear(const void* x, const void* w, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
+                         int act, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && w && y, "mt_linear: null pointer");
+  MT_CHECK_ARG(dtype == MT_F32, "mt_linear: only fp32 is built (dtype %d)", dtype);
+  MT_CHECK_ARG(act == 0 || act == 1, "mt_linear: act must be 0 (identity) or 1 (gelu)");
+  MT_CHECK_ARG(M >= 0 && N > 0 && K > 0 && M < (1 << 30) && N < (1 << 30) && K < (1 << 30),
+               "mt_linear: bad shape");
+  if (M == 0) return MT_OK;
+  const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((M + 31) / 32));
+  return launch(linear_f32_kernel, grid, dim3(256), 0, (cudaStream_t)stream, (const float*)x, (const float*)w,
+                (const float*)bias, (float*)y, (int)M, (int)N, (int)K, act);
+}

@@ -1,0 +1,278 @@
+// Output-diff reduction for the verification ladder: one read of candidate a
+// and reference b produces every statistic the reference's comparison
+// policy needs (autotuner_runtime/numeric.py:50-107, exact.py:5-10,
+// autotuner/ladder/numeric.py:22-35, autotuner/artifact/validate.py:64-103).
+//
+// The per-element excess is computed in fp32 exactly as the policy states it
+// (allowed = max(atol + rtol*|b|, wobble); excess = |a-b| - allowed, with the
+// overflow-safe scaled form where that is NaN), so max/argmax/count match a
+// CPU restatement bit for bit. Block partials go to the workspace in block
+// order and the last block to finish (atomic counter) folds them in that
+// order, so the fp64 cosine sums do not depend on scheduling either. The
+// block count depends only on n.
+#include "mt_common.cuh"
+
+namespace mt {
+
+struct DiffPartial {
+  float max_excess;
+  float max_abs;
+  float amax_a, amax_b;
+  int64_t excess_index;
+  int64_t over, viol, first_viol, mism, first_mism, nan_ex;
+  double dab, daa, dbb;
+};
+
+__device__ __forceinline__ void merge(DiffPartial& x, const DiffPartial& y) {
+  if (y.excess_index >= 0 &&
+      (x.excess_index < 0 || y.max_excess > x.max_excess ||
+       (y.max_excess == x.max_excess && y.excess_index < x.excess_index))) {
+    x.max_excess = y.max_excess;
+    x.excess_index = y.excess_index;
+  }
+  x.max_abs = fmaxf(x.max_abs, y.max_abs);
+  x.amax_a = fmaxf(x.amax_a, y.amax_a);
+  x.amax_b = fmaxf(x.amax_b, y.amax_b);
+  x.over += y.over;
+  x.viol += y.viol;
+  x.mism += y.mism;
+  x.nan_ex += y.nan_ex;
+  if (y.first_viol >= 0 && (x.first_viol < 0 || y.first_viol < x.first_viol)) x.first_viol = y.first_viol;
+  if (y.first_mism >= 0 && (x.first_mism < 0 || y.first_mism < x.first_mism)) x.first_mism = y.first_mism;
+  x.dab += y.dab;
+  x.daa += y.daa;
+  x.dbb += y.dbb;
+}
+
+__device__ __forceinline__ void init(DiffPartial& x) {
+  x.max_excess = 0.f;
+  x.max_abs = 0.f;
+  x.amax_a = 0.f;
+  x.amax_b = 0.f;
+  x.excess_index = -1;
+  x.over = x.viol = x.mism = x.nan_ex = 0;
+  x.first_viol = x.first_mism = -1;
+  x.dab = x.daa = x.dbb = 0.0;
+}
+
+template <typename T> __device__ __forceinline__ float fval(T v);
+template <> __device__ __forceinline__ float fval<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float fval<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float fval<float>(float v) { return v; }
+
+template <typename T> struct Bits;
+template <> struct Bits<__nv_bfloat16> { using U = uint16_t; };
+template <> struct Bits<__half> { using U = uint16_t; };
+template <> struct Bits<float> { using U = uint32_t; };
+
+// float element: full policy
+template <typename T>
+__device__ __forceinline__ void visit_float(const T av, const T bv, int64_t i, float rtol, float atol, float wobble,
+                                            DiffPartial& p) {
+  using U = typename Bits<T>::U;
+  if (*reinterpret_cast<const U*>(&av) != *reinterpret_cast<const U*>(&bv)) {
+    ++p.mism;
+    if (p.first_mism < 0) p.first_mism = i;
+  }
+  const float c = fval<T>(av), r = fval<T>(bv);
+  const bool cf = isfinite(c), rf = isfinite(r);
+  const bool ok = (rf && cf) || (isnan(r) && isnan(c)) || (isinf(r) && c == r);
+  if (!ok) {
+    ++p.viol;
+    if (p.first_viol < 0) p.first_viol = i;
+  }
+  float excess = 0.f;
+  if (rf && ok) {
+    const float allowed = fmaxf(__fadd_rn(atol, __fmul_rn(rtol, fabsf(r))), wobble);
+    const float ad = fabsf(__fsub_rn(c, r));
+    excess = __fsub_rn(ad, allowed);
+    if (isnan(excess)) {
+      const float scale = fmaxf(fmaxf(fabsf(c), fabsf(r)), 1.0f);
+      const float cs = __fdiv_rn(c, scale), rs = __fdiv_rn(r, scale);
+      const float se = __fsub_rn(fabsf(__fsub_rn(cs, rs)),
+                                 __fadd_rn(__fdiv_rn(atol, scale), __fmul_rn(rtol, fabsf(rs))));
+      excess = __fmul_rn(se, scale);
+    }
+    p.max_abs = fmaxf(p.max_abs, ad);
+  }
+  if (isnan(excess)) {
+    ++p.nan_ex;
+  } else {
+    if (excess > 0.f) ++p.over;
+    if (p.excess_index < 0 || excess > p.max_excess) {
+      p.max_excess = excess;
+      p.excess_index = i;
+    }
+  }
+  const float a0 = cf ? c : 0.f, b0 = rf ? r : 0.f;
+  p.amax_a = fmaxf(p.amax_a, fabsf(a0));
+  p.amax_b = fmaxf(p.amax_b, fabsf(b0));
+  p.dab += static_cast<double>(a0) * static_cast<double>(b0);
+  p.daa += static_cast<double>(a0) * static_cast<double>(a0);
+  p.dbb += static_cast<double>(b0) * static_cast<double>(b0);
+}
+
+template <typename U>
+__device__ __forceinline__ void visit_bits(const U av, const U bv, int64_t i, DiffPartial& p) {
+  if (av != bv) {
+    ++p.mism;
+    if (p.first_mism < 0) p.first_mism = i;
+  }
+}
+
+constexpr int kDiffThreads = 256;
+
+static inline int diff_blocks(int64_t n) {
+  const int64_t b = (n + 8191) / 8192;
+  return static_cast<int>(b < 1 ? 1 : (b > 512 ? 512 : b));
+}
+
+template <typename T, bool FLOAT>
+__global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict__ a, const T* __restrict__ b, int64_t n,
+                                                            float rtol, float atol, float wobble,
+                                                            DiffPartial* __restrict__ parts, uint32_t* counter,
+                                                            mt_diff_stats* __restrict__ out) {
+  __shared__ DiffPartial sp[kDiffThreads / 32];
+  __shared__ int am_last;
+  griddep_wait();
+  DiffPartial p;
+  init(p);
+  // contiguous slice per block, strided by thread inside it: every index is
+  // visited once and each thread's indices increase (first-index tracking)
+  const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * per;
+  const int64_t hi = lo + per < n ? lo + per : n;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += kDiffThreads) {
+    if constexpr (FLOAT) visit_float<T>(a[i], b[i], i, rtol, atol, wobble, p);
+    else visit_bits<T>(a[i], b[i], i, p);
+  }
+  // warp then block merge, fixed order
+  for (int o = 1; o < 32; o <<= 1) {
+    DiffPartial q;
+    q.max_excess = __shfl_down_sync(0xffffffffu, p.max_excess, o);
+    q.max_abs = __shfl_down_sync(0xffffffffu, p.max_abs, o);
+    q.amax_a = __shfl_down_sync(0xffffffffu, p.amax_a, o);
+    q.amax_b = __shfl_down_sync(0xffffffffu, p.amax_b, o);
+    q.excess_index = __shfl_down_sync(0xffffffffu, p.excess_index, o);
+    q.over = __shfl_down_sync(0xffffffffu, p.over, o);
+    q.viol = __shfl_down_sync(0xffffffffu, p.viol, o);
+    q.first_viol = __shfl_down_sync(0xffffffffu, p.first_viol, o);
+    q.mism = __shfl_down_sync(0xffffffffu, p.mism, o);
+    q.first_mism = __shfl_down_sync(0xffffffffu, p.first_mism, o);
+    q.nan_ex = __shfl_down_sync(0xffffffffu, p.nan_ex, o);
+    q.dab = __shfl_down_sync(0xffffffffu, p.dab, o);
+    q.daa = __shfl_down_sync(0xffffffffu, p.daa, o);
+    q.dbb = __shfl_down_sync(0xffffffffu, p.dbb, o);
+    if ((threadIdx.x & 31) + o < 32) merge(p, q);
+  }
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) sp[warp] = p;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    DiffPartial acc = sp[0];
+    for (int w = 1; w < kDiffThreads / 32; ++w) merge(acc, sp[w]);
+    parts[blockIdx.x] = acc;
+    __threadfence();
+    const uint32_t prev = atomicAdd(counter, 1u);
+    am_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (am_last && threadIdx.x == 0) {
+    __threadfence();
+    DiffPartial acc;
+    init(acc);
+    for (unsigned blk = 0; blk < gridDim.x; ++blk) {
+      DiffPartial q;
+      const volatile DiffPartial* src = parts + blk;
+      q.max_excess = src->max_excess;
+      q.max_abs = src->max_abs;
+      q.amax_a = src->amax_a;
+      q.amax_b = src->amax_b;
+      q.excess_index = src->excess_index;
+      q.over = src->over;
+      q.viol = src->viol;
+      q.first_viol = src->first_viol;
+      q.mism = src->mism;
+      q.first_mism = src->first_mism;
+      q.nan_ex = src->nan_ex;
+      q.dab = src->dab;
+      q.daa = src->daa;
+      q.dbb = src->dbb;
+      merge(acc, q);
+    }
+    out->max_excess = acc.max_excess;
+    out->max_abs = acc.max_abs;
+    out->dot_ab = acc.dab;
+    out->dot_aa = acc.daa;
+    out->dot_bb = acc.dbb;
+    out->amax_a = acc.amax_a;
+    out->amax_b = acc.amax_b;
+    out->excess_index = acc.excess_index;
+    out->over_count = acc.over;
+    out->nonfinite_violations = acc.viol;
+    out->first_violation = acc.first_viol;
+    out->bit_mismatches = acc.mism;
+    out->first_mismatch = acc.first_mism;
+    out->nan_excess = acc.nan_ex;
+    *counter = 0;  // ready for the next call
+  }
+  griddep_launch();
+}
+
+size_t diff_workspace(int64_t n) { return 256 + static_cast<size_t>(diff_blocks(n)) * sizeof(DiffPartial); }
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" {
+
+size_t mt_diff_workspace_bytes(int64_t n) { return diff_workspace(n); }
+
+int mt_diff_reduce(const void* a, const void* b, int64_t n, int dtype, float rtol, float atol, float wobble,
+                   mt_diff_stats* stats, void* workspace, size_t workspace_bytes, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(stats, "mt_diff_reduce: stats is NULL");
+  MT_CHECK_ARG(n >= 0, "mt_diff_reduce: negative size");
+  MT_CHECK_ARG(n == 0 || (a && b), "mt_diff_reduce: null input");
+  if (!workspace || workspace_bytes < diff_workspace(n) || !aligned(workspace, 256)) {
+    set_error("mt_diff_reduce: workspace of %zu bytes (256-aligned, zero-filled) required, got %zu",
+              diff_workspace(n), workspace_bytes);
+    return MT_ERR_WORKSPACE;
+  }
+  uint32_t* counter = static_cast<uint32_t*>(workspace);
+  DiffPartial* parts = reinterpret_cast<DiffPartial*>(static_cast<uint8_t*>(workspace) + 256);
+  const dim3 grid(diff_blocks(n)), block(kDiffThreads);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (dtype) {
+    case MT_BF16:
+      return launch(diff_kernel<__nv_bfloat16, true>, grid, block, 0, s, (const __nv_bfloat16*)a,
+                    (const __nv_bfloat16*)b, n, rtol, atol, wobble, parts, counter, stats);
+    case MT_F16:
+      return launch(diff_kernel<__half, true>, grid, block, 0, s, (const __half*)a, (const __half*)b, n, rtol, atol,
+                    wobble, parts, counter, stats);
+    case MT_F32:
+      return launch(diff_kernel<float, true>, grid, block, 0, s, (const float*)a, (const float*)b, n, rtol, atol,
+                    wobble, parts, counter, stats);
+    case MT_I32:
+    case MT_U32:
+      return launch(diff_kernel<uint32_t, false>, grid, block, 0, s, (const uint32_t*)a, (const uint32_t*)b, n, rtol,
+                    atol, wobble, parts, counter, stats);
+    case MT_I64:
+    case MT_U64:
+      return launch(diff_kernel<unsigned long long, false>, grid, block, 0, s, (const unsigned long long*)a,
+                    (const unsigned long long*)b, n, rtol, atol, wobble, parts, counter, stats);
+    case MT_I16:
+    case MT_U16:
+      return launch(diff_kernel<uint16_t, false>, grid, block, 0, s, (const uint16_t*)a, (const uint16_t*)b, n, rtol,
+                    atol, wobble, parts, counter, stats);
+    case MT_U8:
+    case MT_I8:
+    case MT_BOOL:
+      return launch(diff_kernel<uint8_t, false>, grid, block, 0, s, (const uint8_t*)a, (const uint8_t*)b, n, rtol,
+                    atol, wobble, parts, counter, stats);
+    default: set_error("mt_diff_reduce: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
+  }
+}
+
+}  // extern "C"

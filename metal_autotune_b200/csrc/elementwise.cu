@@ -1,0 +1,220 @@
+// Elementwise and gather regions: SwiGLU, the quantized embedding gather and
+// the greedy pick from the last row of logits.
+#include "mt_common.cuh"
+#include "qmm_common.cuh"
+
+namespace mt {
+
+template <int DT>
+__global__ void __launch_bounds__(256) swiglu_kernel(const void* __restrict__ gp, const void* __restrict__ up,
+                                                     void* __restrict__ yp, int64_t n) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  const T* g = static_cast<const T*>(gp);
+  const T* u = static_cast<const T*>(up);
+  T* y = static_cast<T*>(yp);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = Elem<DT>::from_f(swiglu_rounded<DT>(Elem<DT>::to_f(g[i]), Elem<DT>::to_f(u[i])));
+  griddep_launch();
+}
+
+// out[t, k] = round(round(s*q) + b) for token tok[t]; one CTA per token.
+template <int DT>
+__global__ void __launch_bounds__(256) qembed_kernel(const int32_t* __restrict__ tokens, const uint32_t* __restrict__ w,
+                                                     const void* __restrict__ sp, const void* __restrict__ bp,
+                                                     void* __restrict__ outp, int64_t vocab, int D, int group,
+                                                     int bits) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  const int t = blockIdx.x;
+  const int tok = tokens[t];
+  T* out = static_cast<T*>(outp) + static_cast<int64_t>(t) * D;
+  if (tok < 0 || tok >= vocab) {
+    for (int k = threadIdx.x; k < D; k += blockDim.x) out[k] = Elem<DT>::from_f(0.f);
+    if (threadIdx.x == 0) report_status(0x601);
+    return;
+  }
+  const int per = 32 / bits;
+  const int G = D / group;
+  const uint32_t* wr = w + static_cast<int64_t>(tok) * (D / per);
+  const T* sr = static_cast<const T*>(sp) + static_cast<int64_t>(tok) * G;
+  const T* br = static_cast<const T*>(bp) + static_cast<int64_t>(tok) * G;
+  const uint32_t mask = (1u << bits) - 1u;
+  for (int k = threadIdx.x; k < D; k += blockDim.x) {
+    const uint32_t q = (wr[k / per] >> ((k % per) * bits)) & mask;
+    const float s = Elem<DT>::to_f(sr[k / group]);
+    const float b = Elem<DT>::to_f(br[k / group]);
+    const float sq = round_to<DT>(__fmul_rn(s, static_cast<float>(q)));
+    out[k] = Elem<DT>::from_f(__fadd_rn(sq, b));
+  }
+  griddep_launch();
+}
+
+// Single CTA of 1024 threads: pass 1 logsumexp (per-thread online max/sum,
+// fixed-order tree), pass 2 argmax of round(x - round(lse)) with the lowest
+// index on ties, as mlx-lm's `logits - logsumexp(logits)` then argmax.
+template <int DT>
+__global__ void __launch_bounds__(1024) logits_pick_kernel(const void* __restrict__ lp, int64_t n,
+                                                           int32_t* __restrict__ token, float* __restrict__ logprob,
+                                                           float* __restrict__ lse_out) {
+  using T = typename Elem<DT>::T;
+  __shared__ float sm_m[32], sm_s[32];
+  __shared__ int64_t sm_i[32];
+  __shared__ float sh_lse;
+  griddep_wait();
+  const T* x = static_cast<const T*>(lp);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float m = -INFINITY, s = 0.f;
+  for (int64_t i = tid; i < n; i += 1024) {
+    const float v = Elem<DT>::to_f(x[i]);
+    if (v > m) {
+      s = s * expf(m - v) + 1.f;
+      m = v;
+    } else if (v == -INFINITY && m == -INFINITY) {
+      // exp(-inf - -inf) is undefined; an all -inf prefix contributes nothing
+    } else {
+      s += expf(v - m);
+    }
+  }
+  // combine (m, s) pairs in a fixed tree
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mn = fmaxf(m, m2);
+    s = (mn == -INFINITY) ? 0.f : s * expf(m - mn) + s2 * expf(m2 - mn);
+    m = mn;
+  }
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_s[warp] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    m = sm_m[lane];
+    s = sm_s[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float mn = fmaxf(m, m2);
+      s = (mn == -INFINITY) ? 0.f : s * expf(m - mn) + s2 * expf(m2 - mn);
+      m = mn;
+    }
+    if (lane == 0) sh_lse = m + logf(s);
+  }
+  __syncthreads();
+  const float lse = sh_lse;
+  const float lse_r = round_to<DT>(lse);
+  float best = -INFINITY;
+  int64_t bi = -1;
+  for (int64_t i = tid; i < n; i += 1024) {
+    const float v = round_to<DT>(__fsub_rn(Elem<DT>::to_f(x[i]), lse_r));
+    if (v > best || bi < 0) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (i2 >= 0 && (b2 > best || (b2 == best && (i2 < bi || bi < 0)) || bi < 0)) {
+      best = b2;
+      bi = i2;
+    }
+  }
+  __syncthreads();
+  if (lane == 0) {
+    sm_m[warp] = best;
+    sm_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = sm_m[lane];
+    bi = sm_i[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (i2 >= 0 && (b2 > best || (b2 == best && (i2 < bi || bi < 0)) || bi < 0)) {
+        best = b2;
+        bi = i2;
+      }
+    }
+    if (lane == 0) {
+      *token = static_cast<int32_t>(bi);
+      *logprob = best;
+      if (lse_out) *lse_out = lse;
+    }
+  }
+  griddep_launch();
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" {
+
+int mt_swiglu(const void* gate, const void* up, void* y, int64_t n, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(gate && up && y, "mt_swiglu: null pointer");
+  MT_CHECK_ARG(n >= 0, "mt_swiglu: negative size");
+  if (n == 0) return MT_OK;
+  int sms = 148;
+  int rc = device_sm_count(&sms);
+  if (rc) return rc;
+  const int64_t want = (n + 255) / 256;
+  const dim3 grid(static_cast<unsigned>(want < sms * 16 ? want : sms * 16));
+  switch (dtype) {
+    case MT_BF16: return launch(swiglu_kernel<MT_BF16>, grid, dim3(256), 0, (cudaStream_t)stream, gate, up, y, n);
+    case MT_F16: return launch(swiglu_kernel<MT_F16>, grid, dim3(256), 0, (cudaStream_t)stream, gate, up, y, n);
+    case MT_F32: return launch(swiglu_kernel<MT_F32>, grid, dim3(256), 0, (cudaStream_t)stream, gate, up, y, n);
+    default: set_error("mt_swiglu: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
+  }
+}
+
+int mt_quantized_embedding(const int32_t* tokens, const uint32_t* w, const void* scales, const void* biases,
+                           void* out, int64_t T, int64_t vocab, int64_t D, int group_size, int bits, int dtype,
+                           mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(tokens && w && scales && biases && out, "mt_quantized_embedding: null pointer");
+  MT_CHECK_ARG(bits == 4 || bits == 8, "mt_quantized_embedding: bits=%d", bits);
+  MT_CHECK_ARG(group_size == 32 || group_size == 64 || group_size == 128, "mt_quantized_embedding: group %d",
+               group_size);
+  MT_CHECK_ARG(D > 0 && D % group_size == 0 && D < (1 << 24) && vocab > 0 && T >= 0 && T < (1 << 30),
+               "mt_quantized_embedding: bad shape");
+  if (T == 0) return MT_OK;
+  const dim3 grid(static_cast<unsigned>(T));
+  if (dtype == MT_BF16)
+    return launch(qembed_kernel<MT_BF16>, grid, dim3(256), 0, (cudaStream_t)stream, tokens, w, scales, biases, out,
+                  vocab, (int)D, group_size, bits);
+  if (dtype == MT_F16)
+    return launch(qembed_kernel<MT_F16>, grid, dim3(256), 0, (cudaStream_t)stream, tokens, w, scales, biases, out,
+                  vocab, (int)D, group_size, bits);
+  set_error("mt_quantized_embedding: dtype must be bf16 or f16");
+  return MT_ERR_UNSUPPORTED;
+}
+
+int mt_logits_pick(const void* logits, int64_t n, int dtype, int32_t* token, float* logprob, float* lse,
+                   mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(logits && token && logprob, "mt_logits_pick: null pointer");
+  MT_CHECK_ARG(n > 0, "mt_logits_pick: empty row");
+  switch (dtype) {
+    case MT_BF16:
+      return launch(logits_pick_kernel<MT_BF16>, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, n, token,
+                    logprob, lse);
+    case MT_F16:
+      return launch(logits_pick_kernel<MT_F16>, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, n, token,
+                    logprob, lse);
+    case MT_F32:
+      return launch(logits_pick_kernel<MT_F32>, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, n, token,
+                    logprob, lse);
+    default: set_error("mt_logits_pick: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
+  }
+}
+
+}  // extern "C"

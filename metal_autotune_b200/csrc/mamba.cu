@@ -1,0 +1,187 @@
+// Mamba-1 selective scan and depthwise causal conv1d.
+//
+// Scan: lanes (channel, state) — d_state lanes per channel, 32/d_state
+// channels per warp — hold h in fp32 registers and walk the L steps in
+// order; y_t = sum_s C[t,s] h[s] is a shuffle reduction inside the channel's
+// lane group. The recurrence is sequential in t, so one channel's latency
+// is L dependent steps; channels are independent (2048 per Mamba-370m
+// layer) and fill the GPU. Inputs of step t+1 are loaded while step t
+// computes.
+#include "mt_common.cuh"
+
+namespace mt {
+
+__device__ __forceinline__ float softplus_f32(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+template <int DT, int NS>
+__global__ void __launch_bounds__(256) mamba_scan_kernel(const void* __restrict__ xp, const void* __restrict__ dtp,
+                                                         const float* __restrict__ dt_bias, const float* __restrict__ A,
+                                                         const void* __restrict__ Bp, const void* __restrict__ Cp,
+                                                         const float* __restrict__ Dv, const void* __restrict__ zp,
+                                                         void* __restrict__ yp, float* __restrict__ hstate, int L,
+                                                         int d_inner) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  constexpr int CPW = 32 / NS;  // channels per warp
+  const int lane = threadIdx.x & 31;
+  const int s = lane % NS;
+  const int c = (blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5)) * CPW + lane / NS;
+  const bool active = c < d_inner;
+  const int cc = active ? c : 0;
+  const T* x = static_cast<const T*>(xp);
+  const T* dtr = static_cast<const T*>(dtp);
+  const T* Bm = static_cast<const T*>(Bp);
+  const T* Cm = static_cast<const T*>(Cp);
+  const T* z = static_cast<const T*>(zp);
+  T* y = static_cast<T*>(yp);
+  const float a = A[static_cast<int64_t>(cc) * NS + s];
+  const float bias = dt_bias ? dt_bias[cc] : 0.f;
+  const float dd = Dv ? Dv[cc] : 0.f;
+  float h = (hstate && active) ? hstate[static_cast<int64_t>(cc) * NS + s] : 0.f;
+  float nx = Elem<DT>::to_f(x[cc]), ndt = Elem<DT>::to_f(dtr[cc]), nz = Elem<DT>::to_f(z[cc]);
+  float nb = Elem<DT>::to_f(Bm[s]), nc = Elem<DT>::to_f(Cm[s]);
+  for (int t = 0; t < L; ++t) {
+    const float xv = nx, dv = ndt, zv = nz, bv = nb, cv = nc;
+    if (t + 1 < L) {
+      const int64_t r = static_cast<int64_t>(t + 1);
+      nx = Elem<DT>::to_f(x[r * d_inner + cc]);
+      ndt = Elem<DT>::to_f(dtr[r * d_inner + cc]);
+      nz = Elem<DT>::to_f(z[r * d_inner + cc]);
+      nb = Elem<DT>::to_f(Bm[r * NS + s]);
+      nc = Elem<DT>::to_f(Cm[r * NS + s]);
+    }
+    const float dt = softplus_f32(__fadd_rn(dv, bias));
+    const float dA = expf(__fmul_rn(dt, a));
+    h = __fadd_rn(__fmul_rn(dA, h), __fmul_rn(__fmul_rn(dt, bv), xv));
+    float part = __fmul_rn(cv, h);
+#pragma unroll
+    for (int o = NS / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (s == 0 && active) {
+      const float yv = __fadd_rn(part, __fmul_rn(dd, xv));
+      const float sg = 1.0f / (1.0f + expf(-zv));
+      y[static_cast<int64_t>(t) * d_inner + c] = Elem<DT>::from_f(__fmul_rn(yv, __fmul_rn(zv, sg)));
+    }
+  }
+  if (hstate && active) hstate[static_cast<int64_t>(c) * NS + s] = h;
+  griddep_launch();
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) causal_conv1d_kernel(const void* __restrict__ xp, const void* __restrict__ wp,
+                                                            const void* __restrict__ bp, const void* __restrict__ sp,
+                                                            void* __restrict__ yp, int L, int C, int W, int silu) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(L) * C) return;
+  const int l = static_cast<int>(i / C), c = static_cast<int>(i % C);
+  const T* x = static_cast<const T*>(xp);
+  const T* w = static_cast<const T*>(wp) + static_cast<int64_t>(c) * W;
+  const T* st = sp ? static_cast<const T*>(sp) + static_cast<int64_t>(c) * (W - 1) : nullptr;
+  float acc = 0.f;
+  for (int j = 0; j < W; ++j) {
+    const int src = l - (W - 1) + j;
+    float xv;
+    if (src >= 0) xv = Elem<DT>::to_f(x[static_cast<int64_t>(src) * C + c]);
+    else xv = st ? Elem<DT>::to_f(st[W - 1 + src]) : 0.f;
+    acc = fmaf(Elem<DT>::to_f(w[j]), xv, acc);
+  }
+  if (bp) acc = __fadd_rn(acc, Elem<DT>::to_f(static_cast<const T*>(bp)[c]));
+  float v = round_to<DT>(acc);
+  if (silu) {
+    const float sg = round_to<DT>(1.0f / (1.0f + expf(-v)));
+    v = __fmul_rn(v, sg);
+  }
+  static_cast<T*>(yp)[i] = Elem<DT>::from_f(v);
+}
+
+// New state = the last W-1 entries of [old state, x]; one thread per channel
+// shifts its own row in registers, so reading and rewriting the same buffer
+// cannot race.
+template <int DT>
+__global__ void conv_state_kernel(const void* __restrict__ xp, void* sp, int L, int C, int W) {
+  using T = typename Elem<DT>::T;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  T* st = static_cast<T*>(sp) + static_cast<int64_t>(c) * (W - 1);
+  T old[15];
+  for (int j = 0; j < W - 1; ++j) old[j] = st[j];
+  for (int j = 0; j < W - 1; ++j) {
+    const int src = L - (W - 1) + j;  // index into x; negative reaches back into the old state
+    st[j] = src >= 0 ? static_cast<const T*>(xp)[static_cast<int64_t>(src) * C + c] : old[W - 1 + src];
+  }
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" {
+
+int mt_mamba_scan(const void* x, const void* dt_raw, const float* dt_bias, const float* A, const void* Bm,
+                  const void* Cm, const float* Dv, const void* z, void* y, float* h_state, int64_t L,
+                  int64_t d_inner, int64_t d_state, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && dt_raw && A && Bm && Cm && z && y, "mt_mamba_scan: null pointer");
+  MT_CHECK_ARG(d_state == 16 || d_state == 8 || d_state == 32, "mt_mamba_scan: d_state %lld (8, 16 or 32)",
+               (long long)d_state);
+  MT_CHECK_ARG(L >= 0 && d_inner > 0 && L < (1 << 30) && d_inner < (1 << 24), "mt_mamba_scan: bad shape");
+  MT_CHECK_ARG(dtype == MT_BF16 || dtype == MT_F16 || dtype == MT_F32, "mt_mamba_scan: bad dtype");
+  if (L == 0) return MT_OK;
+  const int cpw = 32 / static_cast<int>(d_state);
+  const int64_t warps = (d_inner + cpw - 1) / cpw;
+  const dim3 grid(static_cast<unsigned>((warps + 7) / 8));
+  cudaStream_t s = (cudaStream_t)stream;
+#define MT_SCAN(DTV, NSV)                                                                                   \
+  return launch(mamba_scan_kernel<DTV, NSV>, grid, dim3(256), 0, s, x, dt_raw, dt_bias, A, Bm, Cm, Dv, z, y, \
+                h_state, (int)L, (int)d_inner)
+#define MT_SCAN_NS(DTV)        \
+  if (d_state == 8) MT_SCAN(DTV, 8); \
+  if (d_state == 16) MT_SCAN(DTV, 16); \
+  MT_SCAN(DTV, 32)
+  if (dtype == MT_BF16) { MT_SCAN_NS(MT_BF16); }
+  if (dtype == MT_F16) { MT_SCAN_NS(MT_F16); }
+  MT_SCAN_NS(MT_F32);
+#undef MT_SCAN_NS
+#undef MT_SCAN
+}
+
+int mt_causal_conv1d(const void* x, const void* weight, const void* bias, void* conv_state, void* y, int64_t L,
+                     int64_t C, int width, int silu, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && weight && y, "mt_causal_conv1d: null pointer");
+  MT_CHECK_ARG(width >= 1 && width <= 16 && L >= 0 && C > 0 && L * C < (int64_t(1) << 40),
+               "mt_causal_conv1d: bad shape");
+  MT_CHECK_ARG(x != y, "mt_causal_conv1d: y must not alias x");
+  if (L == 0) return MT_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const dim3 grid(static_cast<unsigned>((L * C + 255) / 256));
+  int rc;
+  switch (dtype) {
+    case MT_BF16:
+      rc = launch(causal_conv1d_kernel<MT_BF16>, grid, dim3(256), 0, s, x, weight, bias, conv_state, y, (int)L,
+                  (int)C, width, silu);
+      break;
+    case MT_F16:
+      rc = launch(causal_conv1d_kernel<MT_F16>, grid, dim3(256), 0, s, x, weight, bias, conv_state, y, (int)L,
+                  (int)C, width, silu);
+      break;
+    case MT_F32:
+      rc = launch(causal_conv1d_kernel<MT_F32>, grid, dim3(256), 0, s, x, weight, bias, conv_state, y, (int)L,
+                  (int)C, width, silu);
+      break;
+    default: set_error("mt_causal_conv1d: bad dtype"); return MT_ERR_UNSUPPORTED;
+  }
+  if (rc != MT_OK || !conv_state || width == 1) return rc;
+  // Stream order puts the state update after every read of the old state.
+  const dim3 g2(static_cast<unsigned>((C + 255) / 256));
+  switch (dtype) {
+    case MT_BF16: conv_state_kernel<MT_BF16><<<g2, 256, 0, s>>>(x, conv_state, (int)L, (int)C, width); break;
+    case MT_F16: conv_state_kernel<MT_F16><<<g2, 256, 0, s>>>(x, conv_state, (int)L, (int)C, width); break;
+    default: conv_state_kernel<MT_F32><<<g2, 256, 0, s>>>(x, conv_state, (int)L, (int)C, width); break;
+  }
+  MT_CUDA(cudaGetLastError());
+  return MT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,125 @@
+// Library-wide entry points: version, errors, device status, SM count, and the
+// host helper that encodes TMA tensor maps through the driver entry point.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+
+#include "mt_common.cuh"
+#include "mt_tma.h"
+
+namespace mt {
+
+__device__ int g_device_status = 0;
+
+static thread_local char g_err[1024] = {0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+void clear_error() { g_err[0] = 0; }
+
+int cuda_fail(cudaError_t e, const char* what) {
+  set_error("%s failed: %s (%d)", what, cudaGetErrorString(e), static_cast<int>(e));
+  return MT_ERR_CUDA;
+}
+
+int device_sm_count(int* out) {
+  static int cached[64] = {0};
+  int dev = 0;
+  MT_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) {
+    *out = cached[dev];
+    return MT_OK;
+  }
+  int n = 0;
+  MT_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  *out = n;
+  return MT_OK;
+}
+
+// ------------------------------------------------------------- tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return MT_ERR_CUDA;
+  }
+  if (!aligned(base, 16) || row_stride_bytes % 16 != 0 || (box_inner * elem_bytes) % 16 != 0) {
+    set_error("tensor map: base %p / row stride %llu / box inner %u x %d B break the 16-byte rule",
+              base, (unsigned long long)row_stride_bytes, box_inner, elem_bytes);
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, box %u x %u", (int)r,
+              (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+    return MT_ERR_CUDA;
+  }
+  return MT_OK;
+}
+
+}  // namespace mt
+
+extern "C" {
+
+int mt_version(void) { return (0 << 16) | (1 << 8) | 0; }
+
+const char* mt_last_error_string(void) { return mt::g_err; }
+
+int mt_device_status(int* status_out, int clear) {
+  if (!status_out) {
+    mt::set_error("mt_device_status: status_out is NULL");
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  MT_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  MT_CUDA(cudaMemcpyFromSymbol(&v, mt::g_device_status, sizeof(int)));
+  if (clear) {
+    int z = 0;
+    MT_CUDA(cudaMemcpyToSymbol(mt::g_device_status, &z, sizeof(int)));
+  }
+  *status_out = v;
+  return MT_OK;
+}
+
+int mt_sm_count(int* sm_count_out) {
+  if (!sm_count_out) {
+    mt::set_error("mt_sm_count: output is NULL");
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  return mt::device_sm_count(sm_count_out);
+}
+
+}  // extern "C"

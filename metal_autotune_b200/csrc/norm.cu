@@ -1,0 +1,377 @@
+// Row normalisations and rotary embedding (HBM-bound elementwise/row work).
+//
+// rms_norm / add_rms_norm / layer_norm: one warp per row, 16-byte vector
+// loads when the row allows, fp32 accumulation, the row re-read from L1/L2
+// for the second pass. rope: one thread per rotated pair. The Qwen3
+// attention prologue (q/k RMSNorm -> RoPE -> head-major q, KV-cache append)
+// is one warp per (token, head): 128 values = 4 per lane, the rotation
+// partner d+64 sits in lane l+16.
+//
+// Products that the oracle computes without contraction use __fmul_rn /
+// __fadd_rn so the GPU and the CPU restatement round identically.
+#include "mt_common.cuh"
+
+namespace mt {
+
+template <int DT>
+__device__ __forceinline__ void load8(const typename Elem<DT>::T* p, float* v) {
+  if constexpr (DT == MT_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const typename Elem<DT>::T* e = reinterpret_cast<const typename Elem<DT>::T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = Elem<DT>::to_f(e[i]);
+  }
+}
+template <int DT>
+__device__ __forceinline__ void store8(typename Elem<DT>::T* p, const float* v) {
+  if constexpr (DT == MT_F32) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 u;
+    typename Elem<DT>::T* e = reinterpret_cast<typename Elem<DT>::T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = Elem<DT>::from_f(v[i]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+}
+
+// y = x * rsqrt(mean(x^2) + eps) * w   (HAS_RES: x = round(x + res) first, written to h)
+template <int DT, bool HAS_RES, bool VEC>
+__global__ void __launch_bounds__(256) rms_norm_kernel(const void* __restrict__ xp, const void* __restrict__ rp,
+                                                       const void* __restrict__ wp, float eps,
+                                                       void* __restrict__ hp, void* __restrict__ yp,
+                                                       int64_t rows, int dim) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* x = static_cast<const T*>(xp) + row * dim;
+  const T* res = HAS_RES ? static_cast<const T*>(rp) + row * dim : nullptr;
+  T* h = HAS_RES ? static_cast<T*>(hp) + row * dim : nullptr;
+  const T* w = static_cast<const T*>(wp);
+  T* y = static_cast<T*>(yp) + row * dim;
+  float ss = 0.f;
+  if (VEC) {
+    for (int i = lane * 8; i < dim; i += 256) {
+      float v[8];
+      load8<DT>(x + i, v);
+      if (HAS_RES) {
+        float r[8];
+        load8<DT>(res + i, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = round_to<DT>(__fadd_rn(v[e], r[e]));
+        store8<DT>(h + i, v);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+    }
+  } else {
+    for (int i = lane; i < dim; i += 32) {
+      float v = Elem<DT>::to_f(x[i]);
+      if (HAS_RES) {
+        v = round_to<DT>(__fadd_rn(v, Elem<DT>::to_f(res[i])));
+        h[i] = Elem<DT>::from_f(v);
+      }
+      ss = fmaf(v, v, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(dim)), eps));
+  if (HAS_RES) __syncwarp();
+  const T* src = HAS_RES ? h : x;
+  if (VEC) {
+    for (int i = lane * 8; i < dim; i += 256) {
+      float v[8], g[8];
+      load8<DT>(src + i, v);
+      load8<DT>(w + i, g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], scale), g[e]);
+      store8<DT>(y + i, v);
+    }
+  } else {
+    for (int i = lane; i < dim; i += 32)
+      y[i] = Elem<DT>::from_f(__fmul_rn(__fmul_rn(Elem<DT>::to_f(src[i]), scale), Elem<DT>::to_f(w[i])));
+  }
+  griddep_launch();
+}
+
+// two-pass layer norm: mean, centred variance, optional affine
+template <int DT>
+__global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict__ xp, const void* __restrict__ wp,
+                                                         const void* __restrict__ bp, float eps,
+                                                         void* __restrict__ yp, int64_t rows, int dim) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* x = static_cast<const T*>(xp) + row * dim;
+  const T* w = static_cast<const T*>(wp);
+  const T* b = static_cast<const T*>(bp);
+  T* y = static_cast<T*>(yp) + row * dim;
+  float sx = 0.f;
+  for (int i = lane; i < dim; i += 32) sx += Elem<DT>::to_f(x[i]);
+  sx = warp_sum(sx);
+  const float mean = __fdiv_rn(sx, static_cast<float>(dim));
+  float sv = 0.f;
+  for (int i = lane; i < dim; i += 32) {
+    const float c = __fsub_rn(Elem<DT>::to_f(x[i]), mean);
+    sv = fmaf(c, c, sv);
+  }
+  sv = warp_sum(sv);
+  const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sv, static_cast<float>(dim)), eps));
+  for (int i = lane; i < dim; i += 32) {
+    float v = __fmul_rn(__fsub_rn(Elem<DT>::to_f(x[i]), mean), scale);
+    if (w) v = __fmul_rn(v, Elem<DT>::to_f(w[i]));
+    if (b) v = __fadd_rn(v, Elem<DT>::to_f(b[i]));
+    y[i] = Elem<DT>::from_f(v);
+  }
+  griddep_launch();
+}
+
+struct RopeFreqs {
+  float inv_freq[128];  // base^(-2j/dims), j < dims/2, computed on the host in double
+};
+
+__device__ __forceinline__ void rope_pair(float a, float b, float c, float s, float& oa, float& ob) {
+  // first = a*c - b*s, second = b*c + a*s  (autotuner/scaffold/lower.py:1279)
+  oa = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  ob = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+}
+
+// x, y: [B*H, L, D]; one thread per (row, pair j < dims/2) plus tail copies.
+template <int DT>
+__global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, void* __restrict__ yp,
+                                                   int64_t rows, int L, int D, int dims, int traditional,
+                                                   float scale, int64_t offset, const RopeFreqs f) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  const int half = dims / 2;
+  const int per_row = half + (D - dims);
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= rows * per_row) return;
+  const int64_t row = idx / per_row;
+  const int j = static_cast<int>(idx % per_row);
+  const int l = static_cast<int>(row % L);
+  const T* x = static_cast<const T*>(xp) + row * D;
+  T* y = static_cast<T*>(yp) + row * D;
+  if (j >= half) {  // tail beyond `dims` copies through
+    const int d = dims + (j - half);
+    y[d] = x[d];
+    return;
+  }
+  const float pos = __fmul_rn(static_cast<float>(static_cast<int64_t>(l) + offset), scale);
+  const float th = __fmul_rn(pos, f.inv_freq[j]);
+  float s, c;
+  sincosf(th, &s, &c);
+  const int d0 = traditional ? 2 * j : j;
+  const int d1 = traditional ? 2 * j + 1 : j + half;
+  float o0, o1;
+  rope_pair(Elem<DT>::to_f(x[d0]), Elem<DT>::to_f(x[d1]), c, s, o0, o1);
+  y[d0] = Elem<DT>::from_f(o0);
+  y[d1] = Elem<DT>::from_f(o1);
+}
+
+// Qwen3 attention prologue, D = 128: warp per (token, head) over Hq + Hkv heads.
+template <int DT>
+__global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
+    const void* __restrict__ qp, const void* __restrict__ kp, const void* __restrict__ vp, int64_t q_stride,
+    int64_t kv_stride, const void* __restrict__ qwp, const void* __restrict__ kwp, float eps,
+    void* __restrict__ qo, void* __restrict__ kc, void* __restrict__ vc, int T_, int Hq, int Hkv,
+    int64_t cap, int64_t offset, const RopeFreqs f) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = Hq + Hkv;
+  if (wid >= static_cast<int64_t>(T_) * heads) return;
+  const int t = static_cast<int>(wid / heads);
+  const int hh = static_cast<int>(wid % heads);
+  const bool is_q = hh < Hq;
+  const int h = is_q ? hh : hh - Hq;
+  const T* src = is_q ? static_cast<const T*>(qp) + t * q_stride + h * 128
+                      : static_cast<const T*>(kp) + t * kv_stride + h * 128;
+  const T* nw = static_cast<const T*>(is_q ? qwp : kwp);
+  // 4 values per lane: d = 4*lane .. 4*lane+3
+  float v[4], g[4];
+  {
+    const uint2 u = *reinterpret_cast<const uint2*>(src + 4 * lane);
+    const T* e = reinterpret_cast<const T*>(&u);
+    const uint2 uw = *reinterpret_cast<const uint2*>(nw + 4 * lane);
+    const T* ew = reinterpret_cast<const T*>(&uw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = Elem<DT>::to_f(e[i]);
+      g[i] = Elem<DT>::to_f(ew[i]);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, 128.f), eps));
+  float n[4], p[4], o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = round_to<DT>(__fmul_rn(__fmul_rn(v[i], scale), g[i]));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
+  const float pos = static_cast<float>(static_cast<int64_t>(t) + offset);
+  const bool first = lane < 16;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int j = (4 * lane + i) & 63;
+    float s, c;
+    sincosf(__fmul_rn(pos, f.inv_freq[j]), &s, &c);
+    float o0, o1;
+    if (first) {
+      rope_pair(n[i], p[i], c, s, o0, o1);
+      o[i] = o0;
+    } else {
+      rope_pair(p[i], n[i], c, s, o0, o1);
+      o[i] = o1;
+    }
+  }
+  uint2 out;
+  T* eo = reinterpret_cast<T*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) eo[i] = Elem<DT>::from_f(o[i]);
+  if (is_q) {
+    *reinterpret_cast<uint2*>(static_cast<T*>(qo) + (static_cast<int64_t>(h) * T_ + t) * 128 + 4 * lane) = out;
+  } else {
+    const int64_t crow = static_cast<int64_t>(h) * cap + offset + t;
+    *reinterpret_cast<uint2*>(static_cast<T*>(kc) + crow * 128 + 4 * lane) = out;
+    const T* vs = static_cast<const T*>(vp) + t * kv_stride + h * 128;
+    *reinterpret_cast<uint2*>(static_cast<T*>(vc) + crow * 128 + 4 * lane) =
+        *reinterpret_cast<const uint2*>(vs + 4 * lane);
+  }
+  griddep_launch();
+}
+
+static RopeFreqs make_freqs(int dims, double base) {
+  RopeFreqs f;
+  for (int j = 0; j < 128; ++j)
+    f.inv_freq[j] = j < dims / 2 ? static_cast<float>(pow(base, -2.0 * j / dims)) : 0.f;
+  return f;
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+#define MT_DT_SWITCH(dtype, KERNEL_CALL)                                        \
+  switch (dtype) {                                                             \
+    case MT_BF16: { constexpr int DT = MT_BF16; KERNEL_CALL; } break;          \
+    case MT_F16: { constexpr int DT = MT_F16; KERNEL_CALL; } break;            \
+    case MT_F32: { constexpr int DT = MT_F32; KERNEL_CALL; } break;            \
+    default: set_error("unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED; \
+  }
+
+
+extern "C" {
+
+int mt_rms_norm(const void* x, const void* w, float eps, void* y, int64_t rows, int64_t dim, int dtype,
+                mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && w && y, "mt_rms_norm: null pointer");
+  MT_CHECK_ARG(rows >= 0 && dim > 0 && dim <= (1 << 24), "mt_rms_norm: rows=%lld dim=%lld", (long long)rows,
+               (long long)dim);
+  if (rows == 0) return MT_OK;
+  const bool vec = dim % 8 == 0 && aligned(x, 16) && aligned(y, 16) && aligned(w, 16);
+  const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  int rc = MT_OK;
+  MT_DT_SWITCH(dtype, rc = vec ? launch(rms_norm_kernel<DT, false, true>, grid, dim3(256), 0, (cudaStream_t)stream, x,
+                                        nullptr, w, eps, nullptr, y, rows, (int)dim)
+                               : launch(rms_norm_kernel<DT, false, false>, grid, dim3(256), 0,
+                                        (cudaStream_t)stream, x, nullptr, w, eps, nullptr, y, rows, (int)dim));
+  return rc;
+}
+
+int mt_add_rms_norm(const void* x, const void* residual, const void* w, float eps, void* h, void* y, int64_t rows,
+                    int64_t dim, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && residual && w && h && y, "mt_add_rms_norm: null pointer");
+  MT_CHECK_ARG(rows >= 0 && dim > 0 && dim <= (1 << 24), "mt_add_rms_norm: rows=%lld dim=%lld",
+               (long long)rows, (long long)dim);
+  if (rows == 0) return MT_OK;
+  const bool vec = dim % 8 == 0 && aligned(x, 16) && aligned(y, 16) && aligned(w, 16) && aligned(h, 16) &&
+                   aligned(residual, 16);
+  const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  int rc = MT_OK;
+  MT_DT_SWITCH(dtype, rc = vec ? launch(rms_norm_kernel<DT, true, true>, grid, dim3(256), 0, (cudaStream_t)stream, x,
+                                        residual, w, eps, h, y, rows, (int)dim)
+                               : launch(rms_norm_kernel<DT, true, false>, grid, dim3(256), 0,
+                                        (cudaStream_t)stream, x, residual, w, eps, h, y, rows, (int)dim));
+  return rc;
+}
+
+int mt_layer_norm(const void* x, const void* w, const void* b, float eps, void* y, int64_t rows, int64_t dim,
+                  int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && y, "mt_layer_norm: null pointer");
+  MT_CHECK_ARG(rows >= 0 && dim > 0 && dim <= (1 << 24), "mt_layer_norm: rows=%lld dim=%lld", (long long)rows,
+               (long long)dim);
+  if (rows == 0) return MT_OK;
+  const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  int rc = MT_OK;
+  MT_DT_SWITCH(dtype, rc = launch(layer_norm_kernel<DT>, grid, dim3(256), 0, (cudaStream_t)stream, x, w, b, eps, y,
+                                  rows, (int)dim));
+  return rc;
+}
+
+int mt_rope(const void* x, void* y, int64_t B, int64_t H, int64_t L, int64_t D, int dims, int traditional,
+            float base, float scale, int64_t offset, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && y, "mt_rope: null pointer");
+  MT_CHECK_ARG(B >= 0 && H >= 0 && L >= 0 && D > 0, "mt_rope: bad shape");
+  MT_CHECK_ARG(dims >= 2 && dims % 2 == 0 && dims <= D && dims <= 256, "mt_rope: dims=%d vs D=%lld", dims,
+               (long long)D);
+  MT_CHECK_ARG(base > 0.f, "mt_rope: base must be positive");
+  const int64_t rows = B * H * L;
+  if (rows == 0) return MT_OK;
+  const RopeFreqs f = make_freqs(dims, base);
+  const int64_t total = rows * (dims / 2 + (D - dims));
+  const dim3 grid(static_cast<unsigned>((total + 255) / 256));
+  int rc = MT_OK;
+  MT_DT_SWITCH(dtype, rc = launch(rope_kernel<DT>, grid, dim3(256), 0, (cudaStream_t)stream, x, y, rows, (int)L,
+                                  (int)D, dims, traditional, scale, offset, f));
+  return rc;
+}
+
+int mt_qk_norm_rope_cache(const void* q, const void* k, const void* v, int64_t q_stride, int64_t kv_stride,
+                          const void* q_norm_w, const void* k_norm_w, float eps, void* q_out, void* k_cache,
+                          void* v_cache, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t cache_cap,
+                          int64_t offset, float rope_base, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(q && k && v && q_norm_w && k_norm_w && q_out && k_cache && v_cache,
+               "mt_qk_norm_rope_cache: null pointer");
+  MT_CHECK_ARG(D == 128, "mt_qk_norm_rope_cache: head_dim %lld, only 128 is built", (long long)D);
+  MT_CHECK_ARG(dtype == MT_BF16 || dtype == MT_F16, "mt_qk_norm_rope_cache: dtype must be bf16 or f16");
+  MT_CHECK_ARG(T >= 0 && Hq > 0 && Hkv > 0 && offset >= 0 && offset + T <= cache_cap,
+               "mt_qk_norm_rope_cache: offset %lld + T %lld exceeds cache capacity %lld", (long long)offset,
+               (long long)T, (long long)cache_cap);
+  MT_CHECK_ARG(q_stride % 4 == 0 && kv_stride % 4 == 0 && aligned(q, 8) && aligned(k, 8) && aligned(v, 8),
+               "mt_qk_norm_rope_cache: rows must be 8-byte aligned");
+  if (T == 0) return MT_OK;
+  const RopeFreqs f = make_freqs(128, rope_base);
+  const int64_t warps = T * (Hq + Hkv);
+  const dim3 grid(static_cast<unsigned>((warps + 7) / 8));
+  int rc = MT_OK;
+  if (dtype == MT_BF16)
+    rc = launch(qk_norm_rope_cache_kernel<MT_BF16>, grid, dim3(256), 0, (cudaStream_t)stream, q, k, v, q_stride,
+                kv_stride, q_norm_w, k_norm_w, eps, q_out, k_cache, v_cache, (int)T, (int)Hq, (int)Hkv, cache_cap,
+                offset, f);
+  else
+    rc = launch(qk_norm_rope_cache_kernel<MT_F16>, grid, dim3(256), 0, (cudaStream_t)stream, q, k, v, q_stride,
+                kv_stride, q_norm_w, k_norm_w, eps, q_out, k_cache, v_cache, (int)T, (int)Hq, (int)Hkv, cache_cap,
+                offset, f);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,150 @@
+// C entry points of the affine-quantized matmul family: argument checks and
+// the choice between the vector kernel (M <= 8, decode) and the tcgen05
+// matrix kernel (prefill).
+#include "mt_common.cuh"
+#include "qmm_common.cuh"
+
+namespace mt {
+
+constexpr int64_t kQmvMaxRows = 8;
+
+static int check_common(const QmmRequest& r, const char* who) {
+  MT_CHECK_ARG(r.x, "%s: x is NULL", who);
+  MT_CHECK_ARG(r.bits == 4 || r.bits == 8, "%s: bits=%d (4 or 8)", who, r.bits);
+  MT_CHECK_ARG(r.group == 32 || r.group == 64 || r.group == 128, "%s: group_size=%d (32, 64 or 128)", who,
+               r.group);
+  if (r.dtype != MT_BF16 && r.dtype != MT_F16) {
+    set_error("%s: dtype %d is not built (bf16 or f16)", who, r.dtype);
+    return MT_ERR_UNSUPPORTED;
+  }
+  MT_CHECK_ARG(r.M >= 0 && r.M < (int64_t(1) << 31), "%s: M=%lld", who, (long long)r.M);
+  MT_CHECK_ARG(r.K > 0 && r.K % r.group == 0 && r.K < (int64_t(1) << 24),
+               "%s: K=%lld must be a positive multiple of group_size %d", who, (long long)r.K, r.group);
+  MT_CHECK_ARG(r.K % 64 == 0, "%s: K=%lld must be a multiple of 64", who, (long long)r.K);
+  int nsets = 0;
+  for (int s = 0; s < 3; ++s) {
+    const QmmSetReq& q = r.set[s];
+    if (q.N == 0) continue;
+    MT_CHECK_ARG(q.N > 0 && q.N < (int64_t(1) << 31), "%s: N=%lld", who, (long long)q.N);
+    MT_CHECK_ARG(q.w && q.s && q.b, "%s: weight set %d has a NULL pointer", who, s);
+    MT_CHECK_ARG(q.y || (r.kind == QMM_SWIGLU && s == 1), "%s: output %d is NULL", who, s);
+    MT_CHECK_ARG(aligned(q.w, 16), "%s: packed weights must be 16-byte aligned", who);
+    ++nsets;
+  }
+  MT_CHECK_ARG(nsets > 0, "%s: no output", who);
+  MT_CHECK_ARG(aligned(r.x, 16), "%s: x must be 16-byte aligned", who);
+  if (r.kind == QMM_RESIDUAL) MT_CHECK_ARG(r.residual, "%s: residual is NULL", who);
+  return MT_OK;
+}
+
+static int run(const QmmRequest& r, cudaStream_t stream, const char* who) {
+  clear_error();
+  const int rc = check_common(r, who);
+  if (rc != MT_OK) return rc;
+  if (r.M == 0) return MT_OK;
+  if (r.M <= kQmvMaxRows) return qmv_run(r, stream);
+  return qmm_tc_run(r, stream);
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" {
+
+int mt_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                        int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace,
+                        size_t workspace_bytes, mt_stream_t stream) {
+  QmmRequest r = {};
+  r.x = x;
+  r.set[0] = {w, scales, biases, y, N};
+  r.M = M;
+  r.K = K;
+  r.group = group_size;
+  r.bits = bits;
+  r.dtype = dtype;
+  r.kind = QMM_PLAIN;
+  r.ws = workspace;
+  r.ws_bytes = workspace_bytes;
+  MT_CHECK_ARG(N > 0, "mt_quantized_matmul: N=%lld", (long long)N);
+  return run(r, (cudaStream_t)stream, "mt_quantized_matmul");
+}
+
+int mt_quantized_matmul_residual(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                                 const void* residual, void* y, int64_t M, int64_t N, int64_t K, int group_size,
+                                 int bits, int dtype, void* workspace, size_t workspace_bytes, mt_stream_t stream) {
+  QmmRequest r = {};
+  r.x = x;
+  r.residual = residual;
+  r.set[0] = {w, scales, biases, y, N};
+  r.M = M;
+  r.K = K;
+  r.group = group_size;
+  r.bits = bits;
+  r.dtype = dtype;
+  r.kind = QMM_RESIDUAL;
+  r.ws = workspace;
+  r.ws_bytes = workspace_bytes;
+  MT_CHECK_ARG(N > 0, "mt_quantized_matmul_residual: N=%lld", (long long)N);
+  return run(r, (cudaStream_t)stream, "mt_quantized_matmul_residual");
+}
+
+int mt_quantized_matmul_residual_rms_norm(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                                          const void* residual, const void* norm_w, float eps, void* h, void* y,
+                                          int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype,
+                                          void* workspace, size_t workspace_bytes, mt_stream_t stream) {
+  MT_CHECK_ARG(norm_w && h && y, "mt_quantized_matmul_residual_rms_norm: null output or norm weight");
+  int rc = mt_quantized_matmul_residual(x, w, scales, biases, residual, h, M, N, K, group_size, bits, dtype,
+                                        workspace, workspace_bytes, stream);
+  if (rc != MT_OK) return rc;
+  return mt_rms_norm(h, norm_w, eps, y, M, N, dtype, stream);
+}
+
+int mt_quantized_matmul_swiglu(const void* x, const uint32_t* wg, const void* sg, const void* bg, const uint32_t* wu,
+                               const void* su, const void* bu, void* y, int64_t M, int64_t N, int64_t K,
+                               int group_size, int bits, int dtype, void* workspace, size_t workspace_bytes,
+                               mt_stream_t stream) {
+  QmmRequest r = {};
+  r.x = x;
+  r.set[0] = {wg, sg, bg, y, N};
+  r.set[1] = {wu, su, bu, nullptr, N};
+  r.M = M;
+  r.K = K;
+  r.group = group_size;
+  r.bits = bits;
+  r.dtype = dtype;
+  r.kind = QMM_SWIGLU;
+  r.ws = workspace;
+  r.ws_bytes = workspace_bytes;
+  MT_CHECK_ARG(N > 0, "mt_quantized_matmul_swiglu: N=%lld", (long long)N);
+  return run(r, (cudaStream_t)stream, "mt_quantized_matmul_swiglu");
+}
+
+int mt_quantized_matmul_multi(const void* x, const uint32_t* w0, const void* s0, const void* b0, void* y0, int64_t N0,
+                              const uint32_t* w1, const void* s1, const void* b1, void* y1, int64_t N1,
+                              const uint32_t* w2, const void* s2, const void* b2, void* y2, int64_t N2, int64_t M,
+                              int64_t K, int group_size, int bits, int dtype, void* workspace,
+                              size_t workspace_bytes, mt_stream_t stream) {
+  QmmRequest r = {};
+  r.x = x;
+  r.set[0] = {w0, s0, b0, y0, N0};
+  r.set[1] = {w1, s1, b1, y1, N1};
+  r.set[2] = {w2, s2, b2, y2, N2};
+  r.M = M;
+  r.K = K;
+  r.group = group_size;
+  r.bits = bits;
+  r.dtype = dtype;
+  r.kind = QMM_PLAIN;
+  r.ws = workspace;
+  r.ws_bytes = workspace_bytes;
+  MT_CHECK_ARG(N0 >= 0 && N1 >= 0 && N2 >= 0, "mt_quantized_matmul_multi: negative N");
+  return run(r, (cudaStream_t)stream, "mt_quantized_matmul_multi");
+}
+
+size_t mt_qmm_workspace_bytes(int64_t M, int64_t n_total, int64_t K, int bits, int kind) {
+  if (M <= kQmvMaxRows) return 0;
+  return qmm_tc_workspace(M, n_total, K, bits, kind);
+}
+
+}  // extern "C"
