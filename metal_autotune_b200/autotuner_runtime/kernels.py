@@ -276,6 +276,7 @@ class LoadedKernel:
                 cargs.append(ws.ptr)
                 cargs.append(ws.nbytes)
         rc = self._fn(*cargs)
+        _mt.CALLS[0] += 1
         if rc != 0:
             _mt._check(rc, self._symbol)
         return outputs

@@ -277,7 +277,7 @@ extern "C" int mt_sdpa(const void* q, const void* k, const void* v, void* o, int
   const dim3 grid(static_cast<unsigned>((Lq + 63) / 64), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
   const size_t smem = static_cast<size_t>(64 * D * 2) * 5;
   auto run = [&](auto kern) -> int {
-    MT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (int e = ensure_smem(kern, smem)) return e;
     return launch(kern, grid, dim3(128), smem, (cudaStream_t)stream, p);
   };
   if (dtype == MT_BF16) return D == 128 ? run(sdpa_kernel<MT_BF16, 128>) : run(sdpa_kernel<MT_BF16, 64>);

@@ -61,6 +61,23 @@ inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 int device_sm_count(int* out);
 
+// Raise a kernel's dynamic shared-memory limit once per device (first use
+// happens before any stream capture; later calls are host-side no-ops).
+template <typename... KArgs>
+inline int ensure_smem(void (*kernel)(KArgs...), size_t bytes) {
+  static int set_bytes[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) dev = 63;
+  if (static_cast<size_t>(set_bytes[dev]) >= bytes) return MT_OK;
+  const int want = bytes > 48 * 1024 ? static_cast<int>(bytes) : 48 * 1024;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  set_bytes[dev] = want;
+  return MT_OK;
+}
+
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }

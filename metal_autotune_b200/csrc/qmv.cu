@@ -239,25 +239,25 @@ static int qmv_dispatch_mr(QmvParams& p, int total_rows, cudaStream_t stream) {
     switch (mr) {
       case 1: {
         auto k = qmv_kernel<DT, BITS, 1, MODE>;
-        MT_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (int e = ensure_smem(k, smem)) return e;
         rc = launch(k, grid, dim3(256), smem, stream, p);
         break;
       }
       case 2: {
         auto k = qmv_kernel<DT, BITS, 2, MODE>;
-        MT_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (int e = ensure_smem(k, smem)) return e;
         rc = launch(k, grid, dim3(256), smem, stream, p);
         break;
       }
       case 4: {
         auto k = qmv_kernel<DT, BITS, 4, MODE>;
-        MT_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (int e = ensure_smem(k, smem)) return e;
         rc = launch(k, grid, dim3(256), smem, stream, p);
         break;
       }
       default: {
         auto k = qmv_kernel<DT, BITS, 8, MODE>;
-        MT_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (int e = ensure_smem(k, smem)) return e;
         rc = launch(k, grid, dim3(256), smem, stream, p);
         break;
       }

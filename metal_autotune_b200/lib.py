@@ -87,6 +87,7 @@ SIGNATURES = {
 
 _lib = None
 _lock = threading.Lock()
+CALLS = [0]  # entry-point calls made through this binding (each is one or more kernel launches)
 
 
 def load(path: str | Path | None = None) -> C.CDLL:
@@ -125,6 +126,7 @@ def _check(rc: int, symbol: str) -> None:
 def call(symbol: str, *args) -> int:
     """Call an int-returning entry point and raise on a non-zero code."""
     rc = getattr(load(), symbol)(*args)
+    CALLS[0] += 1
     _check(rc, symbol)
     return rc
 
