@@ -284,6 +284,32 @@ int mt_diff_reduce(const void* a, const void* b, int64_t n, int dtype,
                    void* workspace, size_t workspace_bytes,
                    mt_stream_t stream);
 
+/*
+ * mt_diff_reduce without a workspace argument; it allocates nothing. No
+ * counterpart in the reference: it exists for callers that must not
+ * allocate device memory — a host binding of this C ABI that holds only
+ * buffers lent to it and has no CUDA allocator of its own, or a verification
+ * check that runs while the memory pool is deliberately filled with NaNs (the
+ * reference's poisoned-pool gate), where allocating scratch would take memory
+ * from, or add memory to, the very pool under test.
+ *
+ * Scratch lives in a static device array inside libmt.so (about 12 KB: a
+ * counter and 128 block partials), held by every GPU that loads the library
+ * until the process exits. n may be at most MT_DIFF_NOALLOC_MAX_ELEMS;
+ * larger inputs are rejected with MT_ERR_INVALID_ARGUMENT (use
+ * mt_diff_reduce). Same kernel and block partition as mt_diff_reduce, so the
+ * statistics are identical. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture. Every call on a device shares the
+ * array: calls whose kernels overlap on the GPU (other streams, other host
+ * threads) race and must be serialised by the caller. Each call zeroes the
+ * counter on its stream before its kernel runs.
+ */
+#define MT_DIFF_NOALLOC_MAX_ELEMS 1048576
+int mt_diff_reduce_noalloc(const void* a, const void* b, int64_t n, int dtype,
+                           float rtol, float atol, float wobble,
+                           mt_diff_stats* stats, mt_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* a-7: dense linear (+bias, +GELU), the GELU-MLP region                     */
 /* ------------------------------------------------------------------------ */

@@ -221,6 +221,35 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict_
 
 size_t diff_workspace(int64_t n) { return 256 + static_cast<size_t>(diff_blocks(n)) * sizeof(DiffPartial); }
 
+// Scratch of mt_diff_reduce_noalloc: the completion counter (first 256 bytes)
+// and one partial per block. Every GPU that loads the library holds this
+// array until the process exits; every call of the entry point on a device
+// shares it.
+constexpr int kNoAllocBlocks = 128;
+constexpr int64_t kNoAllocMaxN = static_cast<int64_t>(kNoAllocBlocks) * 8192;  // MT_DIFF_NOALLOC_MAX_ELEMS
+static __device__ __align__(256) uint8_t g_diff_noalloc_scratch[256 + kNoAllocBlocks * sizeof(DiffPartial)];
+
+// Device address of the scratch array for the current device. Host code may
+// not pass the array's name to a kernel (it is only a host-side stand-in), so
+// the address is looked up once per device, with that device current.
+static int noalloc_scratch(void** out) {
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  MT_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_error("mt_diff_reduce_noalloc: device ordinal %d out of range", dev);
+    return MT_ERR_UNSUPPORTED;
+  }
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_diff_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_diff_noalloc_scratch)");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return MT_OK;
+}
+
 }  // namespace mt
 
 using namespace mt;
@@ -272,6 +301,64 @@ int mt_diff_reduce(const void* a, const void* b, int64_t n, int dtype, float rto
       return launch(diff_kernel<uint8_t, false>, grid, block, 0, s, (const uint8_t*)a, (const uint8_t*)b, n, rtol,
                     atol, wobble, parts, counter, stats);
     default: set_error("mt_diff_reduce: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
+  }
+}
+
+// Same statistics as mt_diff_reduce, with its scratch in the library's own
+// static device array instead of a caller workspace. For callers that must
+// not allocate device memory. Same kernel and the same block partition as
+// mt_diff_reduce, so both return identical statistics for the same input.
+int mt_diff_reduce_noalloc(const void* a, const void* b, int64_t n, int dtype, float rtol, float atol, float wobble,
+                           mt_diff_stats* stats, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(stats, "mt_diff_reduce_noalloc: stats is NULL");
+  MT_CHECK_ARG(n >= 0, "mt_diff_reduce_noalloc: negative size");
+  MT_CHECK_ARG(n == 0 || (a && b), "mt_diff_reduce_noalloc: null input");
+  MT_CHECK_ARG(n <= kNoAllocMaxN,
+               "mt_diff_reduce_noalloc: n=%lld exceeds the static scratch maximum of %lld elements "
+               "(%d block partials); use mt_diff_reduce with a workspace",
+               (long long)n, (long long)kNoAllocMaxN, kNoAllocBlocks);
+  if (diff_blocks(n) > kNoAllocBlocks) {
+    set_error("mt_diff_reduce_noalloc: %d blocks exceed the static scratch", diff_blocks(n));
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != MT_OK) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  // The array keeps the previous call's contents; the counter must start at zero.
+  MT_CUDA(cudaMemsetAsync(scratch, 0, sizeof(uint32_t), s));
+  uint32_t* counter = static_cast<uint32_t*>(scratch);
+  DiffPartial* parts = reinterpret_cast<DiffPartial*>(static_cast<uint8_t*>(scratch) + 256);
+  const dim3 grid(diff_blocks(n)), block(kDiffThreads);
+  switch (dtype) {
+    case MT_BF16:
+      return launch(diff_kernel<__nv_bfloat16, true>, grid, block, 0, s, (const __nv_bfloat16*)a,
+                    (const __nv_bfloat16*)b, n, rtol, atol, wobble, parts, counter, stats);
+    case MT_F16:
+      return launch(diff_kernel<__half, true>, grid, block, 0, s, (const __half*)a, (const __half*)b, n, rtol, atol,
+                    wobble, parts, counter, stats);
+    case MT_F32:
+      return launch(diff_kernel<float, true>, grid, block, 0, s, (const float*)a, (const float*)b, n, rtol, atol,
+                    wobble, parts, counter, stats);
+    case MT_I32:
+    case MT_U32:
+      return launch(diff_kernel<uint32_t, false>, grid, block, 0, s, (const uint32_t*)a, (const uint32_t*)b, n, rtol,
+                    atol, wobble, parts, counter, stats);
+    case MT_I64:
+    case MT_U64:
+      return launch(diff_kernel<unsigned long long, false>, grid, block, 0, s, (const unsigned long long*)a,
+                    (const unsigned long long*)b, n, rtol, atol, wobble, parts, counter, stats);
+    case MT_I16:
+    case MT_U16:
+      return launch(diff_kernel<uint16_t, false>, grid, block, 0, s, (const uint16_t*)a, (const uint16_t*)b, n, rtol,
+                    atol, wobble, parts, counter, stats);
+    case MT_U8:
+    case MT_I8:
+    case MT_BOOL:
+      return launch(diff_kernel<uint8_t, false>, grid, block, 0, s, (const uint8_t*)a, (const uint8_t*)b, n, rtol,
+                    atol, wobble, parts, counter, stats);
+    default: set_error("mt_diff_reduce_noalloc: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
   }
 }
 

@@ -79,6 +79,7 @@ SIGNATURES = {
     "mt_logits_pick": (C.c_int, [P, I64, I32, P, P, P, P]),
     "mt_diff_workspace_bytes": (C.c_size_t, [I64]),
     "mt_diff_reduce": (C.c_int, [P, P, I64, I32, F32, F32, F32, P, P, SZ, P]),
+    "mt_diff_reduce_noalloc": (C.c_int, [P, P, I64, I32, F32, F32, F32, P, P]),
     "mt_linear": (C.c_int, [P, P, P, P, I64, I64, I64, I32, I32, P]),
     "mt_layer_norm": (C.c_int, [P, P, P, F32, P, I64, I64, I32, P]),
     "mt_mamba_scan": (C.c_int, [P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I32, P]),
