@@ -11,6 +11,11 @@
  * otherwise. Launches are asynchronous; argument errors are reported before
  * anything is enqueued.
  *
+ * Workspaces: the first 64 KiB of a workspace are control words (flags and
+ * counters at fixed offsets) that every kernel leaves zero when it completes;
+ * data regions start at 64 KiB. One zero-filled workspace can therefore be
+ * shared by all calls issued in order on one stream.
+ *
  * Each declaration names the reference interface it replaces (file:line in
  * shivamg05/metal-autotune). The reference dispatches these regions through
  * autotuner_runtime/kernels.py:247-268 (`call` / `try_call` / `try_sized`)

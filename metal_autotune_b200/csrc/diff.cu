@@ -219,7 +219,8 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict_
   griddep_launch();
 }
 
-size_t diff_workspace(int64_t n) { return 256 + static_cast<size_t>(diff_blocks(n)) * sizeof(DiffPartial); }
+// counter in the workspace's control region, block partials after it
+size_t diff_workspace(int64_t n) { return kWsCtlBytes + static_cast<size_t>(diff_blocks(n)) * sizeof(DiffPartial); }
 
 // Scratch of mt_diff_reduce_noalloc: the completion counter (first 256 bytes)
 // and one partial per block. Every GPU that loads the library holds this
@@ -269,8 +270,8 @@ int mt_diff_reduce(const void* a, const void* b, int64_t n, int dtype, float rto
               diff_workspace(n), workspace_bytes);
     return MT_ERR_WORKSPACE;
   }
-  uint32_t* counter = static_cast<uint32_t*>(workspace);
-  DiffPartial* parts = reinterpret_cast<DiffPartial*>(static_cast<uint8_t*>(workspace) + 256);
+  uint32_t* counter = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWsDiffCounter);
+  DiffPartial* parts = reinterpret_cast<DiffPartial*>(static_cast<uint8_t*>(workspace) + kWsCtlBytes);
   const dim3 grid(diff_blocks(n)), block(kDiffThreads);
   cudaStream_t s = (cudaStream_t)stream;
   switch (dtype) {

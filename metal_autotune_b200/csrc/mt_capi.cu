@@ -27,6 +27,34 @@ int cuda_fail(cudaError_t e, const char* what) {
   return MT_ERR_CUDA;
 }
 
+namespace {
+struct SmemAttr {
+  const void* kernel;
+  int dev;
+  int bytes;
+};
+std::mutex g_smem_mu;
+SmemAttr g_smem_attrs[512];
+int g_smem_n = 0;
+}  // namespace
+
+int smem_attr_lookup(const void* kernel, int dev) {
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  for (int i = 0; i < g_smem_n; ++i)
+    if (g_smem_attrs[i].kernel == kernel && g_smem_attrs[i].dev == dev) return g_smem_attrs[i].bytes;
+  return 0;
+}
+
+void smem_attr_store(const void* kernel, int dev, int bytes) {
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  for (int i = 0; i < g_smem_n; ++i)
+    if (g_smem_attrs[i].kernel == kernel && g_smem_attrs[i].dev == dev) {
+      g_smem_attrs[i].bytes = bytes;
+      return;
+    }
+  if (g_smem_n < 512) g_smem_attrs[g_smem_n++] = {kernel, dev, bytes};
+}
+
 int device_sm_count(int* out) {
   static int cached[64] = {0};
   int dev = 0;

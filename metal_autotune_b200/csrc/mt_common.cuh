@@ -63,20 +63,33 @@ int device_sm_count(int* out);
 
 // Raise a kernel's dynamic shared-memory limit once per device (first use
 // happens before any stream capture; later calls are host-side no-ops).
+// The cache is keyed by (kernel, device): kernels of one signature are distinct entries.
+int smem_attr_lookup(const void* kernel, int dev);
+void smem_attr_store(const void* kernel, int dev, int bytes);
+
 template <typename... KArgs>
 inline int ensure_smem(void (*kernel)(KArgs...), size_t bytes) {
-  static int set_bytes[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) dev = 63;
-  if (static_cast<size_t>(set_bytes[dev]) >= bytes) return MT_OK;
+  const void* key = reinterpret_cast<const void*>(kernel);
+  if (static_cast<size_t>(smem_attr_lookup(key, dev)) >= bytes) return MT_OK;
   const int want = bytes > 48 * 1024 ? static_cast<int>(bytes) : 48 * 1024;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-  set_bytes[dev] = want;
+  smem_attr_store(key, dev, want);
   return MT_OK;
 }
+
+// Workspace convention shared by every entry point that takes one: the first
+// kWsCtlBytes are control words (flags, counters) at fixed offsets, each left
+// zero by the kernel that uses it; data regions (partials) start after them,
+// so one kernel's data can never land on another kernel's control words.
+constexpr size_t kWsCtlBytes = 65536;
+constexpr size_t kWsQmmFlags = 0;         // qmm: [256 CTAs][2] u32
+constexpr size_t kWsDiffCounter = 2048;   // diff: completion counter
+constexpr size_t kWsQmmDone = 4096;       // qmm: per-tile participant counters
+constexpr size_t kWsQmmMaxTiles = (kWsCtlBytes - kWsQmmDone) / 4;
 
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
@@ -294,6 +307,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Shared-memory matrix descriptor (tcgen05 "UMMA" descriptor), K-major operand

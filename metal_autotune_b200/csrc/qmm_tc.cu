@@ -1,45 +1,59 @@
 // Affine-quantized matmul for prefill on the 5th-generation tensor cores.
 //
-// y[M, N] = x[M, K] · dequant(w)[N, K]^T. One CTA owns a tile of 128 weight
-// rows (the MMA's M) and TN tokens (the MMA's N), and walks K in stages of
-// 128. Roles:
-//   warp 0      TMA producer: the packed weight tile (128 rows x 64 B for
-//               4-bit, swizzled) and the x tile (TN rows x 128 bf16, 128-byte
-//               swizzle) of each stage, into a ring of SS shared-memory slots.
+// y[M, N] = x[M, K] · dequant(w)[N, K]^T, as a persistent stream-K kernel.
+//
+// Work: a tile is 128 weight rows (the MMA's M) x TN <= 128 tokens (the MMA's
+// N); a unit is one tile's K-stage of 128. The grid has one CTA per SM; CTA c
+// owns the contiguous unit range [c*U/P, (c+1)*U/P), so every SM gets the
+// same number of K-stages whatever the tile count, and a CTA's pipeline runs
+// across tile boundaries without draining.
+//
+// Roles (512 threads):
+//   warp 0      TMA producer: per unit, the packed weight tile (128 rows x
+//               64 B for 4-bit, 64-byte swizzle) and the x tile (TN rows x 128
+//               bf16, 128-byte swizzle), into a ring of SS shared-memory slots.
+//               The first SS weight tiles are issued before the grid
+//               dependency resolves (weights never depend on the previous
+//               kernel).
 //   warp 1      TMEM owner and MMA issuer: tcgen05.mma.kind::f16 with the
 //               dequantised weights as the A operand read from tensor memory
-//               and x as the B operand read from shared memory; fp32
-//               accumulators in tensor memory.
+//               and x as the B operand from shared memory; fp32 accumulators
+//               in tensor memory, two accumulator slots when they fit, so the
+//               epilogue of one tile overlaps the next tile's MMAs.
 //   warps 4-11  dequantisers: thread (warp%4, lane) owns weight row
-//               32*(warp%4)+lane, turns its packed words into bf16 pairs
-//               (MLX rounding, see dequant_chunk) and stores them straight
-//               into tensor memory with tcgen05.st — dequantised weights never
-//               touch shared memory. After the K loop the same warps run the
-//               epilogue (tcgen05.ld of the accumulators, rounding, residual
-//               or SwiGLU, store).
-// Small-M shapes give few tiles, so K may be split over blockIdx.z; each
-// split writes an fp32 partial to the workspace and the last split of a tile
-// to arrive (atomic counter) sums the partials in split order — the result
-// does not depend on arrival order — applies the epilogue and re-zeroes the
-// counter.
+//               32*(warp%4)+lane and converts its packed words into element
+//               pairs with MLX rounding (dequant_chunk), stored straight into
+//               tensor memory with tcgen05.st; scales/biases for the next unit
+//               are loaded while the current one is converted.
+//   warps 12-15 epilogue: tcgen05.ld of the accumulators. A tile finished by
+//               one CTA is rounded (and SwiGLU-combined), staged in shared
+//               memory and written with coalesced 16-byte stores (+ residual).
+//               A tile shared by several CTAs: each participant writes its
+//               fp32 partial to the workspace and raises a flag; after its
+//               own range every participant waits for the tile's flags and
+//               reduces one slice of the tile's rows, summing the partials in
+//               K order — the result does not depend on timing — then the last
+//               participant to finish clears the tile's flags.
 //
-// Every mbarrier wait is bounded (mbar_wait); on expiry the CTA records the
-// site in the device status word, stops issuing work, waits (bounded) for
-// its in-flight copies and MMAs and frees its tensor memory.
-#include <algorithm>
-
+// Every wait (mbarriers, partial flags) is bounded (2 s); on expiry the CTA
+// records the site in the device status word, stops, drains its in-flight
+// copies and MMAs (bounded) and frees its tensor memory.
 #include "mt_common.cuh"
 #include "mt_tma.h"
 #include "qmm_common.cuh"
 
 namespace mt {
 
-constexpr int kBM = 128;      // weight rows per tile (MMA M)
-constexpr int kBK = 128;      // K per stage
-constexpr int kThreads = 384; // 12 warps
-constexpr int kMaxSS = 8;
+constexpr int kBM = 128;       // weight rows per tile (MMA M)
+constexpr int kBK = 128;       // K per unit
+constexpr int kThreads = 512;  // 16 warps
+constexpr int kMaxSS = 6;
 constexpr int kTmemCols = 512;
-constexpr int kAccCols = 256; // accumulators occupy columns [0, 256)
+constexpr int kAccCols = 256;  // accumulator slots live in columns [0, 256)
+constexpr int kEpiWarp0 = 12;
+constexpr int kEpiBar = 2;     // named barrier of the epilogue warpgroup
+constexpr int kSmemLimit = 232448;
+constexpr int kMaxP = 256;     // CTAs the workspace query provisions for
 
 struct QmmTcParams {
   CUtensorMap tmx;     // x [M, K]
@@ -48,17 +62,19 @@ struct QmmTcParams {
   const void* b[3];
   void* y[3];
   const void* residual;
-  uint32_t* counters;
-  float* partials;
+  uint32_t* flags;     // [P][2]: partial of slot published
+  uint32_t* done;      // [tiles]: participants finished with a shared tile
+  float* partials;     // [P][2][NACC][TNp][128]
+  long long units;
   int N[3];
   int tile_start[4];   // prefix sums of feature tiles per set
   int M, K, G, group;
-  int TN, TNp, SS, splits, nk, kind;
+  int TN, TNp, SS, nk, kind, n_tt, tiles, P, acc_slots, vec;
 };
 
 template <int BITS>
 struct WLayout {
-  static constexpr int kRowBytes = kBK * BITS / 8;  // packed bytes per row per stage
+  static constexpr int kRowBytes = kBK * BITS / 8;  // packed bytes per row per unit
   static constexpr int kChunks = kRowBytes / 16;    // 16-byte chunks per row
   static constexpr int kValuesPerChunk = 128 / BITS;
   // physical 16-byte chunk of logical chunk c in row r under the TMA swizzle
@@ -66,6 +82,42 @@ struct WLayout {
     return BITS == 4 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
   }
 };
+
+__device__ __forceinline__ long long unit_begin(long long c, long long units, int P) { return c * units / P; }
+
+// CTA whose unit range contains unit x
+__device__ __forceinline__ int owner_of(long long x, long long units, int P) {
+  int c = static_cast<int>((x * P) / units);
+  while (c + 1 < P && unit_begin(c + 1, units, P) <= x) ++c;
+  while (c > 0 && unit_begin(c, units, P) > x) --c;
+  return c;
+}
+
+struct TileInfo {
+  int set, n0, tok0;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const QmmTcParams& p, int tile, bool dual) {
+  TileInfo ti;
+  const int ft = tile / p.n_tt;
+  ti.tok0 = (tile - ft * p.n_tt) * p.TN;
+  int set = 0;
+  if (!dual) {
+    if (ft >= p.tile_start[1]) set = 1;
+    if (ft >= p.tile_start[2]) set = 2;
+  }
+  ti.set = set;
+  ti.n0 = (ft - p.tile_start[set]) * kBM;
+  return ti;
+}
+
+template <int DT, int NACC>
+__device__ __forceinline__ float finish_value(const float (&acc)[NACC], int kind, float res) {
+  if (NACC == 2) return swiglu_rounded<DT>(round_to<DT>(acc[0]), round_to<DT>(acc[NACC - 1]));
+  float v = round_to<DT>(acc[0]);
+  if (kind == QMM_RESIDUAL) v = v + res;
+  return v;
+}
 
 template <int DT, int BITS, int DUAL>
 __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_constant__ QmmTcParams p) {
@@ -76,39 +128,30 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-  const int TN = p.TN, SS = p.SS;
+  const int TN = p.TN, SS = p.SS, nk = p.nk;
   const int x_stage_bytes = TN * 256;                 // 2 boxes of TN rows x 128 B
   const int w_set_bytes = kBM * WL::kRowBytes;
   const int w_stage_bytes = NACC * w_set_bytes;
   uint8_t* xs = smem;
   uint8_t* ws_ = smem + SS * x_stage_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ws_ + SS * w_stage_bytes);
+  T* stage_out = reinterpret_cast<T*>(ws_ + SS * w_stage_bytes);  // [TN][128] output staging
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(stage_out) + TN * kBM * sizeof(T));
   uint64_t* w_full = bars;
   uint64_t* x_full = bars + kMaxSS;
   uint64_t* s_empty = bars + 2 * kMaxSS;
   uint64_t* a_full = bars + 3 * kMaxSS;
   uint64_t* a_empty = a_full + 4;
   uint64_t* acc_full = a_empty + 4;
-  uint64_t* drain = acc_full + 1;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // ---- tile coordinates
-  const int ft = blockIdx.x;
-  int set = 0;
-  if (!DUAL) {
-    if (ft >= p.tile_start[1]) set = 1;
-    if (ft >= p.tile_start[2]) set = 2;
-  }
-  const int n0 = (ft - p.tile_start[set]) * kBM;
-  const int tok0 = blockIdx.y * TN;
-  const int split = blockIdx.z;
-  const int k_begin = static_cast<int>((static_cast<int64_t>(split) * p.nk) / p.splits);
-  const int k_end = static_cast<int>((static_cast<int64_t>(split + 1) * p.nk) / p.splits);
-  const int nkl = k_end - k_begin;
+  const int c = blockIdx.x;
+  const long long u0 = unit_begin(c, p.units, p.P);
+  const long long u1 = unit_begin(c + 1, p.units, p.P);
+  const int nunits = static_cast<int>(u1 - u0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMaxSS; ++i) {
@@ -120,10 +163,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       mbar_init(&a_full[i], 8);
       mbar_init(&a_empty[i], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
-    *last_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -132,44 +177,46 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&p.tmx);
-    for (int a = 0; a < NACC; ++a) prefetch_tmap(&p.tmw[DUAL ? a : set]);
+    for (int a = 0; a < (DUAL ? 2 : 3); ++a)
+      if (p.N[a] > 0) prefetch_tmap(&p.tmw[a]);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Dependents only start their own set-up before griddep_wait(); letting
-  // them launch now overlaps their launch latency with this kernel.
+  // Dependents only run set-up before their own griddep_wait(); letting them
+  // launch now hides their launch latency behind this kernel.
   griddep_launch();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const int kw_per_stage = kBK * BITS / 32;  // words of K per stage
-      const int pre = nkl < SS ? nkl : SS;
+      const int kw_per_stage = kBK * BITS / 32;  // words of K per unit
+      const int pre = nunits < SS ? nunits : SS;
       auto issue_w = [&](int i) {
+        const long long u = u0 + i;
+        const int tile = static_cast<int>(u / nk), k = static_cast<int>(u % nk);
+        const TileInfo ti = tile_info(p, tile, DUAL);
         const int s = i % SS;
-        const int kstage = k_begin + i;
         mbar_arrive_expect_tx(&w_full[s], w_stage_bytes);
         for (int a = 0; a < NACC; ++a)
-          tma_load_2d(ws_ + s * w_stage_bytes + a * w_set_bytes, &p.tmw[DUAL ? a : set], &w_full[s],
-                      kstage * kw_per_stage, n0);
+          tma_load_2d(ws_ + s * w_stage_bytes + a * w_set_bytes, &p.tmw[DUAL ? a : ti.set], &w_full[s],
+                      k * kw_per_stage, ti.n0);
       };
       auto issue_x = [&](int i) {
+        const long long u = u0 + i;
+        const int tile = static_cast<int>(u / nk), k = static_cast<int>(u % nk);
+        const int tok0 = (tile % p.n_tt) * TN;
         const int s = i % SS;
-        const int kstage = k_begin + i;
         mbar_arrive_expect_tx(&x_full[s], x_stage_bytes);
         for (int j = 0; j < 2; ++j)
-          tma_load_2d(xs + s * x_stage_bytes + j * TN * 128, &p.tmx, &x_full[s],
-                      kstage * kBK + 64 * j, tok0);
+          tma_load_2d(xs + s * x_stage_bytes + j * TN * 128, &p.tmx, &x_full[s], k * kBK + 64 * j, tok0);
       };
-      // Weights do not depend on the previous kernel: start them before the
-      // grid dependency resolves.
       int issued_w = 0, issued_x = 0;
       for (int i = 0; i < pre; ++i, ++issued_w) issue_w(i);
       griddep_wait();
       for (int i = 0; i < pre; ++i, ++issued_x) issue_x(i);
-      for (int i = pre; i < nkl; ++i) {
+      for (int i = pre; i < nunits; ++i) {
         const int s = i % SS;
         if (!mbar_wait(&s_empty[s], ((i / SS) & 1) ^ 1, abort_flag, 0x101)) break;
         issue_w(i);
@@ -178,7 +225,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         ++issued_x;
       }
       if (*abort_flag) {
-        // let every copy this thread issued land before shared memory is released
         for (int i = (issued_w > SS ? issued_w - SS : 0); i < issued_w; ++i)
           mbar_wait_drain(&w_full[i % SS], (i / SS) & 1, 200000000ull);
         for (int i = (issued_x > SS ? issued_x - SS : 0); i < issued_x; ++i)
@@ -190,188 +236,303 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(kBM, TN, DT == MT_BF16);
       bool issued = false;
-      for (int i = 0; i < nkl; ++i) {
-        const int s = i % SS, t = i % TS;
-        if (!mbar_wait(&x_full[s], (i / SS) & 1, abort_flag, 0x201)) break;
-        if (!mbar_wait(&a_full[t], (i / TS) & 1, abort_flag, 0x202)) break;
+      int use[2] = {0, 0};
+      int slot = 0;
+      int i = 0;
+      bool ok = true;
+      long long u = u0;
+      while (u < u1 && ok) {
+        const int klo = static_cast<int>(u % nk);
+        const int len = static_cast<int>(((nk - klo) < (u1 - u)) ? (nk - klo) : (u1 - u));
+        if (!mbar_wait(&acc_empty[slot], (use[slot] & 1) ^ 1, abort_flag, 0x203)) break;
         tc_fence_after();
-        const uint32_t xbase = smem_addr(xs + s * x_stage_bytes);
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint64_t bdesc = smem_desc_k_sw128(xbase + (kk >> 2) * TN * 128 + (kk & 3) * 32);
-#pragma unroll
-          for (int a = 0; a < NACC; ++a) {
-            const uint32_t a_tmem = tmem + kAccCols + (t * NACC + a) * 64 + kk * 8;
-            const uint32_t d_tmem = tmem + a * TN;
-            tc_mma_ts(d_tmem, a_tmem, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        const uint32_t d_base = tmem + slot * NACC * TN;
+        for (int j = 0; j < len; ++j, ++i) {
+          const int s = i % SS, t = i % TS;
+          if (!mbar_wait(&x_full[s], (i / SS) & 1, abort_flag, 0x201) ||
+              !mbar_wait(&a_full[t], (i / TS) & 1, abort_flag, 0x202)) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
+          const uint32_t xbase = smem_addr(xs + s * x_stage_bytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t bdesc = smem_desc_k_sw128(xbase + (kk >> 2) * TN * 128 + (kk & 3) * 32);
+#pragma unroll
+            for (int a = 0; a < NACC; ++a)
+              tc_mma_ts(d_base + a * TN, tmem + kAccCols + (t * NACC + a) * 64 + kk * 8, bdesc, idesc,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued = true;
+          tc_commit(&s_empty[s]);
+          tc_commit(&a_empty[t]);
         }
-        issued = true;
-        tc_commit(&s_empty[s]);
-        tc_commit(&a_empty[t]);
+        if (!ok) break;
+        tc_commit(&acc_full[slot]);
+        ++use[slot];
+        slot = (slot + 1) % p.acc_slots;
+        u += len;
       }
-      if (issued) tc_commit(acc_full);
       if (*abort_flag && issued) {
-        // MMAs still read tensor and shared memory: wait for them before teardown
         tc_commit(drain);
         mbar_wait_drain(drain, 0, 200000000ull);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && warp < kEpiWarp0) {
     // ------------------------------------------------------------ dequantisers
     const int q = warp & 3;
     const int wg = (warp - 4) >> 2;
-    const int r = q * 32 + lane;                 // weight row within the tile
+    const int r = q * 32 + lane;  // weight row within the tile
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    // single: WG wg converts chunks [wg*C/2, (wg+1)*C/2) of set `set`
-    // dual:   WG wg converts all chunks of set wg (0 gate, 1 up)
+    // single: WG wg converts chunks [wg*C/2, (wg+1)*C/2); dual: all chunks of set wg
     constexpr int kMyChunks = DUAL ? WL::kChunks : WL::kChunks / 2;
     const int aset = DUAL ? wg : 0;
-    const int wset = DUAL ? wg : set;
     const int c0 = DUAL ? 0 : wg * kMyChunks;
-    const int n = n0 + r;
-    const bool row_ok = n < p.N[wset];
-    const T* srow = static_cast<const T*>(p.s[wset]) + static_cast<int64_t>(row_ok ? n : 0) * p.G;
-    const T* brow = static_cast<const T*>(p.b[wset]) + static_cast<int64_t>(row_ok ? n : 0) * p.G;
-    bool ok = true;
-    for (int i = 0; i < nkl && ok; ++i) {
-      const int s = i % SS, t = i % TS;
-      const int kst = (k_begin + i) * kBK;
-      float sc[kMyChunks], bi[kMyChunks];
+    constexpr int kPairsPerChunk = WL::kValuesPerChunk / 2;
+    constexpr int kCols = kMyChunks * kPairsPerChunk;  // 32 (single) or 64 (dual)
+    float sc[kMyChunks], bi[kMyChunks];
+    auto load_sb = [&](int i, float* s_out, float* b_out) {
+      const long long u = u0 + i;
+      const int tile = static_cast<int>(u / nk), k = static_cast<int>(u % nk);
+      const TileInfo ti = tile_info(p, tile, DUAL);
+      const int wset = DUAL ? wg : ti.set;
+      const int n = ti.n0 + r;
+      const bool row_ok = n < p.N[wset];
+      const T* srow = static_cast<const T*>(p.s[wset]) + static_cast<long long>(row_ok ? n : 0) * p.G;
+      const T* brow = static_cast<const T*>(p.b[wset]) + static_cast<long long>(row_ok ? n : 0) * p.G;
 #pragma unroll
-      for (int c = 0; c < kMyChunks; ++c) {
-        const int g = (kst + (c0 + c) * WL::kValuesPerChunk) / p.group;
+      for (int cc = 0; cc < kMyChunks; ++cc) {
+        const int g = (k * kBK + (c0 + cc) * WL::kValuesPerChunk) / p.group;
         const bool gok = row_ok && g < p.G;
-        sc[c] = gok ? Elem<DT>::to_f(srow[g]) : 0.f;
-        bi[c] = gok ? Elem<DT>::to_f(brow[g]) : 0.f;
+        s_out[cc] = gok ? Elem<DT>::to_f(srow[g]) : 0.f;
+        b_out[cc] = gok ? Elem<DT>::to_f(brow[g]) : 0.f;
       }
-      if (!mbar_wait(&w_full[s], (i / SS) & 1, abort_flag, 0x301)) { ok = false; break; }
+    };
+    if (nunits > 0) load_sb(0, sc, bi);
+    for (int i = 0; i < nunits; ++i) {
+      const int s = i % SS, t = i % TS;
+      if (!mbar_wait(&w_full[s], (i / SS) & 1, abort_flag, 0x301)) break;
       uint4 wv[kMyChunks];
       const uint8_t* wrow = ws_ + s * w_stage_bytes + aset * w_set_bytes + r * WL::kRowBytes;
 #pragma unroll
-      for (int c = 0; c < kMyChunks; ++c)
-        wv[c] = *reinterpret_cast<const uint4*>(wrow + WL::phys(r, c0 + c) * 16);
+      for (int cc = 0; cc < kMyChunks; ++cc)
+        wv[cc] = *reinterpret_cast<const uint4*>(wrow + WL::phys(r, c0 + cc) * 16);
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[s]);
-      if (!mbar_wait(&a_empty[t], ((i / TS) & 1) ^ 1, abort_flag, 0x302)) { ok = false; break; }
-      constexpr int kPairsPerChunk = WL::kValuesPerChunk / 2;
-      constexpr int kCols = kMyChunks * kPairsPerChunk;  // 32 (single) or 64 (dual)
+      float scn[kMyChunks], bin[kMyChunks];
+      if (i + 1 < nunits) load_sb(i + 1, scn, bin);
+      if (!mbar_wait(&a_empty[t], ((i / TS) & 1) ^ 1, abort_flag, 0x302)) break;
       const uint32_t col0 = kAccCols + (t * NACC + aset) * 64 + (DUAL ? 0 : wg * 32);
 #pragma unroll
       for (int h = 0; h < kCols / 32; ++h) {
         uint32_t out[32];
         constexpr int kChunksPer32 = 32 / kPairsPerChunk;
 #pragma unroll
-        for (int c = 0; c < kChunksPer32; ++c)
-          dequant_chunk<DT, BITS>(wv[h * kChunksPer32 + c], sc[h * kChunksPer32 + c],
-                                  bi[h * kChunksPer32 + c], out + c * kPairsPerChunk);
+        for (int cc = 0; cc < kChunksPer32; ++cc)
+          dequant_chunk<DT, BITS>(wv[h * kChunksPer32 + cc], sc[h * kChunksPer32 + cc], bi[h * kChunksPer32 + cc],
+                                  out + cc * kPairsPerChunk);
         tmem_st32(tmem + lane_base + col0 + h * 32, out);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[t]);
+#pragma unroll
+      for (int cc = 0; cc < kMyChunks; ++cc) {
+        sc[cc] = scn[cc];
+        bi[cc] = bin[cc];
+      }
+    }
+  } else if (warp >= kEpiWarp0) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;                // accumulator row = weight row in the tile
+    const int et = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const T* res = static_cast<const T*>(p.residual);
+    griddep_wait();
+    int use[2] = {0, 0};
+    int slot = 0;
+    int shared_tiles[2] = {-1, -1};
+    bool alive = true;
+    long long u = u0;
+    while (u < u1) {
+      const int tile = static_cast<int>(u / nk);
+      const int klo = static_cast<int>(u % nk);
+      const int len = static_cast<int>(((nk - klo) < (u1 - u)) ? (nk - klo) : (u1 - u));
+      const bool shared = !(klo == 0 && len == nk);
+      const int pslot = (u == u0) ? 0 : 1;
+      const TileInfo ti = tile_info(p, tile, DUAL);
+      mbar_wait(&acc_full[slot], use[slot] & 1, abort_flag, 0x401);
+      named_barrier(kEpiBar, 128);
+      if (*abort_flag) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t acc_base = tmem + lane_base + slot * NACC * TN;
+      for (int c0 = 0; c0 < TN; c0 += 32) {
+        const int w = (TN - c0) < 32 ? (TN - c0) : 32;
+        uint32_t v[NACC][32];
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          if (w == 32) tmem_ld32(acc_base + a * TN + c0, v[a]);
+          else tmem_ld16(acc_base + a * TN + c0, v[a]);
+        }
+        tmem_wait_ld();
+        if (shared) {
+#pragma unroll
+          for (int a = 0; a < NACC; ++a) {
+            float* dst = p.partials + ((static_cast<long long>(c) * 2 + pslot) * NACC + a) * p.TNp * kBM +
+                         static_cast<long long>(c0) * kBM + r;
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (e < w) __stcg(dst + e * kBM, __uint_as_float(v[a][e]));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (e < w) {
+              float acc[NACC];
+#pragma unroll
+              for (int a = 0; a < NACC; ++a) acc[a] = __uint_as_float(v[a][e]);
+              // the residual is added at the coalesced store below
+              stage_out[(c0 + e) * kBM + r] = Elem<DT>::from_f(finish_value<DT, NACC>(acc, QMM_PLAIN, 0.f));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[slot]);
+      ++use[slot];
+      slot = (slot + 1) % p.acc_slots;
+      if (shared) {
+        __threadfence();
+        named_barrier(kEpiBar, 128);
+        if (et == 0) st_release_gpu(&p.flags[c * 2 + pslot], 1u);
+        shared_tiles[pslot] = tile;
+      } else {
+        named_barrier(kEpiBar, 128);
+        T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
+        const int N = p.N[DUAL ? 0 : ti.set];
+        for (int idx = et; idx < TN * 16; idx += 128) {
+          const int tok = idx >> 4, cc = idx & 15;
+          const int token = ti.tok0 + tok, n = ti.n0 + cc * 8;
+          if (token >= p.M || n >= N) continue;
+          const T* src = stage_out + tok * kBM + cc * 8;
+          const long long off = static_cast<long long>(token) * N + n;
+          if (p.vec && n + 8 <= N) {
+            uint4 val = *reinterpret_cast<const uint4*>(src);
+            if (!DUAL && p.kind == QMM_RESIDUAL) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(res + off);
+              T* ve = reinterpret_cast<T*>(&val);
+              const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ve[e] = Elem<DT>::from_f(Elem<DT>::to_f(ve[e]) + Elem<DT>::to_f(re[e]));
+            }
+            *reinterpret_cast<uint4*>(y + off) = val;
+          } else {
+            for (int e = 0; e < 8 && n + e < N; ++e) {
+              float vv = Elem<DT>::to_f(src[e]);
+              if (!DUAL && p.kind == QMM_RESIDUAL) vv = vv + Elem<DT>::to_f(res[off + e]);
+              y[off + e] = Elem<DT>::from_f(vv);
+            }
+          }
+        }
+        named_barrier(kEpiBar, 128);
+      }
+      u += len;
     }
 
-    // ------------------------------------------------------------ epilogue
-    // Every dequantiser thread reaches this barrier (all waits above are
-    // bounded); the decision to run the epilogue is then uniform, so the
-    // named barriers inside it cannot be left waiting.
-    const bool accd = ok && nkl > 0 && mbar_wait(acc_full, 0, abort_flag, 0x401);
-    if (!accd) *last_flag = 2;
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    const bool run_epilogue = (*last_flag != 2);
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (run_epilogue) {
-      tc_fence_after();
-      griddep_wait();
-      const int nchunks = (TN + 31) / 32;
-      const int tile_id = ft * gridDim.y + blockIdx.y;
-      bool finish = true;
-      if (p.splits > 1) {
-        // write this split's partial, [acc][row][TNp] per (tile, split)
-        for (int ci = wg; ci < nchunks; ci += 2) {
-#pragma unroll
-          for (int a = 0; a < NACC; ++a) {
-            uint32_t v[32];
-            tmem_ld32(tmem + lane_base + a * TN + ci * 32, v);
-            tmem_wait_ld();
-            float* dst = p.partials +
-                         ((static_cast<int64_t>(tile_id) * p.splits + split) * NACC + a) * kBM * p.TNp +
-                         static_cast<int64_t>(r) * p.TNp + ci * 32;
-#pragma unroll
-            for (int e = 0; e < 32; e += 4)
-              __stcg(reinterpret_cast<float4*>(dst + e),
-                     make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                                 __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3])));
+    // ---- reductions of the tiles this CTA shares with its neighbours
+    for (int ps = 0; ps < 2 && alive; ++ps) {
+      const int tile = shared_tiles[ps];
+      if (tile < 0) continue;
+      if (ps == 1 && tile == shared_tiles[0]) continue;
+      const long long t_lo = static_cast<long long>(tile) * nk;
+      const int ca = owner_of(t_lo, p.units, p.P);
+      const int cb = owner_of(t_lo + nk - 1, p.units, p.P);
+      const int S = cb - ca + 1;
+      const int j = c - ca;
+      // wait for every participant's partial
+      bool ok = true;
+      for (int cp = ca; cp <= cb && ok; ++cp) {
+        const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+        const uint32_t* f = &p.flags[cp * 2 + sl];
+        if (ld_acquire_gpu(f) == 1u) continue;
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu(f) != 1u) {
+          if (*abort_flag) {
+            ok = false;
+            break;
+          }
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            report_status(0x402);
+            ok = false;
+            break;
           }
         }
-        __threadfence();
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (threadIdx.x == 128) {
-          const uint32_t prev = atomicAdd(&p.counters[tile_id], 1u);
-          const int last = (prev == static_cast<uint32_t>(p.splits - 1));
-          if (last) p.counters[tile_id] = 0;  // ready for the next call
-          *last_flag = last;
-        }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        finish = *last_flag != 0;
-        if (finish) __threadfence();
       }
-      if (finish) {
-        T* y = static_cast<T*>(p.y[DUAL ? 0 : set]);
-        const int N = p.N[DUAL ? 0 : set];
-        const T* res = static_cast<const T*>(p.residual);
-        for (int ci = wg; ci < nchunks; ci += 2) {
-          float acc[NACC][32];
+      named_barrier(kEpiBar, 128);
+      if (*abort_flag) break;
+      // this participant reduces row groups [g_lo, g_hi) of 8 rows each
+      const int g_lo = (j * 16) / S, g_hi = ((j + 1) * 16) / S;
+      const TileInfo ti = tile_info(p, tile, DUAL);
+      T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
+      const int N = p.N[DUAL ? 0 : ti.set];
+      const int ng = g_hi - g_lo;
+      for (int idx = et; idx < TN * ng; idx += 128) {
+        const int tok = idx / ng, g = g_lo + idx % ng;
+        const int token = ti.tok0 + tok, n = ti.n0 + g * 8;
+        if (token >= p.M || n >= N) continue;
+        float acc[NACC][8];
+#pragma unroll
+        for (int a = 0; a < NACC; ++a)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[a][e] = 0.f;
+        for (int cp = ca; cp <= cb; ++cp) {
+          const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
 #pragma unroll
           for (int a = 0; a < NACC; ++a) {
-            uint32_t v[32];
-            tmem_ld32(tmem + lane_base + a * TN + ci * 32, v);
-            tmem_wait_ld();
-            if (p.splits > 1) {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) acc[a][e] = 0.f;
-              for (int sp = 0; sp < p.splits; ++sp) {
-                if (sp == split) {
-#pragma unroll
-                  for (int e = 0; e < 32; ++e) acc[a][e] += __uint_as_float(v[e]);
-                } else {
-                  const float* src = p.partials +
-                                     ((static_cast<int64_t>(tile_id) * p.splits + sp) * NACC + a) * kBM * p.TNp +
-                                     static_cast<int64_t>(r) * p.TNp + ci * 32;
-#pragma unroll
-                  for (int e = 0; e < 32; e += 4) {
-                    const float4 f = __ldcg(reinterpret_cast<const float4*>(src + e));
-                    acc[a][e] += f.x;
-                    acc[a][e + 1] += f.y;
-                    acc[a][e + 2] += f.z;
-                    acc[a][e + 3] += f.w;
-                  }
-                }
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) acc[a][e] = __uint_as_float(v[e]);
-            }
+            const float* src = p.partials + ((static_cast<long long>(cp) * 2 + sl) * NACC + a) * p.TNp * kBM +
+                               static_cast<long long>(tok) * kBM + g * 8;
+            const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src));
+            const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
+            acc[a][0] += x0.x; acc[a][1] += x0.y; acc[a][2] += x0.z; acc[a][3] += x0.w;
+            acc[a][4] += x1.x; acc[a][5] += x1.y; acc[a][6] += x1.z; acc[a][7] += x1.w;
           }
-          if (n < N) {
-            const int tcount = (TN - ci * 32) < 32 ? (TN - ci * 32) : 32;
-#pragma unroll 4
-            for (int e = 0; e < tcount; ++e) {
-              const int tok = tok0 + ci * 32 + e;
-              if (tok >= p.M) break;
-              const int64_t off = static_cast<int64_t>(tok) * N + n;
-              float v;
-              if (DUAL) {
-                v = swiglu_rounded<DT>(round_to<DT>(acc[0][e]), round_to<DT>(acc[NACC - 1][e]));
-              } else {
-                v = round_to<DT>(acc[0][e]);
-                if (p.kind == QMM_RESIDUAL) v += Elem<DT>::to_f(res[off]);
-              }
-              y[off] = Elem<DT>::from_f(v);
-            }
+        }
+        const long long off = static_cast<long long>(token) * N + n;
+        T outv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float av[NACC];
+#pragma unroll
+          for (int a = 0; a < NACC; ++a) av[a] = acc[a][e];
+          float rv = 0.f;
+          if (!DUAL && p.kind == QMM_RESIDUAL && n + e < N) rv = Elem<DT>::to_f(res[off + e]);
+          outv[e] = Elem<DT>::from_f(finish_value<DT, NACC>(av, DUAL ? QMM_PLAIN : p.kind, rv));
+        }
+        if (p.vec && n + 8 <= N) {
+          *reinterpret_cast<uint4*>(y + off) = *reinterpret_cast<const uint4*>(outv);
+        } else {
+          for (int e = 0; e < 8 && n + e < N; ++e) y[off + e] = outv[e];
+        }
+      }
+      named_barrier(kEpiBar, 128);
+      if (et == 0) {
+        __threadfence();
+        const uint32_t prev = atomicAdd(&p.done[tile], 1u);
+        if (prev == static_cast<uint32_t>(S - 1)) {
+          // every participant has read every partial of this tile: clear for the next call
+          for (int cp = ca; cp <= cb; ++cp) {
+            const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+            p.flags[cp * 2 + sl] = 0u;
           }
+          p.done[tile] = 0u;
         }
       }
     }
@@ -391,69 +552,50 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
 static size_t smem_bytes_for(int TN, int SS, int bits, int dual) {
   const int nacc = dual ? 2 : 1;
   const size_t stage = static_cast<size_t>(TN) * 256 + static_cast<size_t>(nacc) * kBM * (kBK * bits / 8);
-  return 1024 + SS * stage + 512;
+  return 1024 + SS * stage + static_cast<size_t>(TN) * kBM * 2 + 512;
 }
 
 static int pick_ss(int TN, int bits, int dual) {
   int ss = kMaxSS;
-  while (ss > 2 && smem_bytes_for(TN, ss, bits, dual) > 220 * 1024) --ss;
+  while (ss > 2 && smem_bytes_for(TN, ss, bits, dual) > static_cast<size_t>(kSmemLimit)) --ss;
   return ss;
 }
 
-static int tile_tn(int64_t M, int dual) {
-  const int64_t cap = dual ? 128 : 256;
-  int64_t tn = M < cap ? M : cap;
+static int tile_tn(int64_t M) {
+  int64_t tn = M < 128 ? M : 128;
   tn = (tn + 15) / 16 * 16;
   return static_cast<int>(tn);
 }
 
-static size_t ws_need(int64_t tiles, int splits, int nacc, int TNp) {
-  if (splits <= 1) return 0;
-  const size_t counters = (static_cast<size_t>(tiles) * 4 + 255) / 256 * 256;
-  return counters + static_cast<size_t>(tiles) * splits * nacc * kBM * TNp * 4;
-}
+struct WsLayout {
+  size_t flags, done, partials, total;
+};
 
-static int choose_splits(int64_t tiles, int nk, int sms, size_t ws_bytes, int nacc, int TNp) {
-  if (tiles >= sms) return 1;
-  int best = 1;
-  double best_cost = 1e30;
-  const int max_s = std::min(nk, 16);
-  for (int s = 1; s <= max_s; ++s) {
-    if (ws_need(tiles, s, nacc, TNp) > ws_bytes) break;
-    const int64_t waves = (tiles * s + sms - 1) / sms;
-    const double per = static_cast<double>((nk + s - 1) / s);
-    // the split reduction costs roughly a stage per extra partial
-    const double cost = waves * per + (s > 1 ? 0.5 + 0.1 * s : 0.0);
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = s;
-    }
-  }
-  return best;
+static WsLayout ws_layout(int P, int64_t tiles, int nacc, int TNp) {
+  (void)tiles;
+  WsLayout l;
+  l.flags = kWsQmmFlags;
+  l.done = kWsQmmDone;
+  l.partials = kWsCtlBytes;
+  l.total = l.partials + static_cast<size_t>(P) * 2 * nacc * TNp * kBM * 4;
+  return l;
 }
 
 size_t qmm_tc_workspace(int64_t M, int64_t n_total, int64_t K, int bits, int kind) {
   (void)bits;
+  (void)K;
   const int dual = kind == 1;
-  const int TN = tile_tn(M, dual);
-  const int TNp = (TN + 31) / 32 * 32;
-  const int64_t ttiles = (M + TN - 1) / TN;
-  const int64_t ft = dual ? (n_total / 2 + kBM - 1) / kBM : (n_total + kBM - 1) / kBM + 2;
-  const int nk = static_cast<int>((K + kBK - 1) / kBK);
-  return ws_need(ft * ttiles, std::min(nk, 16), dual ? 2 : 1, TNp);
+  const int TN = tile_tn(M);
+  const int64_t n_tt = (M + TN - 1) / TN;
+  const int64_t ft = dual ? (n_total / 2 + kBM - 1) / kBM : (n_total + kBM - 1) / kBM + 3;
+  return ws_layout(kMaxP, ft * n_tt, dual ? 2 : 1, TN).total;
 }
 
 template <int DT, int BITS, int DUAL>
-static int launch_tc(QmmTcParams& p, dim3 grid, size_t smem, cudaStream_t stream) {
+static int launch_tc(QmmTcParams& p, size_t smem, cudaStream_t stream) {
   auto k = qmm_tc_kernel<DT, BITS, DUAL>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  MT_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    MT_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
-  return launch(k, grid, dim3(kThreads), smem, stream, p);
+  if (int e = ensure_smem(k, kSmemLimit)) return e;
+  return launch(k, dim3(p.P), dim3(kThreads), smem, stream, p);
 }
 
 int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
@@ -473,19 +615,21 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
   p.G = static_cast<int>(r.K / r.group);
   p.kind = r.kind;
   p.residual = r.residual;
-  p.TN = tile_tn(r.M, dual);
-  p.TNp = (p.TN + 31) / 32 * 32;
+  p.TN = tile_tn(r.M);
+  p.TNp = p.TN;
   p.SS = pick_ss(p.TN, r.bits, dual);
   p.nk = static_cast<int>((r.K + kBK - 1) / kBK);
+  p.acc_slots = dual ? 1 : 2;
+  p.n_tt = static_cast<int>((r.M + p.TN - 1) / p.TN);
 
   const CUtensorMapDataType xdt =
       r.dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  rc = make_tmap_2d(&p.tmx, r.x, xdt, esz, r.K, r.M, r.K * esz, 64, p.TN,
-                    CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = make_tmap_2d(&p.tmx, r.x, xdt, esz, r.K, r.M, r.K * esz, 64, p.TN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != MT_OK) return rc;
   const int words = static_cast<int>(r.K * r.bits / 32);
   const int nsets = dual ? 2 : 3;
-  int tiles = 0;
+  int ftiles = 0;
+  bool vec = (r.residual == nullptr || aligned(r.residual, 16));
   p.tile_start[0] = 0;
   for (int s = 0; s < 3; ++s) {
     const QmmSetReq& q = r.set[s];
@@ -499,37 +643,44 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
       p.s[s] = q.s;
       p.b[s] = q.b;
       p.y[s] = q.y;
-      if (!dual) tiles += static_cast<int>((q.N + kBM - 1) / kBM);
+      if (!dual) ftiles += static_cast<int>((q.N + kBM - 1) / kBM);
+      if (q.y && (!aligned(q.y, 16) || q.N % 8 != 0)) vec = false;
     }
-    p.tile_start[s + 1] = tiles;
+    p.tile_start[s + 1] = ftiles;
   }
   if (dual) {
-    tiles = static_cast<int>((r.set[0].N + kBM - 1) / kBM);
+    ftiles = static_cast<int>((r.set[0].N + kBM - 1) / kBM);
     p.N[1] = p.N[0];
   }
-  const int ttiles = static_cast<int>((r.M + p.TN - 1) / p.TN);
-  const int64_t tiles_total = static_cast<int64_t>(tiles) * ttiles;
-  MT_CHECK_ARG(ttiles <= 65535, "qmm: M=%lld too large", (long long)r.M);
-  p.splits = choose_splits(tiles_total, p.nk, sms, r.ws ? r.ws_bytes : 0, dual ? 2 : 1, p.TNp);
-  if (p.splits > 1) {
-    const size_t counters = (static_cast<size_t>(tiles_total) * 4 + 255) / 256 * 256;
-    p.counters = static_cast<uint32_t*>(r.ws);
-    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(r.ws) + counters);
-    MT_CHECK_ARG(aligned(r.ws, 256), "qmm: workspace must be 256-byte aligned");
+  p.vec = vec ? 1 : 0;
+  p.tiles = ftiles * p.n_tt;
+  p.units = static_cast<long long>(p.tiles) * p.nk;
+  p.P = static_cast<int>(p.units < sms ? p.units : sms);
+  if (p.P > kMaxP) p.P = kMaxP;
+  if (static_cast<size_t>(p.tiles) > kWsQmmMaxTiles) {
+    set_error("qmm: %d tiles exceed the workspace's %zu tile counters (M=%lld too large for one call)", p.tiles,
+              kWsQmmMaxTiles, (long long)r.M);
+    return MT_ERR_UNSUPPORTED;
   }
+  const WsLayout wl = ws_layout(p.P, p.tiles, dual ? 2 : 1, p.TNp);
+  if (!r.ws || r.ws_bytes < wl.total || !aligned(r.ws, 256)) {
+    set_error("qmm: workspace of %zu bytes (256-aligned, zero-filled) required, got %zu", wl.total,
+              r.ws ? r.ws_bytes : (size_t)0);
+    return MT_ERR_WORKSPACE;
+  }
+  uint8_t* ws = static_cast<uint8_t*>(r.ws);
+  p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags);
+  p.done = reinterpret_cast<uint32_t*>(ws + wl.done);
+  p.partials = reinterpret_cast<float*>(ws + wl.partials);
+
   const size_t smem = smem_bytes_for(p.TN, p.SS, r.bits, dual);
-  const dim3 grid(tiles, ttiles, p.splits);
   const bool bf = r.dtype == MT_BF16;
   if (dual) {
-    if (bf) return r.bits == 4 ? launch_tc<MT_BF16, 4, 1>(p, grid, smem, stream)
-                               : launch_tc<MT_BF16, 8, 1>(p, grid, smem, stream);
-    return r.bits == 4 ? launch_tc<MT_F16, 4, 1>(p, grid, smem, stream)
-                       : launch_tc<MT_F16, 8, 1>(p, grid, smem, stream);
+    if (bf) return r.bits == 4 ? launch_tc<MT_BF16, 4, 1>(p, smem, stream) : launch_tc<MT_BF16, 8, 1>(p, smem, stream);
+    return r.bits == 4 ? launch_tc<MT_F16, 4, 1>(p, smem, stream) : launch_tc<MT_F16, 8, 1>(p, smem, stream);
   }
-  if (bf) return r.bits == 4 ? launch_tc<MT_BF16, 4, 0>(p, grid, smem, stream)
-                             : launch_tc<MT_BF16, 8, 0>(p, grid, smem, stream);
-  return r.bits == 4 ? launch_tc<MT_F16, 4, 0>(p, grid, smem, stream)
-                     : launch_tc<MT_F16, 8, 0>(p, grid, smem, stream);
+  if (bf) return r.bits == 4 ? launch_tc<MT_BF16, 4, 0>(p, smem, stream) : launch_tc<MT_BF16, 8, 0>(p, smem, stream);
+  return r.bits == 4 ? launch_tc<MT_F16, 4, 0>(p, smem, stream) : launch_tc<MT_F16, 8, 0>(p, smem, stream);
 }
 
 }  // namespace mt
