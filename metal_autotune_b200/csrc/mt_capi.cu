@@ -90,32 +90,50 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
-                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                 uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+int make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int rank,
+              const uint64_t* dims, const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
     return MT_ERR_CUDA;
   }
-  if (!aligned(base, 16) || row_stride_bytes % 16 != 0 || (box_inner * elem_bytes) % 16 != 0) {
-    set_error("tensor map: base %p / row stride %llu / box inner %u x %d B break the 16-byte rule",
-              base, (unsigned long long)row_stride_bytes, box_inner, elem_bytes);
+  if (rank < 2 || rank > 5) {
+    set_error("tensor map: rank %d outside 2..5", rank);
     return MT_ERR_INVALID_ARGUMENT;
   }
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+  bool ok = aligned(base, 16) && (box[0] * elem_bytes) % 16 == 0;
+  for (int i = 0; i + 1 < rank; ++i) ok = ok && strides[i] % 16 == 0;
+  if (!ok) {
+    set_error("tensor map: base %p / strides / box inner %u x %d B break the 16-byte rule", base, box[0],
+              elem_bytes);
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    estr[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
+  CUresult r = fn(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st, bx, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_error("cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, box %u x %u", (int)r,
-              (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+    set_error("cuTensorMapEncodeTiled failed (%d): rank %d, dims %llu x %llu, box %u x %u", (int)r, rank,
+              (unsigned long long)dims[0], (unsigned long long)dims[1], box[0], box[1]);
     return MT_ERR_CUDA;
   }
   return MT_OK;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {row_stride_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  return make_tmap(map, base, dt, elem_bytes, 2, dims, strides, box, swizzle);
 }
 
 }  // namespace mt

@@ -12,4 +12,10 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                  uint32_t box_outer, CUtensorMapSwizzle swizzle);
 
+// Tiled tensor map of `rank` (2..5) dimensions, innermost first: dims[rank],
+// byte strides of dimensions 1..rank-1 in strides[rank-1] (any order, each a
+// multiple of 16), box[rank] elements. Out-of-range box elements read as zero.
+int make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int rank,
+              const uint64_t* dims, const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
 }  // namespace mt

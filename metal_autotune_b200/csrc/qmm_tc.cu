@@ -9,12 +9,13 @@
 // across tile boundaries without draining.
 //
 // Roles (512 threads):
-//   warp 0      TMA producer: per unit, the packed weight tile (128 rows x
-//               64 B for 4-bit, 64-byte swizzle) and the x tile (TN rows x 128
-//               bf16, 128-byte swizzle), into a ring of SS shared-memory slots.
-//               The first SS weight tiles are issued before the grid
-//               dependency resolves (weights never depend on the previous
-//               kernel).
+//   warps 0,2,3 TMA producers, one per stream: warp 0 the x tile (TN rows x
+//               2 x 64 bf16, 128-byte swizzle, one 3-D copy), warp 2 (and 3
+//               for the second weight set of SwiGLU) the packed weight tile
+//               (128 rows x 64 B for 4-bit, 64-byte swizzle), into a ring of SS
+//               shared-memory slots. The first SS weight tiles are issued
+//               before the grid dependency resolves (weights never depend on
+//               the previous kernel).
 //   warp 1      TMEM owner and MMA issuer: tcgen05.mma.kind::f16 with the
 //               dequantised weights as the A operand read from tensor memory
 //               and x as the B operand from shared memory; fp32 accumulators
@@ -69,7 +70,7 @@ struct QmmTcParams {
   int N[3];
   int tile_start[4];   // prefix sums of feature tiles per set
   int M, K, G, group;
-  int TN, TNp, SS, nk, kind, n_tt, tiles, P, acc_slots, vec;
+  int TN, TNp, SS, nk, kind, n_tt, tiles, P, acc_slots, vec, sb_vec, gshift;
 };
 
 template <int BITS>
@@ -99,7 +100,7 @@ struct TileInfo {
 
 __device__ __forceinline__ TileInfo tile_info(const QmmTcParams& p, int tile, bool dual) {
   TileInfo ti;
-  const int ft = tile / p.n_tt;
+  const int ft = p.n_tt == 1 ? tile : tile / p.n_tt;
   ti.tok0 = (tile - ft * p.n_tt) * p.TN;
   int set = 0;
   if (!dual) {
@@ -119,6 +120,9 @@ __device__ __forceinline__ float finish_value(const float (&acc)[NACC], int kind
   return v;
 }
 
+// Bytes of the output staging area: TN x 128 finished 16-bit values.
+__host__ __device__ constexpr int stage_bytes_for(int TN) { return TN * kBM * 2; }
+
 template <int DT, int BITS, int DUAL>
 __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_constant__ QmmTcParams p) {
   using T = typename Elem<DT>::T;
@@ -134,18 +138,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   const int w_stage_bytes = NACC * w_set_bytes;
   uint8_t* xs = smem;
   uint8_t* ws_ = smem + SS * x_stage_bytes;
-  T* stage_out = reinterpret_cast<T*>(ws_ + SS * w_stage_bytes);  // [TN][128] output staging
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(stage_out) + TN * kBM * sizeof(T));
-  uint64_t* w_full = bars;
-  uint64_t* x_full = bars + kMaxSS;
-  uint64_t* s_empty = bars + 2 * kMaxSS;
-  uint64_t* a_full = bars + 3 * kMaxSS;
+  // output staging: [TN][128] finished values
+  T* stage_out = reinterpret_cast<T*>(ws_ + SS * w_stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(stage_out) + stage_bytes_for(TN));
+  uint64_t* w_full = bars;                // [2][kMaxSS]: weight set 0 / 1 landed
+  uint64_t* x_full = bars + 2 * kMaxSS;
+  uint64_t* s_empty = bars + 3 * kMaxSS;
+  uint64_t* a_full = bars + 4 * kMaxSS;
   uint64_t* a_empty = a_full + 4;
   uint64_t* acc_full = a_empty + 4;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* shared_tile_slot = abort_flag + 1;  // [2]: tiles this CTA shares (first / last segment)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
@@ -156,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMaxSS; ++i) {
       mbar_init(&w_full[i], 1);
+      mbar_init(&w_full[kMaxSS + i], 1);
       mbar_init(&x_full[i], 1);
       mbar_init(&s_empty[i], 1 + 8);
     }
@@ -169,6 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    shared_tile_slot[0] = -1;
+    shared_tile_slot[1] = -1;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -188,47 +197,48 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   // launch now hides their launch latency behind this kernel.
   griddep_launch();
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == 2 || (DUAL && warp == 3)) {
+    // ------------------------------------------------------------ producers
+    // One warp per stream (x; weight set 0; weight set 1 when dual): copies
+    // issued by different warps are in flight together, while one thread's
+    // successive copies largely serialise.
     if (lane == 0) {
+      const bool is_x = warp == 0;
+      const int a = warp == 3 ? 1 : 0;
       const int kw_per_stage = kBK * BITS / 32;  // words of K per unit
       const int pre = nunits < SS ? nunits : SS;
-      auto issue_w = [&](int i) {
-        const long long u = u0 + i;
-        const int tile = static_cast<int>(u / nk), k = static_cast<int>(u % nk);
-        const TileInfo ti = tile_info(p, tile, DUAL);
+      const int tile0 = static_cast<int>(u0 / nk);
+      int it_tile = tile0, it_k = static_cast<int>(u0 - static_cast<long long>(tile0) * nk);
+      uint64_t* full = is_x ? x_full : w_full + a * kMaxSS;
+      const int bytes = is_x ? x_stage_bytes : w_set_bytes;
+      auto issue = [&](int i) {
+        const TileInfo ti = tile_info(p, it_tile, DUAL);
         const int s = i % SS;
-        mbar_arrive_expect_tx(&w_full[s], w_stage_bytes);
-        for (int a = 0; a < NACC; ++a)
-          tma_load_2d(ws_ + s * w_stage_bytes + a * w_set_bytes, &p.tmw[DUAL ? a : ti.set], &w_full[s],
-                      k * kw_per_stage, ti.n0);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        if (is_x)
+          tma_load_3d(xs + s * x_stage_bytes, &p.tmx, &full[s], 0, ti.tok0, it_k * 2);
+        else
+          tma_load_2d(ws_ + s * w_stage_bytes + a * w_set_bytes, &p.tmw[DUAL ? a : ti.set], &full[s],
+                      it_k * kw_per_stage, ti.n0);
+        if (++it_k == nk) {
+          it_k = 0;
+          ++it_tile;
+        }
       };
-      auto issue_x = [&](int i) {
-        const long long u = u0 + i;
-        const int tile = static_cast<int>(u / nk), k = static_cast<int>(u % nk);
-        const int tok0 = (tile % p.n_tt) * TN;
-        const int s = i % SS;
-        mbar_arrive_expect_tx(&x_full[s], x_stage_bytes);
-        for (int j = 0; j < 2; ++j)
-          tma_load_2d(xs + s * x_stage_bytes + j * TN * 128, &p.tmx, &x_full[s], k * kBK + 64 * j, tok0);
-      };
-      int issued_w = 0, issued_x = 0;
-      for (int i = 0; i < pre; ++i, ++issued_w) issue_w(i);
-      griddep_wait();
-      for (int i = 0; i < pre; ++i, ++issued_x) issue_x(i);
+      int issued = 0;
+      // weights never depend on the previous kernel: their first stages are
+      // issued before the grid dependency resolves
+      if (is_x) griddep_wait();
+      for (int i = 0; i < pre; ++i, ++issued) issue(i);
       for (int i = pre; i < nunits; ++i) {
         const int s = i % SS;
-        if (!mbar_wait(&s_empty[s], ((i / SS) & 1) ^ 1, abort_flag, 0x101)) break;
-        issue_w(i);
-        ++issued_w;
-        issue_x(i);
-        ++issued_x;
+        if (!mbar_wait(&s_empty[s], ((i / SS) & 1) ^ 1, abort_flag, is_x ? 0x101 : 0x102)) break;
+        issue(i);
+        ++issued;
       }
       if (*abort_flag) {
-        for (int i = (issued_w > SS ? issued_w - SS : 0); i < issued_w; ++i)
-          mbar_wait_drain(&w_full[i % SS], (i / SS) & 1, 200000000ull);
-        for (int i = (issued_x > SS ? issued_x - SS : 0); i < issued_x; ++i)
-          mbar_wait_drain(&x_full[i % SS], (i / SS) & 1, 200000000ull);
+        for (int i = (issued > SS ? issued - SS : 0); i < issued; ++i)
+          mbar_wait_drain(&full[i % SS], (i / SS) & 1, 200000000ull);
       }
     }
   } else if (warp == 1) {
@@ -291,28 +301,76 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     const int c0 = DUAL ? 0 : wg * kMyChunks;
     constexpr int kPairsPerChunk = WL::kValuesPerChunk / 2;
     constexpr int kCols = kMyChunks * kPairsPerChunk;  // 32 (single) or 64 (dual)
-    float sc[kMyChunks], bi[kMyChunks];
-    auto load_sb = [&](int i, float* s_out, float* b_out) {
-      const long long u = u0 + i;
-      const int tile = static_cast<int>(u / nk), k = static_cast<int>(u % nk);
+    // Scales and biases: each thread holds an aligned block of 8 consecutive
+    // groups of its row (one 16-byte load each, raw element bits), which
+    // covers group/16 units (4 at group 64). Rows are G*2 bytes apart, so
+    // per-unit scalar loads would touch one sector per lane per load; block
+    // loads cut that 8x. When a block comes into use, the next one is loaded.
+    // Unit bookkeeping is incremental: no integer division in the loop.
+    const int gshift = p.gshift;            // log2(group)
+    const int upb = p.group >> 4;           // units per 8-group block
+    uint4 sc_cur = make_uint4(0, 0, 0, 0), bi_cur = sc_cur, sc_nxt = sc_cur, bi_nxt = sc_cur;
+    auto load_block = [&](int tile, int k, uint4& s_out, uint4& b_out) {
       const TileInfo ti = tile_info(p, tile, DUAL);
       const int wset = DUAL ? wg : ti.set;
       const int n = ti.n0 + r;
       const bool row_ok = n < p.N[wset];
+      const int gb = ((k * kBK) >> gshift) & ~7;
       const T* srow = static_cast<const T*>(p.s[wset]) + static_cast<long long>(row_ok ? n : 0) * p.G;
       const T* brow = static_cast<const T*>(p.b[wset]) + static_cast<long long>(row_ok ? n : 0) * p.G;
+      if (row_ok && p.sb_vec && gb + 8 <= p.G) {
+        s_out = __ldg(reinterpret_cast<const uint4*>(srow + gb));
+        b_out = __ldg(reinterpret_cast<const uint4*>(brow + gb));
+      } else {
+        uint16_t sv[8], bv[8];
 #pragma unroll
-      for (int cc = 0; cc < kMyChunks; ++cc) {
-        const int g = (k * kBK + (c0 + cc) * WL::kValuesPerChunk) / p.group;
-        const bool gok = row_ok && g < p.G;
-        s_out[cc] = gok ? Elem<DT>::to_f(srow[g]) : 0.f;
-        b_out[cc] = gok ? Elem<DT>::to_f(brow[g]) : 0.f;
+        for (int e = 0; e < 8; ++e) {
+          const bool ok = row_ok && gb + e < p.G;
+          sv[e] = ok ? reinterpret_cast<const uint16_t*>(srow)[gb + e] : 0;
+          bv[e] = ok ? reinterpret_cast<const uint16_t*>(brow)[gb + e] : 0;
+        }
+        s_out = make_uint4(sv[0] | (uint32_t(sv[1]) << 16), sv[2] | (uint32_t(sv[3]) << 16),
+                           sv[4] | (uint32_t(sv[5]) << 16), sv[6] | (uint32_t(sv[7]) << 16));
+        b_out = make_uint4(bv[0] | (uint32_t(bv[1]) << 16), bv[2] | (uint32_t(bv[3]) << 16),
+                           bv[4] | (uint32_t(bv[5]) << 16), bv[6] | (uint32_t(bv[7]) << 16));
       }
     };
-    if (nunits > 0) load_sb(0, sc, bi);
+    // element e (0..7) of a block, widened to float
+    auto pick = [](const uint4& v, int e) -> float {
+      const uint32_t w = (e < 4) ? ((e < 2) ? v.x : v.y) : ((e < 6) ? v.z : v.w);
+      const uint32_t bits = (e & 1) ? (w >> 16) : (w & 0xFFFFu);
+      if constexpr (DT == MT_BF16) return __uint_as_float(bits << 16);
+      else return __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+    };
+    // units from (tile, k) to the start of the next block (or of the next tile)
+    auto to_next_block = [&](int k) {
+      const int a = upb - (k & (upb - 1)), b = nk - k;
+      return a < b ? a : b;
+    };
+    int tile = static_cast<int>(u0 / nk), k = static_cast<int>(u0 - static_cast<long long>(tile) * nk);
+    int next_start = nunits;  // unit index where the prefetched block takes over
+    if (nunits > 0) {
+      load_block(tile, k, sc_cur, bi_cur);
+      const int d = to_next_block(k);
+      if (d < nunits) {
+        next_start = d;
+        const bool wrap = (k + d == nk);
+        load_block(wrap ? tile + 1 : tile, wrap ? 0 : k + d, sc_nxt, bi_nxt);
+      }
+    }
     for (int i = 0; i < nunits; ++i) {
       const int s = i % SS, t = i % TS;
-      if (!mbar_wait(&w_full[s], (i / SS) & 1, abort_flag, 0x301)) break;
+      if (i == next_start) {
+        sc_cur = sc_nxt;
+        bi_cur = bi_nxt;
+        const int d = to_next_block(k);
+        if (i + d < nunits) {
+          next_start = i + d;
+          const bool wrap = (k + d == nk);
+          load_block(wrap ? tile + 1 : tile, wrap ? 0 : k + d, sc_nxt, bi_nxt);
+        }
+      }
+      if (!mbar_wait_warp(&w_full[aset * kMaxSS + s], (i / SS) & 1, abort_flag, 0x301)) break;
       uint4 wv[kMyChunks];
       const uint8_t* wrow = ws_ + s * w_stage_bytes + aset * w_set_bytes + r * WL::kRowBytes;
 #pragma unroll
@@ -320,28 +378,29 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         wv[cc] = *reinterpret_cast<const uint4*>(wrow + WL::phys(r, c0 + cc) * 16);
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[s]);
-      float scn[kMyChunks], bin[kMyChunks];
-      if (i + 1 < nunits) load_sb(i + 1, scn, bin);
-      if (!mbar_wait(&a_empty[t], ((i / TS) & 1) ^ 1, abort_flag, 0x302)) break;
+      const int kst = k * kBK;
+      const int gb = (kst >> gshift) & ~7;
+      if (!mbar_wait_warp(&a_empty[t], ((i / TS) & 1) ^ 1, abort_flag, 0x302)) break;
       const uint32_t col0 = kAccCols + (t * NACC + aset) * 64 + (DUAL ? 0 : wg * 32);
 #pragma unroll
       for (int h = 0; h < kCols / 32; ++h) {
         uint32_t out[32];
         constexpr int kChunksPer32 = 32 / kPairsPerChunk;
 #pragma unroll
-        for (int cc = 0; cc < kChunksPer32; ++cc)
-          dequant_chunk<DT, BITS>(wv[h * kChunksPer32 + cc], sc[h * kChunksPer32 + cc], bi[h * kChunksPer32 + cc],
-                                  out + cc * kPairsPerChunk);
+        for (int cc = 0; cc < kChunksPer32; ++cc) {
+          const int ch = h * kChunksPer32 + cc;
+          const int e = ((kst + (c0 + ch) * WL::kValuesPerChunk) >> gshift) - gb;
+          dequant_chunk<DT, BITS>(wv[ch], pick(sc_cur, e), pick(bi_cur, e), out + cc * kPairsPerChunk);
+        }
         tmem_st32(tmem + lane_base + col0 + h * 32, out);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[t]);
-#pragma unroll
-      for (int cc = 0; cc < kMyChunks; ++cc) {
-        sc[cc] = scn[cc];
-        bi[cc] = bin[cc];
+      if (++k == nk) {
+        k = 0;
+        ++tile;
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -354,8 +413,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     griddep_wait();
     int use[2] = {0, 0};
     int slot = 0;
-    int shared_tiles[2] = {-1, -1};
-    bool alive = true;
     long long u = u0;
     while (u < u1) {
       const int tile = static_cast<int>(u / nk);
@@ -364,12 +421,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       const bool shared = !(klo == 0 && len == nk);
       const int pslot = (u == u0) ? 0 : 1;
       const TileInfo ti = tile_info(p, tile, DUAL);
-      mbar_wait(&acc_full[slot], use[slot] & 1, abort_flag, 0x401);
-      named_barrier(kEpiBar, 128);
-      if (*abort_flag) {
-        alive = false;
-        break;
-      }
+      const bool got = mbar_wait(&acc_full[slot], use[slot] & 1, abort_flag, 0x401);
+      if (named_barrier_or(kEpiBar, 128, !got || *abort_flag)) break;
       tc_fence_after();
       const uint32_t acc_base = tmem + lane_base + slot * NACC * TN;
       for (int c0 = 0; c0 < TN; c0 += 32) {
@@ -382,6 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         }
         tmem_wait_ld();
         if (shared) {
+          // fp32 partial, layout [token][row]: for each token a warp writes 32
+          // consecutive rows, one 128-byte line per store instruction
 #pragma unroll
           for (int a = 0; a < NACC; ++a) {
             float* dst = p.partials + ((static_cast<long long>(c) * 2 + pslot) * NACC + a) * p.TNp * kBM +
@@ -411,8 +466,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       if (shared) {
         __threadfence();
         named_barrier(kEpiBar, 128);
-        if (et == 0) st_release_gpu(&p.flags[c * 2 + pslot], 1u);
-        shared_tiles[pslot] = tile;
+        if (et == 0) {
+          st_release_gpu(&p.flags[c * 2 + pslot], 1u);
+          shared_tile_slot[pslot] = tile;
+        }
       } else {
         named_barrier(kEpiBar, 128);
         T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
@@ -445,105 +502,153 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       }
       u += len;
     }
-
-    // ---- reductions of the tiles this CTA shares with its neighbours
-    for (int ps = 0; ps < 2 && alive; ++ps) {
-      const int tile = shared_tiles[ps];
-      if (tile < 0) continue;
-      if (ps == 1 && tile == shared_tiles[0]) continue;
-      const long long t_lo = static_cast<long long>(tile) * nk;
-      const int ca = owner_of(t_lo, p.units, p.P);
-      const int cb = owner_of(t_lo + nk - 1, p.units, p.P);
-      const int S = cb - ca + 1;
-      const int j = c - ca;
-      // wait for every participant's partial
-      bool ok = true;
-      for (int cp = ca; cp <= cb && ok; ++cp) {
-        const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
-        const uint32_t* f = &p.flags[cp * 2 + sl];
-        if (ld_acquire_gpu(f) == 1u) continue;
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_gpu(f) != 1u) {
-          if (*abort_flag) {
-            ok = false;
-            break;
-          }
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            *abort_flag = 1;
-            report_status(0x402);
-            ok = false;
-            break;
-          }
-        }
-      }
-      named_barrier(kEpiBar, 128);
-      if (*abort_flag) break;
-      // this participant reduces row groups [g_lo, g_hi) of 8 rows each
-      const int g_lo = (j * 16) / S, g_hi = ((j + 1) * 16) / S;
-      const TileInfo ti = tile_info(p, tile, DUAL);
-      T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
-      const int N = p.N[DUAL ? 0 : ti.set];
-      const int ng = g_hi - g_lo;
-      for (int idx = et; idx < TN * ng; idx += 128) {
-        const int tok = idx / ng, g = g_lo + idx % ng;
-        const int token = ti.tok0 + tok, n = ti.n0 + g * 8;
-        if (token >= p.M || n >= N) continue;
-        float acc[NACC][8];
-#pragma unroll
-        for (int a = 0; a < NACC; ++a)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[a][e] = 0.f;
-        for (int cp = ca; cp <= cb; ++cp) {
-          const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
-#pragma unroll
-          for (int a = 0; a < NACC; ++a) {
-            const float* src = p.partials + ((static_cast<long long>(cp) * 2 + sl) * NACC + a) * p.TNp * kBM +
-                               static_cast<long long>(tok) * kBM + g * 8;
-            const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src));
-            const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
-            acc[a][0] += x0.x; acc[a][1] += x0.y; acc[a][2] += x0.z; acc[a][3] += x0.w;
-            acc[a][4] += x1.x; acc[a][5] += x1.y; acc[a][6] += x1.z; acc[a][7] += x1.w;
-          }
-        }
-        const long long off = static_cast<long long>(token) * N + n;
-        T outv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          float av[NACC];
-#pragma unroll
-          for (int a = 0; a < NACC; ++a) av[a] = acc[a][e];
-          float rv = 0.f;
-          if (!DUAL && p.kind == QMM_RESIDUAL && n + e < N) rv = Elem<DT>::to_f(res[off + e]);
-          outv[e] = Elem<DT>::from_f(finish_value<DT, NACC>(av, DUAL ? QMM_PLAIN : p.kind, rv));
-        }
-        if (p.vec && n + 8 <= N) {
-          *reinterpret_cast<uint4*>(y + off) = *reinterpret_cast<const uint4*>(outv);
-        } else {
-          for (int e = 0; e < 8 && n + e < N; ++e) y[off + e] = outv[e];
-        }
-      }
-      named_barrier(kEpiBar, 128);
-      if (et == 0) {
-        __threadfence();
-        const uint32_t prev = atomicAdd(&p.done[tile], 1u);
-        if (prev == static_cast<uint32_t>(S - 1)) {
-          // every participant has read every partial of this tile: clear for the next call
-          for (int cp = ca; cp <= cb; ++cp) {
-            const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
-            p.flags[cp * 2 + sl] = 0u;
-          }
-          p.done[tile] = 0u;
-        }
-      }
-    }
   }
 
-  // ---- teardown: every thread arrives here, including after an abort
+  // ---- every role is done with tensor memory: free it before the reductions,
+  // so a dependent kernel's CTA waiting on this SM can allocate
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+
+  // ---- reductions of the tiles this CTA shares with its neighbours, by all threads
+  const T* res = static_cast<const T*>(p.residual);
+  for (int ps = 0; ps < 2; ++ps) {
+    const int tile = shared_tile_slot[ps];
+    if (tile < 0) continue;
+    if (ps == 1 && tile == shared_tile_slot[0]) continue;
+    const long long t_lo = static_cast<long long>(tile) * nk;
+    const int ca = owner_of(t_lo, p.units, p.P);
+    const int cb = owner_of(t_lo + nk - 1, p.units, p.P);
+    const int S = cb - ca + 1;
+    const int j = c - ca;
+    // wait for every participant's partial: thread jj polls participant ca+jj
+    for (int jj = threadIdx.x; jj < S; jj += kThreads) {
+      const int cp = ca + jj;
+      const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+      const uint32_t* f = &p.flags[cp * 2 + sl];
+      if (ld_acquire_gpu(f) == 1u) continue;
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_gpu(f) != 1u) {
+        if (*abort_flag) break;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          *abort_flag = 1;
+          report_status(0x402);
+          break;
+        }
+      }
+    }
+    __threadfence();
+    if (__syncthreads_or(*abort_flag)) break;
+    // this participant reduces row groups [g_lo, g_hi) of 8 rows; a work item
+    // is (token, 4 rows): one float4 per partial and accumulator. A thread
+    // takes kJ items per pass and loads kPB partials of all of them at once,
+    // so 8 float4 loads are in flight per thread.
+    const int g_lo = (j * 16) / S, g_hi = ((j + 1) * 16) / S;
+    const int quads = (g_hi - g_lo) * 2;
+    const int items = TN * quads;
+    const TileInfo ti = tile_info(p, tile, DUAL);
+    T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
+    const int N = p.N[DUAL ? 0 : ti.set];
+    const long long slot_elems = static_cast<long long>(p.TNp) * kBM;
+    constexpr int kJ = 2;
+    constexpr int kPB = 4 / NACC;
+    for (int base = 0; base < items; base += kThreads * kJ) {
+      int poff[kJ];  // element offset inside a partial slot, or -1
+      int tokv[kJ], nv[kJ];
+#pragma unroll
+      for (int jj = 0; jj < kJ; ++jj) {
+        const int idx = base + jj * kThreads + threadIdx.x;
+        const int tok = idx / quads, rq = g_lo * 8 + (idx - tok * quads) * 4;
+        tokv[jj] = ti.tok0 + tok;
+        nv[jj] = ti.n0 + rq;
+        poff[jj] = (idx < items && tokv[jj] < p.M && nv[jj] < N) ? tok * kBM + rq : -1;
+      }
+      float acc[kJ][NACC][4];
+#pragma unroll
+      for (int jj = 0; jj < kJ; ++jj)
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) acc[jj][a][0] = acc[jj][a][1] = acc[jj][a][2] = acc[jj][a][3] = 0.f;
+      // partials summed in participant (= K) order
+      for (int cpb = ca; cpb <= cb; cpb += kPB) {
+        float4 xv[kPB][kJ][NACC];
+#pragma unroll
+        for (int d = 0; d < kPB; ++d) {
+          const int cp = cpb + d;
+          if (cp > cb) break;
+          const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+          const float* src = p.partials + (static_cast<long long>(cp) * 2 + sl) * NACC * slot_elems;
+#pragma unroll
+          for (int jj = 0; jj < kJ; ++jj)
+            if (poff[jj] >= 0) {
+#pragma unroll
+              for (int a = 0; a < NACC; ++a)
+                xv[d][jj][a] = __ldcg(reinterpret_cast<const float4*>(src + a * slot_elems + poff[jj]));
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < kPB; ++d) {
+          if (cpb + d > cb) break;
+#pragma unroll
+          for (int jj = 0; jj < kJ; ++jj)
+            if (poff[jj] >= 0) {
+#pragma unroll
+              for (int a = 0; a < NACC; ++a) {
+                acc[jj][a][0] += xv[d][jj][a].x;
+                acc[jj][a][1] += xv[d][jj][a].y;
+                acc[jj][a][2] += xv[d][jj][a].z;
+                acc[jj][a][3] += xv[d][jj][a].w;
+              }
+            }
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < kJ; ++jj) {
+        if (poff[jj] < 0) continue;
+        const int n = nv[jj];
+        const long long off = static_cast<long long>(tokv[jj]) * N + n;
+        const bool full4 = p.vec && n + 4 <= N;
+        T resv[4];
+        if (!DUAL && p.kind == QMM_RESIDUAL) {
+          if (full4) {
+            *reinterpret_cast<uint2*>(resv) = *reinterpret_cast<const uint2*>(res + off);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) resv[e] = (n + e < N) ? res[off + e] : Elem<DT>::from_f(0.f);
+          }
+        }
+        T outv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float av[NACC];
+#pragma unroll
+          for (int a = 0; a < NACC; ++a) av[a] = acc[jj][a][e];
+          const float rv = (!DUAL && p.kind == QMM_RESIDUAL) ? Elem<DT>::to_f(resv[e]) : 0.f;
+          outv[e] = Elem<DT>::from_f(finish_value<DT, NACC>(av, DUAL ? QMM_PLAIN : p.kind, rv));
+        }
+        if (full4) {
+          *reinterpret_cast<uint2*>(y + off) = *reinterpret_cast<const uint2*>(outv);
+        } else {
+          for (int e = 0; e < 4 && n + e < N; ++e) y[off + e] = outv[e];
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const uint32_t prev = atomicAdd(&p.done[tile], 1u);
+      if (prev == static_cast<uint32_t>(S - 1)) {
+        // every participant has read every partial of this tile: clear for the next call
+        for (int cp = ca; cp <= cb; ++cp) {
+          const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+          p.flags[cp * 2 + sl] = 0u;
+        }
+        p.done[tile] = 0u;
+      }
+    }
   }
 }
 
@@ -552,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
 static size_t smem_bytes_for(int TN, int SS, int bits, int dual) {
   const int nacc = dual ? 2 : 1;
   const size_t stage = static_cast<size_t>(TN) * 256 + static_cast<size_t>(nacc) * kBM * (kBK * bits / 8);
-  return 1024 + SS * stage + static_cast<size_t>(TN) * kBM * 2 + 512;
+  return 1024 + SS * stage + stage_bytes_for(TN) + 512;
 }
 
 static int pick_ss(int TN, int bits, int dual) {
@@ -612,6 +717,7 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
   p.M = static_cast<int>(r.M);
   p.K = static_cast<int>(r.K);
   p.group = r.group;
+  p.gshift = r.group == 32 ? 5 : r.group == 64 ? 6 : 7;
   p.G = static_cast<int>(r.K / r.group);
   p.kind = r.kind;
   p.residual = r.residual;
@@ -624,7 +730,14 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
 
   const CUtensorMapDataType xdt =
       r.dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  rc = make_tmap_2d(&p.tmx, r.x, xdt, esz, r.K, r.M, r.K * esz, 64, p.TN, CU_TENSOR_MAP_SWIZZLE_128B);
+  {
+    // x as (64 values, M rows, K/64 blocks): one copy brings both 64-wide K
+    // halves of a unit, each as TN swizzled rows of 128 B
+    const uint64_t dims[3] = {64, static_cast<uint64_t>(r.M), static_cast<uint64_t>(r.K / 64)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(r.K) * esz, 64 * esz};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(p.TN), 2};
+    rc = make_tmap(&p.tmx, r.x, xdt, esz, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   if (rc != MT_OK) return rc;
   const int words = static_cast<int>(r.K * r.bits / 32);
   const int nsets = dual ? 2 : 3;
@@ -653,6 +766,12 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
     p.N[1] = p.N[0];
   }
   p.vec = vec ? 1 : 0;
+  {
+    bool sbv = (p.G % 8) == 0;
+    for (int s2 = 0; s2 < nsets; ++s2)
+      if (r.set[s2].N > 0 && (!aligned(r.set[s2].s, 16) || !aligned(r.set[s2].b, 16))) sbv = false;
+    p.sb_vec = sbv ? 1 : 0;
+  }
   p.tiles = ftiles * p.n_tt;
   p.units = static_cast<long long>(p.tiles) * p.nk;
   p.P = static_cast<int>(p.units < sms ? p.units : sms);
