@@ -53,6 +53,7 @@ constexpr int kTmemCols = 512;
 constexpr int kAccCols = 256;  // accumulator slots live in columns [0, 256)
 constexpr int kEpiWarp0 = 12;
 constexpr int kEpiBar = 2;     // named barrier of the epilogue warpgroup
+constexpr int kAllBar = 1;     // named barrier of all 512 threads
 constexpr int kSmemLimit = 232448;
 constexpr int kMaxP = 256;     // CTAs the workspace query provisions for
 
@@ -67,6 +68,8 @@ struct QmmTcParams {
   uint32_t* done;      // [tiles]: participants finished with a shared tile
   float* partials;     // [P][2][NACC][TNp][128]
   long long units;
+  uint64_t p_magic;      // ceil(2^64 / P), 0 when P == 1
+  uint64_t units_magic;  // ceil(2^64 / units), 0 when units == 1
   int N[3];
   int tile_start[4];   // prefix sums of feature tiles per set
   int M, K, G, group;
@@ -84,13 +87,22 @@ struct WLayout {
   }
 };
 
-__device__ __forceinline__ long long unit_begin(long long c, long long units, int P) { return c * units / P; }
+// floor(n / d) as a multiply-high by the host-computed magic ceil(2^64 / d)
+// (0 for d = 1); exact while n * d < 2^64, which the host checks.
+__device__ __forceinline__ long long div_magic(uint64_t n, uint64_t magic) {
+  return static_cast<long long>(magic ? __umul64hi(n, magic) : n);
+}
+
+// first unit of CTA c: floor(c * units / P)
+__device__ __forceinline__ long long unit_begin(const QmmTcParams& p, long long c) {
+  return div_magic(static_cast<uint64_t>(c) * static_cast<uint64_t>(p.units), p.p_magic);
+}
 
 // CTA whose unit range contains unit x
-__device__ __forceinline__ int owner_of(long long x, long long units, int P) {
-  int c = static_cast<int>((x * P) / units);
-  while (c + 1 < P && unit_begin(c + 1, units, P) <= x) ++c;
-  while (c > 0 && unit_begin(c, units, P) > x) --c;
+__device__ __forceinline__ int owner_of(const QmmTcParams& p, long long x) {
+  int c = static_cast<int>(div_magic(static_cast<uint64_t>(x) * static_cast<uint64_t>(p.P), p.units_magic));
+  while (c + 1 < p.P && unit_begin(p, c + 1) <= x) ++c;
+  while (c > 0 && unit_begin(p, c) > x) --c;
   return c;
 }
 
@@ -152,11 +164,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* shared_tile_slot = abort_flag + 1;  // [2]: tiles this CTA shares (first / last segment)
+  volatile int* last_seg = shared_tile_slot + 2;  // [5]: tile, shared, pslot, slot, parity of the last segment
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
-  const long long u0 = unit_begin(c, p.units, p.P);
-  const long long u1 = unit_begin(c + 1, p.units, p.P);
+  const long long u0 = unit_begin(p, c);
+  const long long u1 = unit_begin(p, c + 1);
   const int nunits = static_cast<int>(u1 - u0);
 
   if (threadIdx.x == 0) {
@@ -178,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     *abort_flag = 0;
     shared_tile_slot[0] = -1;
     shared_tile_slot[1] = -1;
+    last_seg[0] = -1;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -197,6 +211,92 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   // launch now hides their launch latency behind this kernel.
   griddep_launch();
 
+  // ---- accumulator segments: a segment is the part of one tile a CTA's
+  // range covers. seg_load reads the accumulator slot (rows of subpartition q,
+  // 32-token chunks from chunk0 in steps of cstep) and either writes the fp32
+  // partial to the workspace (a tile shared with other CTAs) or the finished
+  // values to the staging area; seg_publish then raises the partial's flag or
+  // writes the staged tile with coalesced stores (+ residual). Both are run by
+  // a group of gsize threads (gt = index in the group) with named barrier bar.
+  const T* res = static_cast<const T*>(p.residual);
+  auto seg_load = [&](int tile, bool shared, int pslot, int slot, int q, int ln, int chunk0, int cstep) {
+    const int r = q * 32 + ln;
+    const uint32_t acc_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + slot * NACC * TN;
+    (void)tile;
+    for (int c0 = chunk0; c0 < TN; c0 += cstep) {
+      const int w = (TN - c0) < 32 ? (TN - c0) : 32;
+      uint32_t v[NACC][32];
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+        if (w == 32) tmem_ld32(acc_base + a * TN + c0, v[a]);
+        else tmem_ld16(acc_base + a * TN + c0, v[a]);
+      }
+      tmem_wait_ld();
+      if (shared) {
+        // fp32 partial, layout [token][row]: for each token a warp writes 32
+        // consecutive rows, one 128-byte line per store instruction
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          float* dst = p.partials + ((static_cast<long long>(c) * 2 + pslot) * NACC + a) * p.TNp * kBM +
+                       static_cast<long long>(c0) * kBM + r;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < w) __stcg(dst + e * kBM, __uint_as_float(v[a][e]));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          if (e < w) {
+            float acc[NACC];
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) acc[a] = __uint_as_float(v[a][e]);
+            // the residual is added at the coalesced store
+            stage_out[(c0 + e) * kBM + r] = Elem<DT>::from_f(finish_value<DT, NACC>(acc, QMM_PLAIN, 0.f));
+          }
+        }
+      }
+    }
+  };
+  auto seg_publish = [&](int tile, bool shared, int pslot, int gt, int gsize, int bar) {
+    named_barrier(bar, gsize);
+    if (shared) {
+      if (gt == 0) {
+        __threadfence();
+        st_release_gpu(&p.flags[c * 2 + pslot], 1u);
+        shared_tile_slot[pslot] = tile;
+      }
+      return;
+    }
+    const TileInfo ti = tile_info(p, tile, DUAL);
+    T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
+    const int N = p.N[DUAL ? 0 : ti.set];
+    for (int idx = gt; idx < TN * 16; idx += gsize) {
+      const int tok = idx >> 4, cc = idx & 15;
+      const int token = ti.tok0 + tok, n = ti.n0 + cc * 8;
+      if (token >= p.M || n >= N) continue;
+      const T* src = stage_out + tok * kBM + cc * 8;
+      const long long off = static_cast<long long>(token) * N + n;
+      if (p.vec && n + 8 <= N) {
+        uint4 val = *reinterpret_cast<const uint4*>(src);
+        if (!DUAL && p.kind == QMM_RESIDUAL) {
+          const uint4 rv = *reinterpret_cast<const uint4*>(res + off);
+          T* ve = reinterpret_cast<T*>(&val);
+          const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ve[e] = Elem<DT>::from_f(Elem<DT>::to_f(ve[e]) + Elem<DT>::to_f(re[e]));
+        }
+        *reinterpret_cast<uint4*>(y + off) = val;
+      } else {
+        for (int e = 0; e < 8 && n + e < N; ++e) {
+          float vv = Elem<DT>::to_f(src[e]);
+          if (!DUAL && p.kind == QMM_RESIDUAL) vv = vv + Elem<DT>::to_f(res[off + e]);
+          y[off + e] = Elem<DT>::from_f(vv);
+        }
+      }
+    }
+    named_barrier(bar, gsize);
+  };
+
   if (warp == 0 || warp == 2 || (DUAL && warp == 3)) {
     // ------------------------------------------------------------ producers
     // One warp per stream (x; weight set 0; weight set 1 when dual): copies
@@ -207,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       const int a = warp == 3 ? 1 : 0;
       const int kw_per_stage = kBK * BITS / 32;  // words of K per unit
       const int pre = nunits < SS ? nunits : SS;
-      const int tile0 = static_cast<int>(u0 / nk);
+      const int tile0 = static_cast<int>(u0) / nk;
       int it_tile = tile0, it_k = static_cast<int>(u0 - static_cast<long long>(tile0) * nk);
       uint64_t* full = is_x ? x_full : w_full + a * kMaxSS;
       const int bytes = is_x ? x_stage_bytes : w_set_bytes;
@@ -252,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       bool ok = true;
       long long u = u0;
       while (u < u1 && ok) {
-        const int klo = static_cast<int>(u % nk);
+        const int klo = static_cast<int>(u) % nk;
         const int len = static_cast<int>(((nk - klo) < (u1 - u)) ? (nk - klo) : (u1 - u));
         if (!mbar_wait(&acc_empty[slot], (use[slot] & 1) ^ 1, abort_flag, 0x203)) break;
         tc_fence_after();
@@ -347,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       const int a = upb - (k & (upb - 1)), b = nk - k;
       return a < b ? a : b;
     };
-    int tile = static_cast<int>(u0 / nk), k = static_cast<int>(u0 - static_cast<long long>(tile) * nk);
+    int tile = static_cast<int>(u0) / nk, k = static_cast<int>(u0) - tile * nk;
     int next_start = nunits;  // unit index where the prefetched block takes over
     if (nunits > 0) {
       load_block(tile, k, sc_cur, bi_cur);
@@ -405,108 +505,61 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
+    // Every segment but the CTA's last: the last one is finished by all 16
+    // warps once the main loop is over.
     const int q = warp & 3;
-    const int r = q * 32 + lane;                // accumulator row = weight row in the tile
     const int et = threadIdx.x - kEpiWarp0 * 32;  // 0..127
-    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const T* res = static_cast<const T*>(p.residual);
     griddep_wait();
     int use[2] = {0, 0};
     int slot = 0;
     long long u = u0;
     while (u < u1) {
-      const int tile = static_cast<int>(u / nk);
-      const int klo = static_cast<int>(u % nk);
+      const int tile = static_cast<int>(u) / nk;
+      const int klo = static_cast<int>(u) % nk;
       const int len = static_cast<int>(((nk - klo) < (u1 - u)) ? (nk - klo) : (u1 - u));
       const bool shared = !(klo == 0 && len == nk);
       const int pslot = (u == u0) ? 0 : 1;
-      const TileInfo ti = tile_info(p, tile, DUAL);
+      if (u + len == u1) {
+        if (et == 0) {
+          last_seg[0] = tile;
+          last_seg[1] = shared ? 1 : 0;
+          last_seg[2] = pslot;
+          last_seg[3] = slot;
+          last_seg[4] = use[slot] & 1;
+        }
+        break;
+      }
       const bool got = mbar_wait(&acc_full[slot], use[slot] & 1, abort_flag, 0x401);
       if (named_barrier_or(kEpiBar, 128, !got || *abort_flag)) break;
       tc_fence_after();
-      const uint32_t acc_base = tmem + lane_base + slot * NACC * TN;
-      for (int c0 = 0; c0 < TN; c0 += 32) {
-        const int w = (TN - c0) < 32 ? (TN - c0) : 32;
-        uint32_t v[NACC][32];
-#pragma unroll
-        for (int a = 0; a < NACC; ++a) {
-          if (w == 32) tmem_ld32(acc_base + a * TN + c0, v[a]);
-          else tmem_ld16(acc_base + a * TN + c0, v[a]);
-        }
-        tmem_wait_ld();
-        if (shared) {
-          // fp32 partial, layout [token][row]: for each token a warp writes 32
-          // consecutive rows, one 128-byte line per store instruction
-#pragma unroll
-          for (int a = 0; a < NACC; ++a) {
-            float* dst = p.partials + ((static_cast<long long>(c) * 2 + pslot) * NACC + a) * p.TNp * kBM +
-                         static_cast<long long>(c0) * kBM + r;
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (e < w) __stcg(dst + e * kBM, __uint_as_float(v[a][e]));
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            if (e < w) {
-              float acc[NACC];
-#pragma unroll
-              for (int a = 0; a < NACC; ++a) acc[a] = __uint_as_float(v[a][e]);
-              // the residual is added at the coalesced store below
-              stage_out[(c0 + e) * kBM + r] = Elem<DT>::from_f(finish_value<DT, NACC>(acc, QMM_PLAIN, 0.f));
-            }
-          }
-        }
-      }
+      seg_load(tile, shared, pslot, slot, q, lane, 0, 32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[slot]);
       ++use[slot];
       slot = (slot + 1) % p.acc_slots;
-      if (shared) {
-        __threadfence();
-        named_barrier(kEpiBar, 128);
-        if (et == 0) {
-          st_release_gpu(&p.flags[c * 2 + pslot], 1u);
-          shared_tile_slot[pslot] = tile;
-        }
-      } else {
-        named_barrier(kEpiBar, 128);
-        T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
-        const int N = p.N[DUAL ? 0 : ti.set];
-        for (int idx = et; idx < TN * 16; idx += 128) {
-          const int tok = idx >> 4, cc = idx & 15;
-          const int token = ti.tok0 + tok, n = ti.n0 + cc * 8;
-          if (token >= p.M || n >= N) continue;
-          const T* src = stage_out + tok * kBM + cc * 8;
-          const long long off = static_cast<long long>(token) * N + n;
-          if (p.vec && n + 8 <= N) {
-            uint4 val = *reinterpret_cast<const uint4*>(src);
-            if (!DUAL && p.kind == QMM_RESIDUAL) {
-              const uint4 rv = *reinterpret_cast<const uint4*>(res + off);
-              T* ve = reinterpret_cast<T*>(&val);
-              const T* re = reinterpret_cast<const T*>(&rv);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) ve[e] = Elem<DT>::from_f(Elem<DT>::to_f(ve[e]) + Elem<DT>::to_f(re[e]));
-            }
-            *reinterpret_cast<uint4*>(y + off) = val;
-          } else {
-            for (int e = 0; e < 8 && n + e < N; ++e) {
-              float vv = Elem<DT>::to_f(src[e]);
-              if (!DUAL && p.kind == QMM_RESIDUAL) vv = vv + Elem<DT>::to_f(res[off + e]);
-              y[off + e] = Elem<DT>::from_f(vv);
-            }
-          }
-        }
-        named_barrier(kEpiBar, 128);
-      }
+      seg_publish(tile, shared, pslot, et, 128, kEpiBar);
       u += len;
     }
   }
 
-  // ---- every role is done with tensor memory: free it before the reductions,
-  // so a dependent kernel's CTA waiting on this SM can allocate
+  // ---- the CTA's last segment, by all 16 warps: warp w reads subpartition
+  // w % 4 and 32-token chunk w / 4 of the accumulator
   __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (last_seg[0] >= 0) {
+    const int slot = last_seg[3];
+    const bool got = mbar_wait(&acc_full[slot], static_cast<uint32_t>(last_seg[4]), abort_flag, 0x403);
+    if (!named_barrier_or(kAllBar, kThreads, !got || *abort_flag)) {
+      tc_fence_after();
+      seg_load(last_seg[0], last_seg[1] != 0, last_seg[2], slot, warp & 3, lane, (warp >> 2) * 32, 128);
+      seg_publish(last_seg[0], last_seg[1] != 0, last_seg[2], threadIdx.x, kThreads, kAllBar);
+    }
+  }
+
+  // ---- tensor memory is no longer read: free it before the reductions, so a
+  // dependent kernel's CTA waiting on this SM can allocate
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -515,20 +568,19 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   }
 
   // ---- reductions of the tiles this CTA shares with its neighbours, by all threads
-  const T* res = static_cast<const T*>(p.residual);
   for (int ps = 0; ps < 2; ++ps) {
     const int tile = shared_tile_slot[ps];
     if (tile < 0) continue;
     if (ps == 1 && tile == shared_tile_slot[0]) continue;
     const long long t_lo = static_cast<long long>(tile) * nk;
-    const int ca = owner_of(t_lo, p.units, p.P);
-    const int cb = owner_of(t_lo + nk - 1, p.units, p.P);
+    const int ca = owner_of(p, t_lo);
+    const int cb = owner_of(p, t_lo + nk - 1);
     const int S = cb - ca + 1;
     const int j = c - ca;
     // wait for every participant's partial: thread jj polls participant ca+jj
     for (int jj = threadIdx.x; jj < S; jj += kThreads) {
       const int cp = ca + jj;
-      const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+      const int sl = (unit_begin(p, cp) >= t_lo) ? 0 : 1;
       const uint32_t* f = &p.flags[cp * 2 + sl];
       if (ld_acquire_gpu(f) == 1u) continue;
       const uint64_t t0 = globaltimer_ns();
@@ -541,7 +593,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         }
       }
     }
-    __threadfence();
+    // the pollers' acquire loads and the barrier order every thread's reads
+    // of the partials after the writers' releases
     if (__syncthreads_or(*abort_flag)) break;
     // this participant reduces row groups [g_lo, g_hi) of 8 rows; a work item
     // is (token, 4 rows): one float4 per partial and accumulator. A thread
@@ -579,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         for (int d = 0; d < kPB; ++d) {
           const int cp = cpb + d;
           if (cp > cb) break;
-          const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+          const int sl = (unit_begin(p, cp) >= t_lo) ? 0 : 1;
           const float* src = p.partials + (static_cast<long long>(cp) * 2 + sl) * NACC * slot_elems;
 #pragma unroll
           for (int jj = 0; jj < kJ; ++jj)
@@ -643,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       if (prev == static_cast<uint32_t>(S - 1)) {
         // every participant has read every partial of this tile: clear for the next call
         for (int cp = ca; cp <= cb; ++cp) {
-          const int sl = (unit_begin(cp, p.units, p.P) >= t_lo) ? 0 : 1;
+          const int sl = (unit_begin(p, cp) >= t_lo) ? 0 : 1;
           p.flags[cp * 2 + sl] = 0u;
         }
         p.done[tile] = 0u;
@@ -776,6 +829,12 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
   p.units = static_cast<long long>(p.tiles) * p.nk;
   p.P = static_cast<int>(p.units < sms ? p.units : sms);
   if (p.P > kMaxP) p.P = kMaxP;
+  if (p.units >= (1ll << 28)) {
+    set_error("qmm: %lld K-stage units exceed the 2^28 the unit arithmetic supports", p.units);
+    return MT_ERR_UNSUPPORTED;
+  }
+  p.p_magic = p.P > 1 ? ~0ull / static_cast<uint64_t>(p.P) + 1 : 0;
+  p.units_magic = p.units > 1 ? ~0ull / static_cast<uint64_t>(p.units) + 1 : 0;
   if (static_cast<size_t>(p.tiles) > kWsQmmMaxTiles) {
     set_error("qmm: %d tiles exceed the workspace's %zu tile counters (M=%lld too large for one call)", p.tiles,
               kWsQmmMaxTiles, (long long)r.M);
