@@ -118,12 +118,17 @@ template <> struct Elem<MT_BF16> {
   using T2 = __nv_bfloat162;
   static __device__ __forceinline__ float to_f(T v) { return __bfloat162float(v); }
   static __device__ __forceinline__ T from_f(float v) { return __float2bfloat16_rn(v); }
+  // two values rounded with one packed conversion
+  static __device__ __forceinline__ T2 pack2(float a, float b) { return __floats2bfloat162_rn(a, b); }
+  static __device__ __forceinline__ float2 unpack2(T2 v) { return __bfloat1622float2(v); }
 };
 template <> struct Elem<MT_F16> {
   using T = __half;
   using T2 = __half2;
   static __device__ __forceinline__ float to_f(T v) { return __half2float(v); }
   static __device__ __forceinline__ T from_f(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ T2 pack2(float a, float b) { return __floats2half2_rn(a, b); }
+  static __device__ __forceinline__ float2 unpack2(T2 v) { return __half22float2(v); }
 };
 template <> struct Elem<MT_F32> {
   using T = float;
@@ -137,6 +142,12 @@ template <> struct Elem<MT_F32> {
 template <int DT>
 __device__ __forceinline__ float round_to(float v) {
   return Elem<DT>::to_f(Elem<DT>::from_f(v));
+}
+
+// round_to of two values with one packed conversion
+template <int DT>
+__device__ __forceinline__ float2 round2_to(float a, float b) {
+  return Elem<DT>::unpack2(Elem<DT>::pack2(a, b));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -238,6 +249,24 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_addr(dst)),
       "l"(map), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completing `bytes` on the mbarrier.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Order this thread's earlier generic-proxy accesses (and those it has
+// acquired) before its later async-proxy (TMA) accesses of global / shared memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");

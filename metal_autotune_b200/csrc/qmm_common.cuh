@@ -161,4 +161,18 @@ __device__ __forceinline__ float swiglu_rounded(float g, float u) {
   return a * u;
 }
 
+// swiglu_rounded for two values, the sigmoid from the hardware exponential
+// and reciprocal approximations (a few fp32 ulps; the bf16 / f16 roundings that
+// follow hide the difference except near rounding boundaries, where the result
+// moves by one ulp of the element type) and each rounding done for both values
+// with one packed conversion. g and u are the raw fp32 accumulators.
+template <int DT>
+__device__ __forceinline__ typename Elem<DT>::T2 swiglu2_fast(float g0, float g1, float u0, float u1) {
+  const float2 g = round2_to<DT>(g0, g1);
+  const float2 u = round2_to<DT>(u0, u1);
+  const float2 sg = round2_to<DT>(__fdividef(1.0f, 1.0f + __expf(-g.x)), __fdividef(1.0f, 1.0f + __expf(-g.y)));
+  const float2 a = round2_to<DT>(g.x * sg.x, g.y * sg.y);
+  return Elem<DT>::pack2(a.x * u.x, a.y * u.y);
+}
+
 }  // namespace mt

@@ -66,7 +66,7 @@ struct QmmTcParams {
   const void* residual;
   uint32_t* flags;     // [P][2]: partial of slot published
   uint32_t* done;      // [tiles]: participants finished with a shared tile
-  float* partials;     // [P][2][NACC][TNp][128]
+  float* partials;     // [P][2][NACC][16 groups][TNp][8 rows]
   long long units;
   uint64_t p_magic;      // ceil(2^64 / P), 0 when P == 1
   uint64_t units_magic;  // ceil(2^64 / units), 0 when units == 1
@@ -124,12 +124,12 @@ __device__ __forceinline__ TileInfo tile_info(const QmmTcParams& p, int tile, bo
   return ti;
 }
 
+// Finished values of two outputs from their fp32 accumulators (gate and up
+// for SwiGLU): the element-type result, residual not included.
 template <int DT, int NACC>
-__device__ __forceinline__ float finish_value(const float (&acc)[NACC], int kind, float res) {
-  if (NACC == 2) return swiglu_rounded<DT>(round_to<DT>(acc[0]), round_to<DT>(acc[NACC - 1]));
-  float v = round_to<DT>(acc[0]);
-  if (kind == QMM_RESIDUAL) v = v + res;
-  return v;
+__device__ __forceinline__ typename Elem<DT>::T2 finish2(float a0, float a1, float b0, float b1) {
+  if constexpr (NACC == 2) return swiglu2_fast<DT>(a0, a1, b0, b1);
+  else return Elem<DT>::pack2(a0, a1);
 }
 
 // Bytes of the output staging area: TN x 128 finished 16-bit values.
@@ -161,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   uint64_t* acc_full = a_empty + 4;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* red_bar = drain + 1;  // partial slices landed (reduction)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* shared_tile_slot = abort_flag + 1;  // [2]: tiles this CTA shares (first / last segment)
   volatile int* last_seg = shared_tile_slot + 2;  // [5]: tile, shared, pslot, slot, parity of the last segment
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       mbar_init(&acc_empty[i], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(red_bar, 1);
     *abort_flag = 0;
     shared_tile_slot[0] = -1;
     shared_tile_slot[1] = -1;
@@ -233,25 +235,27 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       }
       tmem_wait_ld();
       if (shared) {
-        // fp32 partial, layout [token][row]: for each token a warp writes 32
-        // consecutive rows, one 128-byte line per store instruction
+        // fp32 partial, layout [8-row group][token][8 rows], so that a row
+        // range of all tokens is contiguous; for each token a warp's store
+        // covers four full 32-byte sectors
 #pragma unroll
         for (int a = 0; a < NACC; ++a) {
           float* dst = p.partials + ((static_cast<long long>(c) * 2 + pslot) * NACC + a) * p.TNp * kBM +
-                       static_cast<long long>(c0) * kBM + r;
+                       (r >> 3) * (p.TNp * 8) + c0 * 8 + (r & 7);
 #pragma unroll
           for (int e = 0; e < 32; ++e)
-            if (e < w) __stcg(dst + e * kBM, __uint_as_float(v[a][e]));
+            if (e < w) __stcg(dst + e * 8, __uint_as_float(v[a][e]));
         }
       } else {
+        // the residual is added at the coalesced store
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < 32; e += 2) {
           if (e < w) {
-            float acc[NACC];
-#pragma unroll
-            for (int a = 0; a < NACC; ++a) acc[a] = __uint_as_float(v[a][e]);
-            // the residual is added at the coalesced store
-            stage_out[(c0 + e) * kBM + r] = Elem<DT>::from_f(finish_value<DT, NACC>(acc, QMM_PLAIN, 0.f));
+            const typename Elem<DT>::T2 o =
+                finish2<DT, NACC>(__uint_as_float(v[0][e]), __uint_as_float(v[0][e + 1]),
+                                  __uint_as_float(v[NACC - 1][e]), __uint_as_float(v[NACC - 1][e + 1]));
+            stage_out[(c0 + e) * kBM + r] = o.x;
+            stage_out[(c0 + e + 1) * kBM + r] = o.y;
           }
         }
       }
@@ -567,7 +571,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     tmem_dealloc(tmem, kTmemCols);
   }
 
-  // ---- reductions of the tiles this CTA shares with its neighbours, by all threads
+  // ---- reductions of the tiles this CTA shares with its neighbours, by all
+  // threads. Participant j of a tile's S participants reduces row groups
+  // [16j/S, 16(j+1)/S) of 8 rows. The participants' slices of those groups
+  // (contiguous in the partial layout) are brought into the idle pipeline
+  // buffers with bulk copies (one per participant and accumulator; chunks of
+  // participants when they do not all fit), summed in participant (= K) order
+  // from shared memory, finished into a padded staging tile and written with
+  // coalesced stores.
+  const int area = SS * (x_stage_bytes + w_stage_bytes);
+  constexpr int kStgPitch = kBM + 8;  // staging row in elements: 272 B, 2-way conflicts at most
+  T* stg = reinterpret_cast<T*>(smem + area - TN * kStgPitch * static_cast<int>(sizeof(T)));
+  const int slice_bytes = TN * 32;    // one 8-row group of one partial, all tokens
+  const int max_slices = (area - TN * kStgPitch * static_cast<int>(sizeof(T))) / slice_bytes;
+  uint32_t red_phase = 0;
   for (int ps = 0; ps < 2; ++ps) {
     const int tile = shared_tile_slot[ps];
     if (tile < 0) continue;
@@ -596,102 +613,111 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     // the pollers' acquire loads and the barrier order every thread's reads
     // of the partials after the writers' releases
     if (__syncthreads_or(*abort_flag)) break;
-    // this participant reduces row groups [g_lo, g_hi) of 8 rows; a work item
-    // is (token, 4 rows): one float4 per partial and accumulator. A thread
-    // takes kJ items per pass and loads kPB partials of all of them at once,
-    // so 8 float4 loads are in flight per thread.
     const int g_lo = (j * 16) / S, g_hi = ((j + 1) * 16) / S;
-    const int quads = (g_hi - g_lo) * 2;
-    const int items = TN * quads;
-    const TileInfo ti = tile_info(p, tile, DUAL);
-    T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
-    const int N = p.N[DUAL ? 0 : ti.set];
-    const long long slot_elems = static_cast<long long>(p.TNp) * kBM;
-    constexpr int kJ = 2;
-    constexpr int kPB = 4 / NACC;
-    for (int base = 0; base < items; base += kThreads * kJ) {
-      int poff[kJ];  // element offset inside a partial slot, or -1
-      int tokv[kJ], nv[kJ];
+    const int ng = g_hi - g_lo;
+    const int per_part = NACC * ng;  // slices per participant
+    const int pc_max = ng > 0 ? max_slices / per_part : S;
+    const int nit = ng * TN * 2;     // items: (group, token, 4-row half)
+    constexpr int kMaxIt = 4;        // ng <= 8, TN <= 128: at most 4 items per thread
+    float acc[kMaxIt][NACC][4];
 #pragma unroll
-      for (int jj = 0; jj < kJ; ++jj) {
-        const int idx = base + jj * kThreads + threadIdx.x;
-        const int tok = idx / quads, rq = g_lo * 8 + (idx - tok * quads) * 4;
-        tokv[jj] = ti.tok0 + tok;
-        nv[jj] = ti.n0 + rq;
-        poff[jj] = (idx < items && tokv[jj] < p.M && nv[jj] < N) ? tok * kBM + rq : -1;
-      }
-      float acc[kJ][NACC][4];
+    for (int jj = 0; jj < kMaxIt; ++jj)
 #pragma unroll
-      for (int jj = 0; jj < kJ; ++jj)
-#pragma unroll
-        for (int a = 0; a < NACC; ++a) acc[jj][a][0] = acc[jj][a][1] = acc[jj][a][2] = acc[jj][a][3] = 0.f;
-      // partials summed in participant (= K) order
-      for (int cpb = ca; cpb <= cb; cpb += kPB) {
-        float4 xv[kPB][kJ][NACC];
-#pragma unroll
-        for (int d = 0; d < kPB; ++d) {
-          const int cp = cpb + d;
-          if (cp > cb) break;
-          const int sl = (unit_begin(p, cp) >= t_lo) ? 0 : 1;
-          const float* src = p.partials + (static_cast<long long>(cp) * 2 + sl) * NACC * slot_elems;
-#pragma unroll
-          for (int jj = 0; jj < kJ; ++jj)
-            if (poff[jj] >= 0) {
-#pragma unroll
-              for (int a = 0; a < NACC; ++a)
-                xv[d][jj][a] = __ldcg(reinterpret_cast<const float4*>(src + a * slot_elems + poff[jj]));
-            }
-        }
-#pragma unroll
-        for (int d = 0; d < kPB; ++d) {
-          if (cpb + d > cb) break;
-#pragma unroll
-          for (int jj = 0; jj < kJ; ++jj)
-            if (poff[jj] >= 0) {
-#pragma unroll
-              for (int a = 0; a < NACC; ++a) {
-                acc[jj][a][0] += xv[d][jj][a].x;
-                acc[jj][a][1] += xv[d][jj][a].y;
-                acc[jj][a][2] += xv[d][jj][a].z;
-                acc[jj][a][3] += xv[d][jj][a].w;
-              }
-            }
-        }
-      }
-#pragma unroll
-      for (int jj = 0; jj < kJ; ++jj) {
-        if (poff[jj] < 0) continue;
-        const int n = nv[jj];
-        const long long off = static_cast<long long>(tokv[jj]) * N + n;
-        const bool full4 = p.vec && n + 4 <= N;
-        T resv[4];
-        if (!DUAL && p.kind == QMM_RESIDUAL) {
-          if (full4) {
-            *reinterpret_cast<uint2*>(resv) = *reinterpret_cast<const uint2*>(res + off);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) resv[e] = (n + e < N) ? res[off + e] : Elem<DT>::from_f(0.f);
+      for (int a = 0; a < NACC; ++a) acc[jj][a][0] = acc[jj][a][1] = acc[jj][a][2] = acc[jj][a][3] = 0.f;
+    bool ok = true;
+    for (int pc0 = 0; ng > 0 && pc0 < S; pc0 += pc_max) {
+      const int npc = (S - pc0) < pc_max ? (S - pc0) : pc_max;
+      if (threadIdx.x == 0)
+        mbar_arrive_expect_tx(red_bar, static_cast<uint32_t>(npc * per_part * slice_bytes));
+      __syncthreads();  // expect_tx registered; the previous chunk's reads are done
+      if (lane == 0) {
+        // copies spread over the 16 warps so that they are in flight together
+        for (int i = warp; i < npc * NACC; i += kThreads / 32) {
+          if (i == warp) {
+            fence_proxy_async_global();
+            fence_proxy_async_shared();
           }
+          const int pi = i / NACC, a = i - pi * NACC;
+          const int cp = ca + pc0 + pi;
+          const int sl = (unit_begin(p, cp) >= t_lo) ? 0 : 1;
+          const float* src = p.partials + ((static_cast<long long>(cp) * 2 + sl) * NACC + a) * p.TNp * kBM +
+                             g_lo * (p.TNp * 8);
+          bulk_load(smem + (pi * per_part + a * ng) * slice_bytes, src, ng * slice_bytes, red_bar);
         }
-        T outv[4];
+      }
+      const bool got = mbar_wait(red_bar, red_phase & 1, abort_flag, 0x404);
+      ++red_phase;
+      if (__syncthreads_or(!got || *abort_flag)) {
+        if (threadIdx.x == 0) mbar_wait_drain(red_bar, (red_phase - 1) & 1, 200000000ull);
+        ok = false;
+        break;
+      }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float av[NACC];
+      for (int jj = 0; jj < kMaxIt; ++jj) {
+        const int it = threadIdx.x + jj * kThreads;
+        if (it >= nit) break;
+        const int h = it & 1, tg = it >> 1;
+        const int gg = tg / TN, tok = tg - gg * TN;
+        const uint8_t* base = smem + (gg * TN + tok) * 32 + h * 16;
+        for (int pi = 0; pi < npc; ++pi) {
 #pragma unroll
-          for (int a = 0; a < NACC; ++a) av[a] = acc[jj][a][e];
-          const float rv = (!DUAL && p.kind == QMM_RESIDUAL) ? Elem<DT>::to_f(resv[e]) : 0.f;
-          outv[e] = Elem<DT>::from_f(finish_value<DT, NACC>(av, DUAL ? QMM_PLAIN : p.kind, rv));
-        }
-        if (full4) {
-          *reinterpret_cast<uint2*>(y + off) = *reinterpret_cast<const uint2*>(outv);
-        } else {
-          for (int e = 0; e < 4 && n + e < N; ++e) y[off + e] = outv[e];
+          for (int a = 0; a < NACC; ++a) {
+            const float4 v = *reinterpret_cast<const float4*>(base + (pi * per_part + a * ng) * slice_bytes);
+            acc[jj][a][0] += v.x;
+            acc[jj][a][1] += v.y;
+            acc[jj][a][2] += v.z;
+            acc[jj][a][3] += v.w;
+          }
         }
       }
     }
+    if (!ok) break;
+    // finish into the staging tile (the residual is added at the store)
+#pragma unroll
+    for (int jj = 0; jj < kMaxIt; ++jj) {
+      const int it = threadIdx.x + jj * kThreads;
+      if (it >= nit) break;
+      const int h = it & 1, tg = it >> 1;
+      const int gg = tg / TN, tok = tg - gg * TN;
+      typename Elem<DT>::T2 o[2];
+#pragma unroll
+      for (int e = 0; e < 4; e += 2)
+        o[e / 2] = finish2<DT, NACC>(acc[jj][0][e], acc[jj][0][e + 1], acc[jj][NACC - 1][e], acc[jj][NACC - 1][e + 1]);
+      *reinterpret_cast<uint2*>(stg + tok * kStgPitch + (g_lo + gg) * 8 + h * 4) =
+          *reinterpret_cast<const uint2*>(o);
+    }
     __syncthreads();
+    {
+      const TileInfo ti = tile_info(p, tile, DUAL);
+      T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
+      const int N = p.N[DUAL ? 0 : ti.set];
+      for (int idx = threadIdx.x; idx < TN * ng; idx += kThreads) {
+        const int tok = idx / ng, k8 = idx - tok * ng;
+        const int token = ti.tok0 + tok, n = ti.n0 + (g_lo + k8) * 8;
+        if (token >= p.M || n >= N) continue;
+        const T* src = stg + tok * kStgPitch + (g_lo + k8) * 8;
+        const long long off = static_cast<long long>(token) * N + n;
+        if (p.vec && n + 8 <= N) {
+          uint4 val = *reinterpret_cast<const uint4*>(src);
+          if (!DUAL && p.kind == QMM_RESIDUAL) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(res + off);
+            T* ve = reinterpret_cast<T*>(&val);
+            const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ve[e] = Elem<DT>::from_f(Elem<DT>::to_f(ve[e]) + Elem<DT>::to_f(re[e]));
+          }
+          *reinterpret_cast<uint4*>(y + off) = val;
+        } else {
+          for (int e = 0; e < 8 && n + e < N; ++e) {
+            float vv = Elem<DT>::to_f(src[e]);
+            if (!DUAL && p.kind == QMM_RESIDUAL) vv = vv + Elem<DT>::to_f(res[off + e]);
+            y[off + e] = Elem<DT>::from_f(vv);
+          }
+        }
+      }
+    }
+    __syncthreads();  // staging and slices are reused by the next tile
     if (threadIdx.x == 0) {
-      __threadfence();
       const uint32_t prev = atomicAdd(&p.done[tile], 1u);
       if (prev == static_cast<uint32_t>(S - 1)) {
         // every participant has read every partial of this tile: clear for the next call
@@ -850,6 +876,17 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
   p.flags = reinterpret_cast<uint32_t*>(ws + wl.flags);
   p.done = reinterpret_cast<uint32_t*>(ws + wl.done);
   p.partials = reinterpret_cast<float*>(ws + wl.partials);
+  {
+    // the reduction's largest chunk (one participant's slices: 8 groups per
+    // accumulator) and the padded staging tile must fit the pipeline buffers
+    const size_t area = static_cast<size_t>(p.SS) *
+                        (static_cast<size_t>(p.TN) * 256 + (dual ? 2 : 1) * kBM * (kBK * r.bits / 8));
+    const size_t need = static_cast<size_t>(dual ? 2 : 1) * 8 * p.TN * 32 + static_cast<size_t>(p.TN) * (kBM + 8) * 2;
+    if (area < need) {
+      set_error("qmm: pipeline buffers (%zu B) smaller than the reduction needs (%zu B)", area, need);
+      return MT_ERR_UNSUPPORTED;
+    }
+  }
 
   const size_t smem = smem_bytes_for(p.TN, p.SS, r.bits, dual);
   const bool bf = r.dtype == MT_BF16;
