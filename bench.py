@@ -458,6 +458,9 @@ def main():
     ap.add_argument("--mode", default="request", choices=["request", "kernels"])
     ap.add_argument("--only", default="", help="kernels mode: comma-separated kernel names")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launch-list", action="store_true",
+                    help="replay the request W + K times, the K inside an NVTX range 'request', and exit "
+                         "(for ncu --nvtx --nvtx-include request/)")
     args = ap.parse_args()
     if args.warmup < 3 and args.mode == "request":
         args.warmup = 3
@@ -481,6 +484,14 @@ def main():
     for _ in range(args.warmup):
         req.replay()
     torch.cuda.synchronize()
+    if args.launch_list:
+        torch.cuda.nvtx.range_push("request")
+        for _ in range(args.steps):
+            req.replay()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        log(f"launch list: {args.steps} request(s) of {req.launches_per_step} launches")
+        return 0
     with ClockSampler(local) as clk:
         ms_total = time_region(req.replay, args.steps, world)
         ms_e2e_total = time_region(req.e2e_step, args.steps, world)
