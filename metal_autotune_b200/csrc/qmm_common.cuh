@@ -27,6 +27,8 @@ struct QmmRequest {
 };
 
 int qmv_run(const QmmRequest& r, cudaStream_t stream);
+bool qmv_stream_eligible(const QmmRequest& r);
+int qmv_stream_run(const QmmRequest& r, cudaStream_t stream);
 int qmm_tc_run(const QmmRequest& r, cudaStream_t stream);
 size_t qmm_tc_workspace(int64_t M, int64_t n_total, int64_t K, int bits, int kind);
 

@@ -277,6 +277,8 @@ static int qmv_dispatch(QmvParams& p, int bits, int dtype, int total_rows, cudaS
 }
 
 int qmv_run(const QmmRequest& r, cudaStream_t stream) {
+  // 4-bit decode shapes whose rows fit the streamed kernel's shared memory
+  if (qmv_stream_eligible(r)) return qmv_stream_run(r, stream);
   QmvParams p = {};
   p.x = r.x;
   p.residual = r.residual;

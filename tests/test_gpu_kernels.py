@@ -57,6 +57,11 @@ QMM_CASES = [
     (64, 256, 1024, 64, 8, "bfloat16"),
     (96, 256, 1024, 64, 4, "float16"),
     (512, 256, 512, 64, 4, "bfloat16"),
+    # decode shapes of Qwen3-4B (streamed qmv): down, o_proj, a wide projection, 2 rows of x
+    (1, 2560, 9728, 64, 4, "bfloat16"),
+    (1, 2560, 4096, 64, 4, "bfloat16"),
+    (1, 20000, 2560, 64, 4, "bfloat16"),
+    (2, 1536, 2560, 64, 4, "float16"),
 ]
 
 
