@@ -1,5 +1,7 @@
 // Elementwise and gather regions: SwiGLU, the quantized embedding gather and
 // the greedy pick from the last row of logits.
+#include <cooperative_groups.h>
+
 #include "mt_common.cuh"
 #include "qmm_common.cuh"
 
@@ -54,101 +56,127 @@ __global__ void __launch_bounds__(256) qembed_kernel(const int32_t* __restrict__
 // Single CTA of 1024 threads: pass 1 logsumexp (per-thread online max/sum,
 // fixed-order tree), pass 2 argmax of round(x - round(lse)) with the lowest
 // index on ties, as mlx-lm's `logits - logsumexp(logits)` then argmax.
+// Greedy pick over one row of logits (autotuner_runtime/inference.py:140-147,
+// mlx-lm generate_step): lse = log(sum exp(x - max)) + max in fp32,
+// logprobs = round(x - round(lse)), token = first argmax of the logprobs.
+// One cluster of 8 CTAs x 1024 threads, CTA r owning the contiguous chunk
+// [r*n/8, (r+1)*n/8): three passes over the chunk (max, sum of exp, argmax of
+// the rounded log-probabilities), the CTAs' partial results exchanged through
+// distributed shared memory and combined in rank order, so every CTA forms
+// the same max and lse and the result does not depend on timing.
+constexpr int kLpCtas = 8;
+constexpr int kLpThreads = 1024;
+
 template <int DT>
-__global__ void __launch_bounds__(1024) logits_pick_kernel(const void* __restrict__ lp, int64_t n,
-                                                           int32_t* __restrict__ token, float* __restrict__ logprob,
-                                                           float* __restrict__ lse_out) {
+__global__ void __cluster_dims__(kLpCtas, 1, 1) __launch_bounds__(kLpThreads)
+    logits_pick_kernel(const void* __restrict__ lp, int64_t n, int32_t* __restrict__ token,
+                       float* __restrict__ logprob, float* __restrict__ lse_out) {
+  namespace cg = cooperative_groups;
   using T = typename Elem<DT>::T;
-  __shared__ float sm_m[32], sm_s[32];
+  __shared__ float sm_f[32];
   __shared__ int64_t sm_i[32];
-  __shared__ float sh_lse;
+  __shared__ float pub_m, pub_s, pub_best;  // this CTA's partials, read by the cluster
+  __shared__ int64_t pub_bi;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t lo = n * rank / kLpCtas, hi = n * (rank + 1) / kLpCtas;
   griddep_wait();
   const T* x = static_cast<const T*>(lp);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float m = -INFINITY, s = 0.f;
-  for (int64_t i = tid; i < n; i += 1024) {
-    const float v = Elem<DT>::to_f(x[i]);
-    if (v > m) {
-      s = s * expf(m - v) + 1.f;
-      m = v;
-    } else if (v == -INFINITY && m == -INFINITY) {
-      // exp(-inf - -inf) is undefined; an all -inf prefix contributes nothing
-    } else {
-      s += expf(v - m);
-    }
-  }
-  // combine (m, s) pairs in a fixed tree
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    const float mn = fmaxf(m, m2);
-    s = (mn == -INFINITY) ? 0.f : s * expf(m - mn) + s2 * expf(m2 - mn);
-    m = mn;
-  }
-  if (lane == 0) {
-    sm_m[warp] = m;
-    sm_s[warp] = s;
-  }
+
+  // pass 1: max
+  float m = -INFINITY;
+  for (int64_t i = lo + tid; i < hi; i += kLpThreads) m = fmaxf(m, Elem<DT>::to_f(x[i]));
+  m = warp_max(m);
+  if (lane == 0) sm_f[warp] = m;
   __syncthreads();
   if (warp == 0) {
-    m = sm_m[lane];
-    s = sm_s[lane];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      const float mn = fmaxf(m, m2);
-      s = (mn == -INFINITY) ? 0.f : s * expf(m - mn) + s2 * expf(m2 - mn);
-      m = mn;
-    }
-    if (lane == 0) sh_lse = m + logf(s);
+    m = warp_max(sm_f[lane]);
+    if (lane == 0) pub_m = m;
   }
+  cluster.sync();
+  float gmax = -INFINITY;
+  for (int r = 0; r < kLpCtas; ++r) gmax = fmaxf(gmax, *cluster.map_shared_rank(&pub_m, r));
+
+  // pass 2: sum of exp(x - max)
+  float s = 0.f;
+  if (gmax != -INFINITY)
+    for (int64_t i = lo + tid; i < hi; i += kLpThreads) s += expf(Elem<DT>::to_f(x[i]) - gmax);
+  s = warp_sum(s);
   __syncthreads();
-  const float lse = sh_lse;
+  if (lane == 0) sm_f[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    s = warp_sum(sm_f[lane]);
+    if (lane == 0) pub_s = s;
+  }
+  cluster.sync();
+  float gsum = 0.f;
+  for (int r = 0; r < kLpCtas; ++r) gsum += *cluster.map_shared_rank(&pub_s, r);
+  const float lse = logf(gsum) + gmax;
   const float lse_r = round_to<DT>(lse);
+
+  // pass 3: first argmax of the rounded log-probabilities
   float best = -INFINITY;
   int64_t bi = -1;
-  for (int64_t i = tid; i < n; i += 1024) {
+  for (int64_t i = lo + tid; i < hi; i += kLpThreads) {
     const float v = round_to<DT>(__fsub_rn(Elem<DT>::to_f(x[i]), lse_r));
-    if (v > best || bi < 0) {
+    if (bi < 0 || v > best) {
       best = v;
       bi = i;
     }
   }
+  auto better = [](float b2, int64_t i2, float b, int64_t i) {
+    return i2 >= 0 && (i < 0 || b2 > b || (b2 == b && i2 < i));
+  };
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
     const int64_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (i2 >= 0 && (b2 > best || (b2 == best && (i2 < bi || bi < 0)) || bi < 0)) {
+    if (better(b2, i2, best, bi)) {
       best = b2;
       bi = i2;
     }
   }
-  __syncthreads();
   if (lane == 0) {
-    sm_m[warp] = best;
+    sm_f[warp] = best;
     sm_i[warp] = bi;
   }
   __syncthreads();
   if (warp == 0) {
-    best = sm_m[lane];
+    best = sm_f[lane];
     bi = sm_i[lane];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
       const int64_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (i2 >= 0 && (b2 > best || (b2 == best && (i2 < bi || bi < 0)) || bi < 0)) {
+      if (better(b2, i2, best, bi)) {
         best = b2;
         bi = i2;
       }
     }
     if (lane == 0) {
-      *token = static_cast<int32_t>(bi);
-      *logprob = best;
-      if (lse_out) *lse_out = lse;
+      pub_best = best;
+      pub_bi = bi;
     }
   }
+  cluster.sync();
+  if (rank == 0 && tid == 0) {
+    float b = -INFINITY;
+    int64_t ib = -1;
+    for (int r = 0; r < kLpCtas; ++r) {
+      const float b2 = *cluster.map_shared_rank(&pub_best, r);
+      const int64_t i2 = *cluster.map_shared_rank(&pub_bi, r);
+      if (better(b2, i2, b, ib)) {
+        b = b2;
+        ib = i2;
+      }
+    }
+    *token = static_cast<int32_t>(ib);
+    *logprob = b;
+    if (lse_out) *lse_out = lse;
+  }
+  cluster.sync();  // the other CTAs' shared memory stays alive until rank 0 has read it
   griddep_launch();
 }
 
@@ -205,13 +233,13 @@ int mt_logits_pick(const void* logits, int64_t n, int dtype, int32_t* token, flo
   MT_CHECK_ARG(n > 0, "mt_logits_pick: empty row");
   switch (dtype) {
     case MT_BF16:
-      return launch(logits_pick_kernel<MT_BF16>, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, n, token,
+      return launch(logits_pick_kernel<MT_BF16>, dim3(kLpCtas), dim3(kLpThreads), 0, (cudaStream_t)stream, logits, n, token,
                     logprob, lse);
     case MT_F16:
-      return launch(logits_pick_kernel<MT_F16>, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, n, token,
+      return launch(logits_pick_kernel<MT_F16>, dim3(kLpCtas), dim3(kLpThreads), 0, (cudaStream_t)stream, logits, n, token,
                     logprob, lse);
     case MT_F32:
-      return launch(logits_pick_kernel<MT_F32>, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, n, token,
+      return launch(logits_pick_kernel<MT_F32>, dim3(kLpCtas), dim3(kLpThreads), 0, (cudaStream_t)stream, logits, n, token,
                     logprob, lse);
     default: set_error("mt_logits_pick: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
   }

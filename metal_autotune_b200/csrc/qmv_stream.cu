@@ -6,7 +6,10 @@
 // contiguous row range [c*R/P, (c+1)*R/P) of the output; the packed rows of
 // that range are one contiguous byte stream (rows of the same set are
 // adjacent in the MLX layout), which a producer warp copies into a ring of
-// 16 KB shared-memory stages with bulk copies. Weights and scales never depend
+// 16 KB shared-memory stages with bulk copies. The CTA's scales and biases
+// are copied once up front; when they do not fit (row ranges of an lm_head),
+// each stage receives those of the rows it touches instead. Weights and
+// scales never depend
 // on the previous kernel, so the producer starts before the grid dependency
 // resolves: with programmatic dependent launch the first stages are in flight
 // while the predecessor is still finishing. The 16 consumer warps stage x as
@@ -53,19 +56,26 @@ struct QsParams {
   int rows;          // rows of the output space (plain: all sets; residual / SwiGLU: set 0)
   int P;             // CTAs
   int NST;           // stages in the ring
-  int max_rows;      // stream rows of one CTA, upper bound (shared-memory layout)
+  int max_rows;      // stream rows of one CTA, upper bound (SwiGLU row sums)
+  int spr;           // rows a stage can touch: 16 KB / row bytes + 2
+  int stage_sc;      // 1: scales and biases travel with each stage; 0: copied once up front
 };
 
 // Byte offsets of the shared-memory regions (host and device agree on them).
+// A stage slot: 16 KB of the weight stream, then (stage_sc) the scales and
+// biases ([spr][G] each) of the rows those bytes belong to; without stage_sc
+// the CTA's scales and biases ([max_rows][G] each) follow the ring.
 struct QsLayout {
-  int sbs, sbb, xs, xsum, gsum, bars, total;
+  int slot, sc, sbs, sbb, xs, xsum, gsum, bars, total;
 };
 
-__host__ __device__ inline QsLayout qs_layout(int K, int G, int max_rows, int MR, int NST) {
+__host__ __device__ inline QsLayout qs_layout(int K, int G, int max_rows, int spr, int MR, int NST, int stage_sc) {
   QsLayout l;
-  l.sbs = NST * kQsStageBytes;
-  l.sbb = l.sbs + max_rows * G * 2;        // G*2 is a multiple of 16
-  l.xs = l.sbb + max_rows * G * 2;
+  l.sc = kQsStageBytes;  // G*2 is a multiple of 16
+  l.slot = stage_sc ? (kQsStageBytes + 2 * spr * G * 2 + 127) & ~127 : kQsStageBytes;
+  l.sbs = NST * l.slot;
+  l.sbb = l.sbs + (stage_sc ? 0 : max_rows * G * 2);
+  l.xs = l.sbb + (stage_sc ? 0 : max_rows * G * 2);
   l.xsum = l.xs + MR * K * 2;
   l.gsum = l.xsum + MR * (K / 32) * 4;
   l.bars = (l.gsum + max_rows * MR * 4 + 15) & ~15;
@@ -110,7 +120,7 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   const int K = p.K, G = p.G, NST = p.NST;
   const int rowB = K / 2;   // packed bytes per row
   const int rowU = K / 32;  // 16-byte units per row
-  const QsLayout L = qs_layout(K, G, p.max_rows, MR, NST);
+  const QsLayout L = qs_layout(K, G, p.max_rows, p.spr, MR, NST, p.stage_sc);
   uint8_t* ring = smem;
   T* sbS = reinterpret_cast<T*>(smem + L.sbs);
   T* sbB = reinterpret_cast<T*>(smem + L.sbb);
@@ -172,15 +182,17 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   if (warp == kQsConsumerWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      // scales and biases of the CTA's rows, then the weight stream
-      mbar_arrive_expect_tx(sb_bar, static_cast<uint32_t>(srows * G * 2 * 2));
-      int lr = 0;
-      for (int sg = 0; sg < nseg; ++sg) {
-        const QsSet& st = p.set[seg_set[sg]];
-        const size_t off = static_cast<size_t>(seg_row[sg]) * G * 2;
-        bulk_load(sbS + lr * G, st.s + off, seg_n[sg] * G * 2, sb_bar);
-        bulk_load(sbB + lr * G, st.b + off, seg_n[sg] * G * 2, sb_bar);
-        lr += seg_n[sg];
+      if (!p.stage_sc) {
+        // scales and biases of the CTA's rows, once
+        mbar_arrive_expect_tx(sb_bar, static_cast<uint32_t>(srows * G * 2 * 2));
+        int lr = 0;
+        for (int sg = 0; sg < nseg; ++sg) {
+          const QsSet& st = p.set[seg_set[sg]];
+          const size_t off = static_cast<size_t>(seg_row[sg]) * G * 2;
+          bulk_load(sbS + lr * G, st.s + off, seg_n[sg] * G * 2, sb_bar);
+          bulk_load(sbB + lr * G, st.b + off, seg_n[sg] * G * 2, sb_bar);
+          lr += seg_n[sg];
+        }
       }
       const long long total = static_cast<long long>(srows) * rowB;
       int issued = 0;
@@ -189,8 +201,26 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
         if (k >= NST && !mbar_wait(&empty[slot], ((k / NST) - 1) & 1, abort_flag, 0x501)) break;
         long long off = static_cast<long long>(k) * kQsStageBytes;
         const long long end = (off + kQsStageBytes < total) ? off + kQsStageBytes : total;
-        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(end - off));
-        uint8_t* dst = ring + slot * kQsStageBytes;
+        // stream rows [r_first, r_last] touched by this stage: their scales and biases
+        const int r_first = p.stage_sc ? static_cast<int>(off) / rowB : 0;
+        const int r_last = p.stage_sc ? static_cast<int>(end - 1) / rowB : -1;
+        const int nrk = r_last - r_first + 1;
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(end - off + 2 * nrk * G * 2));
+        uint8_t* dst = ring + slot * L.slot;
+        if (p.stage_sc) {
+          int base = 0;
+          for (int sg = 0; sg < nseg; ++sg) {
+            const int lo = r_first > base ? r_first : base;
+            const int hi = (r_last + 1) < (base + seg_n[sg]) ? (r_last + 1) : (base + seg_n[sg]);
+            if (lo < hi) {
+              const QsSet& st = p.set[seg_set[sg]];
+              const size_t so = static_cast<size_t>(seg_row[sg] + lo - base) * G * 2;
+              bulk_load(dst + L.sc + (lo - r_first) * G * 2, st.s + so, (hi - lo) * G * 2, &full[slot]);
+              bulk_load(dst + L.sc + (p.spr + lo - r_first) * G * 2, st.b + so, (hi - lo) * G * 2, &full[slot]);
+            }
+            base += seg_n[sg];
+          }
+        }
         long long seg0 = 0;  // stream offset of segment sg
         for (int sg = 0; sg < nseg && off < end; ++sg) {
           const long long seg_bytes = static_cast<long long>(seg_n[sg]) * rowB;
@@ -206,7 +236,7 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
         ++issued;
       }
       if (*abort_flag) {
-        mbar_wait_drain(sb_bar, 0, 200000000ull);
+        if (!p.stage_sc) mbar_wait_drain(sb_bar, 0, 200000000ull);
         for (int k = (issued > NST ? issued - NST : 0); k < issued; ++k)
           mbar_wait_drain(&full[k % NST], (k / NST) & 1, 200000000ull);
       }
@@ -252,7 +282,7 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   }
   named_barrier(kQsConsumerBar, kQsConsumerWarps * 32);
   griddep_launch();
-  bool ok = mbar_wait_warp(sb_bar, 0, abort_flag, 0x502);
+  bool ok = p.stage_sc ? true : mbar_wait_warp(sb_bar, 0, abort_flag, 0x502);
 
   int lr = warp;  // stream row of this warp
   float acc[MR];
@@ -263,13 +293,18 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
     if (!mbar_wait_warp(&full[slot], (k / NST) & 1, abort_flag, 0x503)) break;
     const int u_lo = k * kQsStageUnits;
     const int u_hi = (u_lo + kQsStageUnits < total_units) ? u_lo + kQsStageUnits : total_units;
-    const uint8_t* stage = ring + slot * kQsStageBytes;
+    const uint8_t* stage = ring + slot * L.slot;
+    const int r_first = p.stage_sc ? (k * kQsStageBytes) / rowB : 0;  // stream offsets fit 32 bits
+    // scale rows: the stage's own ([spr][G] from stream row r_first) or the CTA's
+    const T* stS = p.stage_sc ? reinterpret_cast<const T*>(stage + L.sc) : sbS;
+    const T* stB = p.stage_sc ? stS + p.spr * G : sbB;
+    const int sc_row0 = p.stage_sc ? r_first : 0;
     while (lr < srows && lr * rowU < u_hi) {
       const int r_lo = lr * rowU, r_hi = r_lo + rowU;
       const int a = r_lo > u_lo ? r_lo : u_lo;
       const int bnd = r_hi < u_hi ? r_hi : u_hi;
-      const T* srow = sbS + lr * G;
-      const T* brow = sbB + lr * G;
+      const T* srow = stS + (lr - sc_row0) * G;
+      const T* brow = stB + (lr - sc_row0) * G;
       for (int u = a + lane; u < bnd; u += 32) {
         const uint4 wv = *reinterpret_cast<const uint4*>(stage + (u - u_lo) * 16);
         const int kc = u - r_lo;  // unit within the row: values [32 kc, 32 kc + 32)
@@ -353,7 +388,7 @@ static int qs_max_rows(int rows, int P, int mode) {
 }
 
 struct QsGeometry {
-  int mode, rows, P, max_rows, MR, NST;
+  int mode, rows, P, max_rows, spr, MR, NST, stage_sc;
 };
 
 // Grid and ring depth of a request; NST = 0 when at least 4 stages do not fit
@@ -366,11 +401,18 @@ static QsGeometry qs_geometry(const QmmRequest& r, int sms) {
   if (g.rows <= 0) return g;
   g.P = g.rows < sms ? g.rows : sms;
   g.max_rows = qs_max_rows(g.rows, g.P, g.mode);
+  g.spr = kQsStageBytes / static_cast<int>(r.K / 2) + 2;
   g.MR = r.M <= 1 ? 1 : r.M <= 2 ? 2 : 4;
   const int K = static_cast<int>(r.K), G = static_cast<int>(r.K / r.group);
   g.NST = kQsMaxStages;
-  while (g.NST > 4 && qs_layout(K, G, g.max_rows, g.MR, g.NST).total + 128 > kQsSmemLimit) --g.NST;
-  if (qs_layout(K, G, g.max_rows, g.MR, g.NST).total + 128 > kQsSmemLimit) g.NST = 0;
+  // scales copied once when at least 4 stages fit next to them, else per stage
+  for (g.stage_sc = 0; g.stage_sc < 2; ++g.stage_sc) {
+    g.NST = kQsMaxStages;
+    while (g.NST > 4 && qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc).total + 128 > kQsSmemLimit)
+      --g.NST;
+    if (qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc).total + 128 <= kQsSmemLimit) return g;
+  }
+  g.NST = 0;
   return g;
 }
 
@@ -394,7 +436,7 @@ bool qmv_stream_eligible(const QmmRequest& r) {
 
 template <int DT, int MR, int MODE>
 static int qs_launch(QsParams& p, cudaStream_t stream) {
-  const QsLayout L = qs_layout(p.K, p.G, p.max_rows, MR, p.NST);
+  const QsLayout L = qs_layout(p.K, p.G, p.max_rows, p.spr, MR, p.NST, p.stage_sc);
   auto k = qmv_stream_kernel<DT, MR, MODE>;
   if (int e = ensure_smem(k, kQsSmemLimit)) return e;
   return launch(k, dim3(p.P), dim3(kQsThreads), static_cast<size_t>(L.total) + 128, stream, p);
@@ -438,6 +480,8 @@ int qmv_stream_run(const QmmRequest& r, cudaStream_t stream) {
   p.rows = g.rows;
   p.P = g.P;
   p.max_rows = g.max_rows;
+  p.spr = g.spr;
+  p.stage_sc = g.stage_sc;
   p.NST = g.NST;
   if (r.dtype == MT_BF16) {
     if (mode == 2) return qs_dispatch_mr<MT_BF16, 2>(p, stream);

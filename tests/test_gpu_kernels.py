@@ -61,6 +61,7 @@ QMM_CASES = [
     (1, 2560, 9728, 64, 4, "bfloat16"),
     (1, 2560, 4096, 64, 4, "bfloat16"),
     (1, 20000, 2560, 64, 4, "bfloat16"),
+    (1, 151936, 2560, 64, 4, "bfloat16"),  # lm_head rows: scales streamed with the weight stages
     (2, 1536, 2560, 64, 4, "float16"),
 ]
 
