@@ -99,6 +99,8 @@ __global__ void __launch_bounds__(128) sdpa_kernel(const SdpaParams p) {
   const T* vg = static_cast<const T*>(p.v) + b * p.vs_b + kvh * p.vs_h;
 
   griddep_wait();
+
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   // keys this block can see: causal limit of its last query row
   int kend = p.Lk;
   if (p.causal) {
@@ -234,7 +236,6 @@ __global__ void __launch_bounds__(128) sdpa_kernel(const SdpaParams p) {
     }
     __syncthreads();
   }
-  griddep_launch();
   T* og = static_cast<T*>(p.o) + b * p.os_b + h * p.os_h;
 #pragma unroll
   for (int r = 0; r < 2; ++r) {

@@ -17,6 +17,7 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(const float* __restrict
   __shared__ float xs[32][33];
   __shared__ float wsm[32][33];
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
   const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -47,7 +48,6 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(const float* __restrict
       y[static_cast<int64_t>(m) * N + n] = v;
     }
   }
-  griddep_launch();
 }
 
 }  // namespace mt

@@ -135,6 +135,7 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict_
   __shared__ DiffPartial sp[kDiffThreads / 32];
   __shared__ int am_last;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   DiffPartial p;
   init(p);
   // contiguous slice per block, strided by thread inside it: every index is
@@ -216,7 +217,6 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict_
     out->nan_excess = acc.nan_ex;
     *counter = 0;  // ready for the next call
   }
-  griddep_launch();
 }
 
 // counter in the workspace's control region, block partials after it

@@ -12,13 +12,13 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const void* __restrict__ gp
                                                      void* __restrict__ yp, int64_t n) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const T* g = static_cast<const T*>(gp);
   const T* u = static_cast<const T*>(up);
   T* y = static_cast<T*>(yp);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
     y[i] = Elem<DT>::from_f(swiglu_rounded<DT>(Elem<DT>::to_f(g[i]), Elem<DT>::to_f(u[i])));
-  griddep_launch();
 }
 
 // out[t, k] = round(round(s*q) + b) for token tok[t]; one CTA per token.
@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(256) qembed_kernel(const int32_t* __restrict__
                                                      int bits) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const int t = blockIdx.x;
   const int tok = tokens[t];
   T* out = static_cast<T*>(outp) + static_cast<int64_t>(t) * D;
@@ -50,7 +51,6 @@ __global__ void __launch_bounds__(256) qembed_kernel(const int32_t* __restrict__
     const float sq = round_to<DT>(__fmul_rn(s, static_cast<float>(q)));
     out[k] = Elem<DT>::from_f(__fadd_rn(sq, b));
   }
-  griddep_launch();
 }
 
 // Single CTA of 1024 threads: pass 1 logsumexp (per-thread online max/sum,
@@ -82,6 +82,7 @@ __global__ void __cluster_dims__(kLpCtas, 1, 1) __launch_bounds__(kLpThreads)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t lo = n * rank / kLpCtas, hi = n * (rank + 1) / kLpCtas;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const T* x = static_cast<const T*>(lp);
 
   // pass 1: max
@@ -177,7 +178,6 @@ __global__ void __cluster_dims__(kLpCtas, 1, 1) __launch_bounds__(kLpThreads)
     if (lse_out) *lse_out = lse;
   }
   cluster.sync();  // the other CTAs' shared memory stays alive until rank 0 has read it
-  griddep_launch();
 }
 
 }  // namespace mt

@@ -22,6 +22,7 @@ __global__ void __launch_bounds__(256) mamba_scan_kernel(const void* __restrict_
                                                          int d_inner) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   constexpr int CPW = 32 / NS;  // channels per warp
   const int lane = threadIdx.x & 31;
   const int s = lane % NS;
@@ -63,7 +64,6 @@ __global__ void __launch_bounds__(256) mamba_scan_kernel(const void* __restrict_
     }
   }
   if (hstate && active) hstate[static_cast<int64_t>(c) * NS + s] = h;
-  griddep_launch();
 }
 
 template <int DT>
@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(256) causal_conv1d_kernel(const void* __restri
                                                             void* __restrict__ yp, int L, int C, int W, int silu) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<int64_t>(L) * C) return;
   const int l = static_cast<int>(i / C), c = static_cast<int>(i % C);

@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const void* __restrict__ 
                                                        int64_t rows, int dim) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -99,7 +100,6 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const void* __restrict__ 
     for (int i = lane; i < dim; i += 32)
       y[i] = Elem<DT>::from_f(__fmul_rn(__fmul_rn(Elem<DT>::to_f(src[i]), scale), Elem<DT>::to_f(w[i])));
   }
-  griddep_launch();
 }
 
 // two-pass layer norm: mean, centred variance, optional affine
@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict_
                                                          void* __restrict__ yp, int64_t rows, int dim) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -133,7 +134,6 @@ __global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict_
     if (b) v = __fadd_rn(v, Elem<DT>::to_f(b[i]));
     y[i] = Elem<DT>::from_f(v);
   }
-  griddep_launch();
 }
 
 struct RopeFreqs {
@@ -153,6 +153,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, 
                                                    float scale, int64_t offset, const RopeFreqs f) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const int half = dims / 2;
   const int per_row = half + (D - dims);
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
     int64_t cap, int64_t offset, const RopeFreqs f) {
   using T = typename Elem<DT>::T;
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int heads = Hq + Hkv;
@@ -251,7 +253,6 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
     *reinterpret_cast<uint2*>(static_cast<T*>(vc) + crow * 128 + 4 * lane) =
         *reinterpret_cast<const uint2*>(vs + 4 * lane);
   }
-  griddep_launch();
 }
 
 static RopeFreqs make_freqs(int dims, double base) {

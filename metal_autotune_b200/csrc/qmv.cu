@@ -130,6 +130,8 @@ __global__ void __launch_bounds__(256) qmv_kernel(const QmvParams p) {
   float* xsum = reinterpret_cast<float*>(xs + MR * (K / 4));  // [MR][nchunk]
 
   griddep_wait();
+
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const T* x = static_cast<const T*>(p.x);
   for (int i = threadIdx.x; i < MR * (K / 4); i += blockDim.x) {
     const int m = i / (K / 4), q = i % (K / 4);
@@ -153,7 +155,6 @@ __global__ void __launch_bounds__(256) qmv_kernel(const QmvParams p) {
     xsum[i] = s;
   }
   __syncthreads();
-  griddep_launch();
 
   const int lane = threadIdx.x & 31;
   const int j = lane & 15;

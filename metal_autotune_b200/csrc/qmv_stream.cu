@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   // -------------------------------------------------------------- consumers
   const int ct = threadIdx.x;  // 0..511
   griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
   const T* x = static_cast<const T*>(p.x);
   // x as element-type pairs (x_{8wi+i}, x_{8wi+i+4}), one 16-byte slot per
   // (unit, word), and the fp32 sum of every unit
@@ -281,7 +282,6 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
     xsum[i] = s;
   }
   named_barrier(kQsConsumerBar, kQsConsumerWarps * 32);
-  griddep_launch();
   bool ok = p.stage_sc ? true : mbar_wait_warp(sb_bar, 0, abort_flag, 0x502);
 
   int lr = warp;  // stream row of this warp
