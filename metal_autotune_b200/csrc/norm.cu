@@ -102,6 +102,74 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const void* __restrict__ 
   }
 }
 
+// rms_norm with the row held in registers: dim = 256 * NC, lane l owns the
+// 8-value chunks l, l+32, ...; all loads of the row (x, residual) are issued
+// before the first use, so the row costs one memory round trip. Same
+// arithmetic in the same order as rms_norm_kernel (bit-identical results).
+template <int DT, bool HAS_RES, int NC>
+__global__ void __launch_bounds__(128) rms_norm_reg_kernel(const void* __restrict__ xp, const void* __restrict__ rp,
+                                                           const void* __restrict__ wp, float eps,
+                                                           void* __restrict__ hp, void* __restrict__ yp,
+                                                           int64_t rows) {
+  using T = typename Elem<DT>::T;
+  constexpr int dim = 256 * NC;
+  griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* x = static_cast<const T*>(xp) + row * dim;
+  const T* w = static_cast<const T*>(wp);
+  float v[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) load8<DT>(x + lane * 8 + c * 256, v[c]);
+  if (HAS_RES) {
+    const T* res = static_cast<const T*>(rp) + row * dim;
+    T* h = static_cast<T*>(hp) + row * dim;
+    float r[NC][8];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) load8<DT>(res + lane * 8 + c * 256, r[c]);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[c][e] = round_to<DT>(__fadd_rn(v[c][e], r[c][e]));
+      store8<DT>(h + lane * 8 + c * 256, v[c]);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(v[c][e], v[c][e], ss);
+  ss = warp_sum(ss);
+  const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(dim)), eps));
+  T* y = static_cast<T*>(yp) + row * dim;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    float g[8], o[8];
+    load8<DT>(w + lane * 8 + c * 256, g);  // the weight row is shared by every row: an L1/L2 hit
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(__fmul_rn(v[c][e], scale), g[e]);
+    store8<DT>(y + lane * 8 + c * 256, o);
+  }
+}
+
+// Launches rms_norm_reg_kernel when dim is a multiple of 256 with a register
+// specialisation; returns 1 when it does not apply.
+template <int DT, bool HAS_RES>
+static int rms_norm_reg_launch(const void* x, const void* res, const void* w, float eps, void* h, void* y,
+                               int64_t rows, int64_t dim, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>((rows + 3) / 4)), block(128);
+  switch (dim) {
+    case 1024: return launch(rms_norm_reg_kernel<DT, HAS_RES, 4>, grid, block, 0, stream, x, res, w, eps, h, y, rows);
+    case 2048: return launch(rms_norm_reg_kernel<DT, HAS_RES, 8>, grid, block, 0, stream, x, res, w, eps, h, y, rows);
+    case 2560: return launch(rms_norm_reg_kernel<DT, HAS_RES, 10>, grid, block, 0, stream, x, res, w, eps, h, y, rows);
+    case 3072: return launch(rms_norm_reg_kernel<DT, HAS_RES, 12>, grid, block, 0, stream, x, res, w, eps, h, y, rows);
+    case 4096: return launch(rms_norm_reg_kernel<DT, HAS_RES, 16>, grid, block, 0, stream, x, res, w, eps, h, y, rows);
+    default: return 1;
+  }
+}
+
 // two-pass layer norm: mean, centred variance, optional affine
 template <int DT>
 __global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict__ xp, const void* __restrict__ wp,
@@ -287,6 +355,14 @@ int mt_rms_norm(const void* x, const void* w, float eps, void* y, int64_t rows, 
   const bool vec = dim % 8 == 0 && aligned(x, 16) && aligned(y, 16) && aligned(w, 16);
   const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
   int rc = MT_OK;
+  if (vec && (dtype == MT_BF16 || dtype == MT_F16)) {
+    rc = dtype == MT_BF16 ? rms_norm_reg_launch<MT_BF16, false>(x, nullptr, w, eps, nullptr, y, rows, dim,
+                                                                   (cudaStream_t)stream)
+                          : rms_norm_reg_launch<MT_F16, false>(x, nullptr, w, eps, nullptr, y, rows, dim,
+                                                               (cudaStream_t)stream);
+    if (rc != 1) return rc;
+    rc = MT_OK;
+  }
   MT_DT_SWITCH(dtype, rc = vec ? launch(rms_norm_kernel<DT, false, true>, grid, dim3(256), 0, (cudaStream_t)stream, x,
                                         nullptr, w, eps, nullptr, y, rows, (int)dim)
                                : launch(rms_norm_kernel<DT, false, false>, grid, dim3(256), 0,
@@ -305,6 +381,14 @@ int mt_add_rms_norm(const void* x, const void* residual, const void* w, float ep
                    aligned(residual, 16);
   const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
   int rc = MT_OK;
+  if (vec && (dtype == MT_BF16 || dtype == MT_F16)) {
+    rc = dtype == MT_BF16 ? rms_norm_reg_launch<MT_BF16, true>(x, residual, w, eps, h, y, rows, dim,
+                                                                  (cudaStream_t)stream)
+                          : rms_norm_reg_launch<MT_F16, true>(x, residual, w, eps, h, y, rows, dim,
+                                                              (cudaStream_t)stream);
+    if (rc != 1) return rc;
+    rc = MT_OK;
+  }
   MT_DT_SWITCH(dtype, rc = vec ? launch(rms_norm_kernel<DT, true, true>, grid, dim3(256), 0, (cudaStream_t)stream, x,
                                         residual, w, eps, h, y, rows, (int)dim)
                                : launch(rms_norm_kernel<DT, true, false>, grid, dim3(256), 0,
