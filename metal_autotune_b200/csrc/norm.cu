@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
     const void* __restrict__ qp, const void* __restrict__ kp, const void* __restrict__ vp, int64_t q_stride,
     int64_t kv_stride, const void* __restrict__ qwp, const void* __restrict__ kwp, float eps,
     void* __restrict__ qo, void* __restrict__ kc, void* __restrict__ vc, int T_, int Hq, int Hkv,
-    int64_t cap, int64_t offset, const RopeFreqs f) {
+    int64_t cap, int64_t offset, const __grid_constant__ RopeFreqs f) {
   using T = typename Elem<DT>::T;
   griddep_wait();
   griddep_launch();  // dependents may launch now; their own wait covers this grid
@@ -269,7 +269,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
   const T* src = is_q ? static_cast<const T*>(qp) + t * q_stride + h * 128
                       : static_cast<const T*>(kp) + t * kv_stride + h * 128;
   const T* nw = static_cast<const T*>(is_q ? qwp : kwp);
-  // 4 values per lane: d = 4*lane .. 4*lane+3
+  // 4 values per lane: d = 4*lane .. 4*lane+3; a k head's v row is loaded
+  // together with the k row (one memory round trip)
+  uint2 vrow = make_uint2(0, 0);
+  if (!is_q) vrow = *reinterpret_cast<const uint2*>(static_cast<const T*>(vp) + t * kv_stride + h * 128 + 4 * lane);
   float v[4], g[4];
   {
     const uint2 u = *reinterpret_cast<const uint2*>(src + 4 * lane);
@@ -317,9 +320,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
   } else {
     const int64_t crow = static_cast<int64_t>(h) * cap + offset + t;
     *reinterpret_cast<uint2*>(static_cast<T*>(kc) + crow * 128 + 4 * lane) = out;
-    const T* vs = static_cast<const T*>(vp) + t * kv_stride + h * 128;
-    *reinterpret_cast<uint2*>(static_cast<T*>(vc) + crow * 128 + 4 * lane) =
-        *reinterpret_cast<const uint2*>(vs + 4 * lane);
+    *reinterpret_cast<uint2*>(static_cast<T*>(vc) + crow * 128 + 4 * lane) = vrow;
   }
 }
 
