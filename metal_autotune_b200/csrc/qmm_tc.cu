@@ -347,51 +347,71 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16(kBM, TN, DT == MT_BF16);
-      bool issued = false;
-      int use[2] = {0, 0};
-      int slot = 0;
-      int i = 0;
-      bool ok = true;
-      long long u = u0;
-      while (u < u1 && ok) {
-        const int klo = static_cast<int>(u) % nk;
-        const int len = static_cast<int>(((nk - klo) < (u1 - u)) ? (nk - klo) : (u1 - u));
-        if (!mbar_wait(&acc_empty[slot], (use[slot] & 1) ^ 1, abort_flag, 0x203)) break;
+    // The whole warp runs the loop (its waits and bookkeeping stay warp-uniform)
+    // and one elected lane issues; descriptors are formed once, and each MMA
+    // only adds a precomputed offset, so the issue rate is the tensor core's.
+    const uint32_t idesc = idesc_f16(kBM, TN, DT == MT_BF16);
+    const uint64_t xdesc0 = smem_desc_k_sw128(smem_addr(xs));
+    uint32_t koff[kBK / 16];  // descriptor address offset of each 16-wide K step
+#pragma unroll
+    for (int kk = 0; kk < kBK / 16; ++kk) koff[kk] = static_cast<uint32_t>(((kk >> 2) * TN * 128 + (kk & 3) * 32) >> 4);
+    const uint32_t xstep = static_cast<uint32_t>(x_stage_bytes >> 4);
+    bool issued = false;
+    int use[2] = {0, 0};
+    int slot = 0;
+    int s = 0, sph = 0, t = 0, tph = 0;
+    bool ok = true;
+    long long u = u0;
+    while (u < u1 && ok) {
+      const int klo = static_cast<int>(u) % nk;
+      const int len = static_cast<int>(((nk - klo) < (u1 - u)) ? (nk - klo) : (u1 - u));
+      if (!mbar_wait_warp(&acc_empty[slot], (use[slot] & 1) ^ 1, abort_flag, 0x203)) break;
+      tc_fence_after();
+      const uint32_t d_base = tmem + slot * NACC * TN;
+      for (int j = 0; j < len; ++j) {
+        if (!mbar_wait_warp(&x_full[s], sph, abort_flag, 0x201) ||
+            !mbar_wait_warp(&a_full[t], tph, abort_flag, 0x202)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d_base = tmem + slot * NACC * TN;
-        for (int j = 0; j < len; ++j, ++i) {
-          const int s = i % SS, t = i % TS;
-          if (!mbar_wait(&x_full[s], (i / SS) & 1, abort_flag, 0x201) ||
-              !mbar_wait(&a_full[t], (i / TS) & 1, abort_flag, 0x202)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t xbase = smem_addr(xs + s * x_stage_bytes);
+        const uint64_t sdesc = xdesc0 + s * xstep;
+        const uint32_t abase = tmem + kAccCols + t * NACC * 64;
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t bdesc = smem_desc_k_sw128(xbase + (kk >> 2) * TN * 128 + (kk & 3) * 32);
 #pragma unroll
             for (int a = 0; a < NACC; ++a)
-              tc_mma_ts(d_base + a * TN, tmem + kAccCols + (t * NACC + a) * 64 + kk * 8, bdesc, idesc,
+              tc_mma_ts(d_base + a * TN, abase + a * 64 + kk * 8, sdesc + koff[kk], idesc,
                         (j > 0 || kk > 0) ? 1u : 0u);
           }
-          issued = true;
           tc_commit(&s_empty[s]);
           tc_commit(&a_empty[t]);
         }
-        if (!ok) break;
-        tc_commit(&acc_full[slot]);
-        ++use[slot];
-        slot = (slot + 1) % p.acc_slots;
-        u += len;
+        __syncwarp();
+        issued = true;
+        if (++s == SS) {
+          s = 0;
+          sph ^= 1;
+        }
+        if (++t == TS) {
+          t = 0;
+          tph ^= 1;
+        }
       }
-      if (*abort_flag && issued) {
+      if (!ok) break;
+      if (elect_one()) tc_commit(&acc_full[slot]);
+      __syncwarp();
+      ++use[slot];
+      slot = (slot + 1) % p.acc_slots;
+      u += len;
+    }
+    if (__any_sync(0xffffffffu, *abort_flag != 0) && issued) {
+      if (elect_one()) {
         tc_commit(drain);
         mbar_wait_drain(drain, 0, 200000000ull);
       }
+      __syncwarp();
     }
   } else if (warp >= 4 && warp < kEpiWarp0) {
     // ------------------------------------------------------------ dequantisers
@@ -462,8 +482,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         load_block(wrap ? tile + 1 : tile, wrap ? 0 : k + d, sc_nxt, bi_nxt);
       }
     }
+    // The tensor-memory stores of unit i complete (wait + fence + a_full
+    // arrive) after unit i+1's weights are read from shared memory, so their
+    // latency overlaps that read; if unit i+1's weights have not landed yet,
+    // unit i is completed first rather than held back behind the copy.
+    int s = 0, sph = 0, t = 0, tph = 0;
+    int pend_t = -1;  // A stage whose stores are issued but not yet published
+    auto publish = [&]() {
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[pend_t]);
+      pend_t = -1;
+    };
     for (int i = 0; i < nunits; ++i) {
-      const int s = i % SS, t = i % TS;
       if (i == next_start) {
         sc_cur = sc_nxt;
         bi_cur = bi_nxt;
@@ -474,7 +506,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
           load_block(wrap ? tile + 1 : tile, wrap ? 0 : k + d, sc_nxt, bi_nxt);
         }
       }
-      if (!mbar_wait_warp(&w_full[aset * kMaxSS + s], (i / SS) & 1, abort_flag, 0x301)) break;
+      uint64_t* wf = &w_full[aset * kMaxSS + s];
+      if (pend_t >= 0 && !__all_sync(0xffffffffu, mbar_test(wf, sph))) publish();
+      if (!mbar_wait_warp(wf, sph, abort_flag, 0x301)) break;
       uint4 wv[kMyChunks];
       const uint8_t* wrow = ws_ + s * w_stage_bytes + aset * w_set_bytes + r * WL::kRowBytes;
 #pragma unroll
@@ -482,9 +516,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         wv[cc] = *reinterpret_cast<const uint4*>(wrow + WL::phys(r, c0 + cc) * 16);
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[s]);
+      if (pend_t >= 0) publish();
       const int kst = k * kBK;
       const int gb = (kst >> gshift) & ~7;
-      if (!mbar_wait_warp(&a_empty[t], ((i / TS) & 1) ^ 1, abort_flag, 0x302)) break;
+      if (!mbar_wait_warp(&a_empty[t], tph ^ 1, abort_flag, 0x302)) break;
       const uint32_t col0 = kAccCols + (t * NACC + aset) * 64 + (DUAL ? 0 : wg * 32);
 #pragma unroll
       for (int h = 0; h < kCols / 32; ++h) {
@@ -498,15 +533,21 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         }
         tmem_st32(tmem + lane_base + col0 + h * 32, out);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[t]);
+      pend_t = t;
       if (++k == nk) {
         k = 0;
         ++tile;
       }
+      if (++s == SS) {
+        s = 0;
+        sph ^= 1;
+      }
+      if (++t == TS) {
+        t = 0;
+        tph ^= 1;
+      }
     }
+    if (pend_t >= 0) publish();
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
     // Every segment but the CTA's last: the last one is finished by all 16
