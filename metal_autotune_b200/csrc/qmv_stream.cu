@@ -182,6 +182,7 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   if (warp == kQsConsumerWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      const uint64_t pol = l2_evict_first();  // weights, scales and biases are read once
       if (!p.stage_sc) {
         // scales and biases of the CTA's rows, once
         mbar_arrive_expect_tx(sb_bar, static_cast<uint32_t>(srows * G * 2 * 2));
@@ -189,8 +190,8 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
         for (int sg = 0; sg < nseg; ++sg) {
           const QsSet& st = p.set[seg_set[sg]];
           const size_t off = static_cast<size_t>(seg_row[sg]) * G * 2;
-          bulk_load(sbS + lr * G, st.s + off, seg_n[sg] * G * 2, sb_bar);
-          bulk_load(sbB + lr * G, st.b + off, seg_n[sg] * G * 2, sb_bar);
+          bulk_load_hint(sbS + lr * G, st.s + off, seg_n[sg] * G * 2, sb_bar, pol);
+          bulk_load_hint(sbB + lr * G, st.b + off, seg_n[sg] * G * 2, sb_bar, pol);
           lr += seg_n[sg];
         }
       }
@@ -215,8 +216,9 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
             if (lo < hi) {
               const QsSet& st = p.set[seg_set[sg]];
               const size_t so = static_cast<size_t>(seg_row[sg] + lo - base) * G * 2;
-              bulk_load(dst + L.sc + (lo - r_first) * G * 2, st.s + so, (hi - lo) * G * 2, &full[slot]);
-              bulk_load(dst + L.sc + (p.spr + lo - r_first) * G * 2, st.b + so, (hi - lo) * G * 2, &full[slot]);
+              bulk_load_hint(dst + L.sc + (lo - r_first) * G * 2, st.s + so, (hi - lo) * G * 2, &full[slot], pol);
+              bulk_load_hint(dst + L.sc + (p.spr + lo - r_first) * G * 2, st.b + so, (hi - lo) * G * 2, &full[slot],
+                             pol);
             }
             base += seg_n[sg];
           }
@@ -227,8 +229,8 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
           if (off < seg0 + seg_bytes) {
             const long long n = ((seg0 + seg_bytes) < end ? (seg0 + seg_bytes) : end) - off;
             const uint8_t* src = p.set[seg_set[sg]].w + static_cast<long long>(seg_row[sg]) * rowB + (off - seg0);
-            bulk_load(dst + (off - static_cast<long long>(k) * kQsStageBytes), src, static_cast<uint32_t>(n),
-                      &full[slot]);
+            bulk_load_hint(dst + (off - static_cast<long long>(k) * kQsStageBytes), src, static_cast<uint32_t>(n),
+                           &full[slot], pol);
             off += n;
           }
           seg0 += seg_bytes;
