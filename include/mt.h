@@ -108,6 +108,19 @@ int mt_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
                         mt_stream_t stream);
 
 /*
+ * Host-only check of the prefill kernel's work partition (no GPU needed): C
+ * thread-block clusters of S CTAs over `tiles` x `nk` K-stages, each cluster's
+ * unit range split by tile segment and each segment by K among its CTAs.
+ * Verifies that every K-stage of every tile is computed exactly once, that
+ * every tile split across CTAs has exactly one owner reducing it from
+ * partials that are all produced, each workspace partial slot written at most
+ * once per CTA and read by its owner, and the K order of the owner's sum.
+ * Writes the largest number of K-stages of one CTA to *max_units_out.
+ * Returns MT_OK, or MT_ERR_INVALID_ARGUMENT naming the broken rule.
+ */
+int mt_qmm_partition_check(int64_t tiles, int nk, int cluster_size, int clusters, int64_t* max_units_out);
+
+/*
  * Fused region: y = residual + quantized_matmul(x, w, ...), each step rounded
  * to dtype as the unfused ops would (the `v22 = v0 + v21` cut of the
  * reference's generated wrapper,

@@ -53,6 +53,7 @@
 // work between them), so no CTA can be left waiting at one.
 #include <cooperative_groups.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "mt_common.cuh"
@@ -1038,6 +1039,120 @@ static PlanStats plan_stats(const QmmTcParams& p) {
   return st;
 }
 
+// Host mirror of the kernel's partition bookkeeping (the same seg_of /
+// sub_k / seg_complete / seg_slot / cluster_begin the kernel runs): which CTA
+// computes which K-stages, where each partial goes, and which cluster reduces
+// which tile from which partials, checked for exact coverage.
+static int partition_check(long long tiles, int nk, int S, int C, long long* max_units) {
+  if (tiles < 1 || nk < 1 || S < 1 || S > kMaxS || C < 1 || static_cast<long long>(C) * S > kMaxP ||
+      (S > 1 && S > nk)) {
+    set_error("qmm partition: bad shape tiles=%lld nk=%d S=%d C=%d", tiles, nk, S, C);
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  QmmTcParams p;
+  memset(&p, 0, sizeof(p));
+  p.nk = nk;
+  p.S = S;
+  p.C = C;
+  p.units = tiles * nk;
+  p.c_magic = C > 1 ? ~0ull / static_cast<uint64_t>(C) + 1 : 0;
+  const int P = C * S;
+  std::vector<std::vector<int>> cover(static_cast<size_t>(tiles));  // K-stages computed, per tile
+  std::vector<int> written(static_cast<size_t>(P) * kSlots, -1);    // tile of each (CTA, slot) partial
+  std::vector<int> read(static_cast<size_t>(P) * kSlots, 0);
+  std::vector<int> owners(static_cast<size_t>(tiles), 0);
+  long long mu = 0;
+  auto fail = [&](const char* what, long long a, long long b) {
+    set_error("qmm partition (tiles=%lld nk=%d S=%d C=%d): %s (%lld, %lld)", tiles, nk, S, C, what, a, b);
+    return MT_ERR_INVALID_ARGUMENT;
+  };
+  // what every CTA computes and where its partials go
+  for (int j = 0; j < C; ++j) {
+    const long long U0 = cluster_begin(p, j), U1 = cluster_begin(p, j + 1);
+    if (U1 <= U0) continue;
+    const int t0 = static_cast<int>(U0 / nk);
+    const int nseg = static_cast<int>((U1 - 1) / nk) - t0 + 1;
+    if (S > 1 && nseg > kMaxSegK) return fail("segments per cluster", j, nseg);
+    const Seg last = seg_of(nk, U0, U1, t0, nseg - 1);
+    const bool xchg = last.ka == 0 && !seg_complete(S, nk, last);
+    for (int r = 0; r < S; ++r) {
+      long long u = 0;
+      for (int i = 0; i < nseg; ++i) {
+        const Seg s = seg_of(nk, U0, U1, t0, i);
+        const int lo = sub_k(s.ka, s.kb, S, r), hi = sub_k(s.ka, s.kb, S, r + 1);
+        if (hi <= lo) continue;
+        u += hi - lo;
+        for (int k = lo; k < hi; ++k) cover[static_cast<size_t>(s.tile)].push_back(k);
+        if (seg_complete(S, nk, s) || (xchg && i == nseg - 1)) continue;
+        const size_t slot = static_cast<size_t>(j * S + r) * kSlots + seg_slot(i);
+        if (written[slot] >= 0) return fail("partial slot written twice", j * S + r, seg_slot(i));
+        written[slot] = s.tile;
+      }
+      if (u > mu) mu = u;
+    }
+  }
+  // what every owner reduces, in the order the kernel sums it
+  for (int j = 0; j < C; ++j) {
+    const long long U0 = cluster_begin(p, j), U1 = cluster_begin(p, j + 1);
+    if (U1 <= U0) continue;
+    const int t0 = static_cast<int>(U0 / nk);
+    const int nseg = static_cast<int>((U1 - 1) / nk) - t0 + 1;
+    const Seg last = seg_of(nk, U0, U1, t0, nseg - 1);
+    const bool xchg = last.ka == 0 && !seg_complete(S, nk, last);
+    for (int i = 0; i < nseg; ++i) {
+      const Seg s = seg_of(nk, U0, U1, t0, i);
+      if (seg_complete(S, nk, s)) {
+        ++owners[static_cast<size_t>(s.tile)];
+        continue;
+      }
+      if (s.ka != 0) continue;
+      ++owners[static_cast<size_t>(s.tile)];
+      int kpos = 0;  // the sum runs in K order
+      for (int r = 0; r < S; ++r) {
+        const int lo = sub_k(s.ka, s.kb, S, r), hi = sub_k(s.ka, s.kb, S, r + 1);
+        if (hi <= lo) continue;
+        if (lo != kpos) return fail("owner's own partials out of K order", s.tile, lo);
+        kpos = hi;
+        if (xchg && i == nseg - 1) continue;
+        const size_t slot = static_cast<size_t>(j * S + r) * kSlots + seg_slot(i);
+        if (written[slot] != s.tile) return fail("owner reads a slot holding another tile", s.tile, written[slot]);
+        ++read[slot];
+      }
+      const long long tile_end = static_cast<long long>(s.tile + 1) * nk;
+      for (int jj = j + 1; jj < C; ++jj) {
+        const long long V0 = cluster_begin(p, jj);
+        if (V0 >= tile_end) break;
+        const long long V1 = cluster_begin(p, jj + 1);
+        const int ka = static_cast<int>(V0 - static_cast<long long>(s.tile) * nk);
+        const int kb = V1 < tile_end ? static_cast<int>(V1 - static_cast<long long>(s.tile) * nk) : nk;
+        for (int r = 0; r < S; ++r) {
+          const int lo = sub_k(ka, kb, S, r), hi = sub_k(ka, kb, S, r + 1);
+          if (hi <= lo) continue;
+          if (lo != kpos) return fail("following partials out of K order", s.tile, lo);
+          kpos = hi;
+          const size_t slot = static_cast<size_t>(jj * S + r) * kSlots;
+          if (written[slot] != s.tile) return fail("owner reads a following slot holding another tile", s.tile,
+                                                   written[slot]);
+          ++read[slot];
+        }
+      }
+      if (kpos != nk) return fail("owner's sum does not reach the tile's last K-stage", s.tile, kpos);
+    }
+  }
+  for (long long t = 0; t < tiles; ++t) {
+    std::vector<int>& c = cover[static_cast<size_t>(t)];
+    std::sort(c.begin(), c.end());
+    if (static_cast<int>(c.size()) != nk) return fail("K-stages computed for a tile", t, static_cast<long long>(c.size()));
+    for (int k = 0; k < nk; ++k)
+      if (c[static_cast<size_t>(k)] != k) return fail("K-stage computed twice or never", t, k);
+    if (owners[static_cast<size_t>(t)] != 1) return fail("owners of a tile", t, owners[static_cast<size_t>(t)]);
+  }
+  for (size_t i = 0; i < written.size(); ++i)
+    if (written[i] >= 0 && read[i] != 1) return fail("partial read by its owner", static_cast<long long>(i), read[i]);
+  if (max_units) *max_units = mu;
+  return MT_OK;
+}
+
 template <int DT, int BITS, int DUAL>
 static int launch_tc(QmmTcParams& p, size_t smem, int sms, cudaStream_t stream) {
   auto k = qmm_tc_kernel<DT, BITS, DUAL>;
@@ -1220,3 +1335,11 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
 }
 
 }  // namespace mt
+
+extern "C" int mt_qmm_partition_check(int64_t tiles, int nk, int cluster_size, int clusters, int64_t* max_units_out) {
+  mt::clear_error();
+  long long mu = 0;
+  const int rc = mt::partition_check(tiles, nk, cluster_size, clusters, &mu);
+  if (rc == MT_OK && max_units_out) *max_units_out = mu;
+  return rc;
+}

@@ -67,6 +67,7 @@ SIGNATURES = {
     "mt_quantized_matmul_multi": (
         C.c_int, [P, P, P, P, P, I64, P, P, P, P, I64, P, P, P, P, I64, I64, I64, I32, I32, I32, P, SZ, P]),
     "mt_qmm_workspace_bytes": (C.c_size_t, [I64, I64, I64, I32, I32]),
+    "mt_qmm_partition_check": (C.c_int, [I64, I32, I32, I32, P]),
     "mt_rms_norm": (C.c_int, [P, P, F32, P, I64, I64, I32, P]),
     "mt_add_rms_norm": (C.c_int, [P, P, P, F32, P, P, I64, I64, I32, P]),
     "mt_rope": (C.c_int, [P, P, I64, I64, I64, I64, I32, I32, F32, F32, I64, I32, P]),
