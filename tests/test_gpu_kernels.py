@@ -194,6 +194,11 @@ def test_qk_norm_rope_cache(cuda, oracle, T, offset):
     (2, 4, 4, 70, 70, 64, False),
     (1, 8, 2, 33, 100, 128, True),
     (1, 4, 1, 200, 200, 128, True),
+    # decode shapes (a kv head's query rows in one CTA): two tokens, four tokens, long keys, head_dim 64
+    (1, 8, 2, 2, 300, 64, True),
+    (2, 16, 4, 4, 77, 128, False),
+    (1, 4, 4, 3, 1000, 128, True),
+    (1, 32, 8, 1, 2048, 128, True),
 ])
 def test_sdpa(cuda, oracle, B, Hq, Hkv, Lq, Lk, D, causal):
     q = oracle.round_to(rng.standard_normal((B, Hq, Lq, D)).astype(np.float32), "bfloat16")
