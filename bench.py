@@ -443,6 +443,12 @@ def run_kernels(args, cfg):
         bench(f"{tag}_down", lambda: lib.quantized_matmul(xf, *W["d"], residual=res), 2 * M * h * ff, h * ff * bpp)
         nw = torch.ones(h, device="cuda", dtype=torch.bfloat16)
         bench(f"{tag}_rms_norm", lambda: lib.rms_norm(xh, nw, 1e-6), 0, 2 * M * h * 2)
+        if M <= 4:
+            # the decode cuts with the RMSNorm fused into the matmul's staging of x
+            bench(f"{tag}_norm_qkv", lambda: lib.rms_norm_quantized_matmul_multi(xh, nw, 1e-6, [W["q"], W["k"], W["v"]]),
+                  2 * M * (q + 2 * kv) * h, (q + 2 * kv) * h * bpp)
+            bench(f"{tag}_norm_gate_up", lambda: lib.rms_norm_quantized_matmul_swiglu(xh, nw, 1e-6, *W["g"], *W["u"]),
+                  4 * M * ff * h, 2 * ff * h * bpp)
     print(json.dumps({"kernels": rows, "peaks": peaks}), flush=True)
     return 0
 

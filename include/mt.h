@@ -173,6 +173,32 @@ int mt_quantized_matmul_multi(const void* x, const uint32_t* w0,
                               mt_stream_t stream);
 
 /*
+ * Decode regions with the RMSNorm before them fused in (M <= 4):
+ * y_i = quantized_matmul(rms_norm(x, norm_w, eps), w_i, ...) for up to three
+ * sets, and y = silu(qmm(xn, wg)) * qmm(xn, wu) with xn = rms_norm(x, ...).
+ * Same results as mt_rms_norm followed by mt_quantized_matmul_multi /
+ * mt_quantized_matmul_swiglu (the normalised rows are never written). They
+ * replace the rms_norm -> qkv and rms_norm -> gate/up region pairs of the
+ * reference's decoder-layer wrapper
+ * (examples/lfm2_5_1_2b_prefill/lfm2_5_1_2b_prefill_artifact/patch/wrappers.py:38-106)
+ * at decode, where the reference's cuts keep them apart. No workspace.
+ * MT_ERR_UNSUPPORTED when the shape needs more than the streamed decode
+ * kernel (M > 4, bits != 4, K > 16384, norm_w not 16-byte aligned).
+ */
+int mt_rms_norm_quantized_matmul_multi(
+    const void* x, const void* norm_w, float eps, const uint32_t* w0,
+    const void* s0, const void* b0, void* y0, int64_t N0, const uint32_t* w1,
+    const void* s1, const void* b1, void* y1, int64_t N1, const uint32_t* w2,
+    const void* s2, const void* b2, void* y2, int64_t N2, int64_t M, int64_t K,
+    int group_size, int bits, int dtype, mt_stream_t stream);
+
+int mt_rms_norm_quantized_matmul_swiglu(
+    const void* x, const void* norm_w, float eps, const uint32_t* wg,
+    const void* sg, const void* bg, const uint32_t* wu, const void* su,
+    const void* bu, void* y, int64_t M, int64_t N, int64_t K, int group_size,
+    int bits, int dtype, mt_stream_t stream);
+
+/*
  * Bytes of workspace the quantized-matmul entry points need for this shape.
  * `n_total` is the summed N over all sets (2N for the SwiGLU pair);
  * `kind` is 0 (plain/residual/multi) or 1 (SwiGLU pair).

@@ -89,6 +89,43 @@ def qwen3_specs(eps: float = 1e-6, rope_theta: float = 1e6, head_dim: int = 128)
             {"int": QMM_BITS}, {"dtype": "in0"}, _ws("2 * in1.shape[0]", 1), {"stream": True}]},
         output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",),
         fallback_predicate="in0.shape[1] % 64 != 0", reassociates=True))
+    # decode cuts with the RMSNorm before the matmul fused in (M <= 4, the
+    # streamed decode kernel's shapes); prefill takes rms_norm + the matmul
+    dec = f"in0.shape[0] > 4 or in0.shape[1] % {8 * QMM_GROUP} != 0 or in0.shape[1] > 16384"
+    S.append(KernelSpec(
+        kernel_id="rms_norm_qkv_qmm", name="mt_rms_norm_quantized_matmul_multi",
+        input_names=tuple(f"in{i}" for i in range(11)), output_names=("out0", "out1", "out2"),
+        cuda={"symbol": "mt_rms_norm_quantized_matmul_multi", "args": [
+            {"in": 0}, {"in": 1}, {"float": eps},
+            {"in": 2}, {"in": 3}, {"in": 4}, {"out": 0}, {"expr": "in2.shape[0]"},
+            {"in": 5}, {"in": 6}, {"in": 7}, {"out": 1}, {"expr": "in5.shape[0]"},
+            {"in": 8}, {"in": 9}, {"in": 10}, {"out": 2}, {"expr": "in8.shape[0]"},
+            {"expr": "in0.shape[0]"}, {"expr": "in0.shape[1]"}, {"int": QMM_GROUP}, {"int": QMM_BITS},
+            {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in2.shape[0]"), ("in0.shape[0]", "in5.shape[0]"),
+                       ("in0.shape[0]", "in8.shape[0]")),
+        output_dtypes=("in0", "in0", "in0"), fallback_predicate=dec, reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="rms_norm_gate_up_swiglu", name="mt_rms_norm_quantized_matmul_swiglu",
+        input_names=tuple(f"in{i}" for i in range(8)), output_names=("out0",),
+        cuda={"symbol": "mt_rms_norm_quantized_matmul_swiglu", "args": [
+            {"in": 0}, {"in": 1}, {"float": eps}, {"in": 2}, {"in": 3}, {"in": 4}, {"in": 5}, {"in": 6}, {"in": 7},
+            {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in2.shape[0]"}, {"expr": "in0.shape[1]"},
+            {"int": QMM_GROUP}, {"int": QMM_BITS}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in2.shape[0]"),), output_dtypes=("in0",), fallback_predicate=dec,
+        reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="rms_norm_lm_head", name="mt_rms_norm_quantized_matmul_multi",
+        input_names=("in0", "in1", "in2", "in3", "in4"), output_names=("out0",),
+        cuda={"symbol": "mt_rms_norm_quantized_matmul_multi", "args": [
+            {"in": 0}, {"in": 1}, {"float": eps},
+            {"in": 2}, {"in": 3}, {"in": 4}, {"out": 0}, {"expr": "in2.shape[0]"},
+            {"null": True}, {"null": True}, {"null": True}, {"null": True}, {"int": 0},
+            {"null": True}, {"null": True}, {"null": True}, {"null": True}, {"int": 0},
+            {"expr": "in0.shape[0]"}, {"expr": "in0.shape[1]"}, {"int": QMM_GROUP}, {"int": QMM_BITS},
+            {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in2.shape[0]"),), output_dtypes=("in0",), fallback_predicate=dec,
+        reassociates=True))
     S.append(KernelSpec(
         kernel_id="quantized_embedding", name="mt_quantized_embedding", input_names=("in0", "in1", "in2", "in3"),
         output_names=("out0",),
@@ -118,8 +155,8 @@ def qwen3_specs(eps: float = 1e-6, rope_theta: float = 1e6, head_dim: int = 128)
 
 
 LAYER_KERNELS = ["rms_norm", "qkv_qmm", "qk_norm_rope_cache", "sdpa_causal_gqa", "o_proj_residual",
-                 "gate_up_swiglu", "down_proj_residual"]
-ROOT_KERNELS = ["quantized_embedding", "rms_norm", "lm_head", "logits_pick"]
+                 "gate_up_swiglu", "down_proj_residual", "rms_norm_qkv_qmm", "rms_norm_gate_up_swiglu"]
+ROOT_KERNELS = ["quantized_embedding", "rms_norm", "lm_head", "logits_pick", "rms_norm_lm_head"]
 
 
 def write_qwen3_bundle(directory: str | Path, n_layers: int) -> Path:

@@ -7,6 +7,11 @@ predicate covers the call (None), the wrapper runs that region's original
 ops from the wrapped module. Fallbacks are counted on the wrapper; with
 MT_STRICT_REGIONS=1 a fallback raises instead, so a benchmark can prove every
 region ran on its kernel.
+
+At decode (at most 4 tokens) the RMSNorm and the matmul after it run as one
+fused cut (rms_norm_qkv_qmm, rms_norm_gate_up_swiglu, rms_norm_lm_head); its
+predicate sends prefill shapes to the two-region path, which is not a
+fallback.
 """
 import os
 
@@ -33,13 +38,18 @@ class _Counting(ReplayWrapper):
             object.__setattr__(self, "fallbacks", self.fallbacks + 1)
         return out
 
+    def _fused(self, kid, inputs):
+        """The fused decode cut, or None when its predicate sends these shapes
+        to the unfused regions."""
+        return _kernels.try_call(self._specs[kid], inputs)
+
 
 class W_qwen3_layer(_Counting):
     """One decoder layer: rms_norm | qkv | q/k norm + rope + cache | sdpa |
     o_proj + residual | rms_norm | gate/up + swiglu | down + residual."""
 
     KERNEL_IDS = ["rms_norm", "qkv_qmm", "qk_norm_rope_cache", "sdpa_causal_gqa", "o_proj_residual",
-                  "gate_up_swiglu", "down_proj_residual"]
+                  "gate_up_swiglu", "down_proj_residual", "rms_norm_qkv_qmm", "rms_norm_gate_up_swiglu"]
 
     def __init__(self, wrapped, specs=None):
         super().__init__(wrapped, specs)
@@ -63,20 +73,28 @@ class W_qwen3_layer(_Counting):
         a, m = L.self_attn, L.mlp
         T = h.shape[0]
         off = cache.offset
-        r = self._call("rms_norm", [h, W["in_norm"]])
-        xn = r[0] if r is not None else L.input_layernorm(h)
-        r = self._call("qkv_qmm", [xn, *W["qkv"]])
-        q, k, v = r if r is not None else a.qkv(xn)
+        r = self._fused("rms_norm_qkv_qmm", [h, W["in_norm"], *W["qkv"]])
+        if r is None:
+            r = self._call("rms_norm", [h, W["in_norm"]])
+            xn = r[0] if r is not None else L.input_layernorm(h)
+            r = self._call("qkv_qmm", [xn, *W["qkv"]])
+            if r is None:
+                r = a.qkv(xn)
+        q, k, v = r
         r = self._call("qk_norm_rope_cache", [q, k, v, *W["qk_norm"], cache.k, cache.v], {"offset": off})
         qh = r[0] if r is not None else a.prologue(q, k, v, cache)
         r = self._call("sdpa_causal_gqa", [qh, cache.k, cache.v], {"offset": off, "kv_len": off + T})
         o = r[0] if r is not None else a.attend(qh, cache, off + T)
         r = self._call("o_proj_residual", [o, *W["o"], h])
         h2 = r[0] if r is not None else h + a.o_proj(o)
-        r = self._call("rms_norm", [h2, W["post_norm"]])
-        xn2 = r[0] if r is not None else L.post_attention_layernorm(h2)
-        r = self._call("gate_up_swiglu", [xn2, *W["gate_up"]])
-        act = r[0] if r is not None else m.gate_up(xn2)
+        r = self._fused("rms_norm_gate_up_swiglu", [h2, W["post_norm"], *W["gate_up"]])
+        if r is None:
+            r = self._call("rms_norm", [h2, W["post_norm"]])
+            xn2 = r[0] if r is not None else L.post_attention_layernorm(h2)
+            r = self._call("gate_up_swiglu", [xn2, *W["gate_up"]])
+            if r is None:
+                r = [m.gate_up(xn2)]
+        act = r[0]
         r = self._call("down_proj_residual", [act, *W["down"], h2])
         return r[0] if r is not None else h2 + m.down_proj(act)
 
@@ -85,7 +103,7 @@ class W_qwen3_root(_Counting):
     """Embedding gather, the (wrapped) layers, final norm on the last row,
     tied lm_head and the greedy pick (mlx-lm generate_step)."""
 
-    KERNEL_IDS = ["quantized_embedding", "rms_norm", "lm_head", "logits_pick"]
+    KERNEL_IDS = ["quantized_embedding", "rms_norm", "lm_head", "logits_pick", "rms_norm_lm_head"]
 
     def forward(self, tokens, cache):
         M = self.wrapped
@@ -98,10 +116,14 @@ class W_qwen3_root(_Counting):
         for c in cache.layers:
             c.offset += T
         last = h[-1:]
-        r = self._call("rms_norm", [last, M.norm.weight])
-        xn = r[0] if r is not None else M.norm(last)
-        r = self._call("lm_head", [xn, E.weight, E.scales, E.biases])
-        logits = r[0] if r is not None else E.as_linear(xn)
+        r = self._fused("rms_norm_lm_head", [last, M.norm.weight, E.weight, E.scales, E.biases])
+        if r is None:
+            r = self._call("rms_norm", [last, M.norm.weight])
+            xn = r[0] if r is not None else M.norm(last)
+            r = self._call("lm_head", [xn, E.weight, E.scales, E.biases])
+            if r is None:
+                r = [E.as_linear(xn)]
+        logits = r[0]
         r = self._call("logits_pick", [logits])
         if r is None:
             lse = torch.logsumexp(logits.float(), dim=-1, keepdim=True)

@@ -142,6 +142,65 @@ int mt_quantized_matmul_multi(const void* x, const uint32_t* w0, const void* s0,
   return run(r, (cudaStream_t)stream, "mt_quantized_matmul_multi");
 }
 
+// RMSNorm fused into the decode matmul's staging of x (M <= 4): every CTA of
+// the streamed kernel normalises the rows it stages, so no normalised copy of
+// x is written.
+static int run_normed(QmmRequest& r, const void* norm_w, float eps, cudaStream_t stream, const char* who) {
+  clear_error();
+  MT_CHECK_ARG(norm_w, "%s: norm weight is NULL", who);
+  MT_CHECK_ARG(aligned(norm_w, 16), "%s: norm weight must be 16-byte aligned", who);
+  MT_CHECK_ARG(eps >= 0.f, "%s: eps=%g", who, static_cast<double>(eps));
+  r.norm_w = norm_w;
+  r.norm_eps = eps;
+  const int rc = check_common(r, who);
+  if (rc != MT_OK) return rc;
+  if (r.M == 0) return MT_OK;
+  if (!qmv_stream_eligible(r)) {
+    set_error("%s: needs the streamed decode kernel (M <= 4, 4-bit, bf16/f16, K <= 16384; M=%lld bits=%d)", who,
+              (long long)r.M, r.bits);
+    return MT_ERR_UNSUPPORTED;
+  }
+  return qmv_stream_run(r, stream);
+}
+
+int mt_rms_norm_quantized_matmul_multi(const void* x, const void* norm_w, float eps, const uint32_t* w0,
+                                       const void* s0, const void* b0, void* y0, int64_t N0, const uint32_t* w1,
+                                       const void* s1, const void* b1, void* y1, int64_t N1, const uint32_t* w2,
+                                       const void* s2, const void* b2, void* y2, int64_t N2, int64_t M, int64_t K,
+                                       int group_size, int bits, int dtype, mt_stream_t stream) {
+  QmmRequest r = {};
+  r.x = x;
+  r.set[0] = {w0, s0, b0, y0, N0};
+  r.set[1] = {w1, s1, b1, y1, N1};
+  r.set[2] = {w2, s2, b2, y2, N2};
+  r.M = M;
+  r.K = K;
+  r.group = group_size;
+  r.bits = bits;
+  r.dtype = dtype;
+  r.kind = QMM_PLAIN;
+  MT_CHECK_ARG(N0 >= 0 && N1 >= 0 && N2 >= 0, "mt_rms_norm_quantized_matmul_multi: negative N");
+  return run_normed(r, norm_w, eps, (cudaStream_t)stream, "mt_rms_norm_quantized_matmul_multi");
+}
+
+int mt_rms_norm_quantized_matmul_swiglu(const void* x, const void* norm_w, float eps, const uint32_t* wg,
+                                        const void* sg, const void* bg, const uint32_t* wu, const void* su,
+                                        const void* bu, void* y, int64_t M, int64_t N, int64_t K, int group_size,
+                                        int bits, int dtype, mt_stream_t stream) {
+  QmmRequest r = {};
+  r.x = x;
+  r.set[0] = {wg, sg, bg, y, N};
+  r.set[1] = {wu, su, bu, nullptr, N};
+  r.M = M;
+  r.K = K;
+  r.group = group_size;
+  r.bits = bits;
+  r.dtype = dtype;
+  r.kind = QMM_SWIGLU;
+  MT_CHECK_ARG(N > 0, "mt_rms_norm_quantized_matmul_swiglu: N=%lld", (long long)N);
+  return run_normed(r, norm_w, eps, (cudaStream_t)stream, "mt_rms_norm_quantized_matmul_swiglu");
+}
+
 size_t mt_qmm_workspace_bytes(int64_t M, int64_t n_total, int64_t K, int bits, int kind) {
   if (M <= kQmvMaxRows) return 0;
   return qmm_tc_workspace(M, n_total, K, bits, kind);

@@ -24,6 +24,8 @@ struct QmmRequest {
   QmmKind kind;
   void* ws;
   size_t ws_bytes;
+  const void* norm_w;  // non-NULL: x is first RMS-normalised with this weight (decode only)
+  float norm_eps;
 };
 
 int qmv_run(const QmmRequest& r, cudaStream_t stream);

@@ -59,17 +59,21 @@ struct QsParams {
   int max_rows;      // stream rows of one CTA, upper bound (SwiGLU row sums)
   int spr;           // rows a stage can touch: 16 KB / row bytes + 2
   int stage_sc;      // 1: scales and biases travel with each stage; 0: copied once up front
+  const void* norm_w;  // non-NULL: stage rms_norm(x, norm_w, eps) instead of x
+  float eps;
 };
 
 // Byte offsets of the shared-memory regions (host and device agree on them).
 // A stage slot: 16 KB of the weight stream, then (stage_sc) the scales and
 // biases ([spr][G] each) of the rows those bytes belong to; without stage_sc
-// the CTA's scales and biases ([max_rows][G] each) follow the ring.
+// the CTA's scales and biases ([max_rows][G] each) follow the ring. With a
+// fused RMSNorm the norm weight row (K values) and the M row scales follow.
 struct QsLayout {
-  int slot, sc, sbs, sbb, xs, xsum, gsum, bars, total;
+  int slot, sc, sbs, sbb, xs, xsum, gsum, gw, rs, bars, total;
 };
 
-__host__ __device__ inline QsLayout qs_layout(int K, int G, int max_rows, int spr, int MR, int NST, int stage_sc) {
+__host__ __device__ inline QsLayout qs_layout(int K, int G, int max_rows, int spr, int MR, int NST, int stage_sc,
+                                              bool norm) {
   QsLayout l;
   l.sc = kQsStageBytes;  // G*2 is a multiple of 16
   l.slot = stage_sc ? (kQsStageBytes + 2 * spr * G * 2 + 127) & ~127 : kQsStageBytes;
@@ -78,9 +82,18 @@ __host__ __device__ inline QsLayout qs_layout(int K, int G, int max_rows, int sp
   l.xs = l.sbb + (stage_sc ? 0 : max_rows * G * 2);
   l.xsum = l.xs + MR * K * 2;
   l.gsum = l.xsum + MR * (K / 32) * 4;
-  l.bars = (l.gsum + max_rows * MR * 4 + 15) & ~15;
+  l.gw = (l.gsum + max_rows * MR * 4 + 15) & ~15;
+  l.rs = l.gw + (norm ? K * 2 : 0);
+  l.bars = l.rs + (norm ? 16 : 0);
   l.total = l.bars + (2 * kQsMaxStages + 2) * 8;
   return l;
+}
+
+// x_{8q..8q+7} as loaded (pairs (0,1) (2,3) (4,5) (6,7)) regrouped to the
+// pairs (i, i+4), i = 0..3
+__device__ __forceinline__ uint4 qs_regroup(uint4 raw) {
+  return make_uint4(__byte_perm(raw.x, raw.z, 0x5410), __byte_perm(raw.x, raw.z, 0x7632),
+                    __byte_perm(raw.y, raw.w, 0x5410), __byte_perm(raw.y, raw.w, 0x7632));
 }
 
 // 16-byte slot of (unit c, word wi) of one staged x row, holding the pairs
@@ -120,7 +133,8 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   const int K = p.K, G = p.G, NST = p.NST;
   const int rowB = K / 2;   // packed bytes per row
   const int rowU = K / 32;  // 16-byte units per row
-  const QsLayout L = qs_layout(K, G, p.max_rows, p.spr, MR, NST, p.stage_sc);
+  const bool norm = p.norm_w != nullptr;
+  const QsLayout L = qs_layout(K, G, p.max_rows, p.spr, MR, NST, p.stage_sc, norm);
   uint8_t* ring = smem;
   T* sbS = reinterpret_cast<T*>(smem + L.sbs);
   T* sbB = reinterpret_cast<T*>(smem + L.sbb);
@@ -251,6 +265,8 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   griddep_wait();
   griddep_launch();  // dependents may launch now; their own wait covers this grid
   const T* x = static_cast<const T*>(p.x);
+  uint4* gw = reinterpret_cast<uint4*>(smem + L.gw);  // norm weight words, regrouped like x
+  float* rscale = reinterpret_cast<float*>(smem + L.rs);
   // x as element-type pairs (x_{8wi+i}, x_{8wi+i+4}), one 16-byte slot per
   // (unit, word), and the fp32 sum of every unit
   for (int i = ct; i < MR * (K / 8); i += kQsConsumerWarps * 32) {
@@ -259,27 +275,63 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
     if (m < p.M) {
       const uint4 raw = *reinterpret_cast<const uint4*>(x + static_cast<long long>(m) * p.ldx + 8 * q);
       // raw holds x_{8q..8q+7} as pairs (0,1) (2,3) (4,5) (6,7); regroup to (i, i+4)
-      v.x = __byte_perm(raw.x, raw.z, 0x5410);
-      v.y = __byte_perm(raw.x, raw.z, 0x7632);
-      v.z = __byte_perm(raw.y, raw.w, 0x5410);
-      v.w = __byte_perm(raw.y, raw.w, 0x7632);
+      v = qs_regroup(raw);
     }
+    if (norm && m == 0) gw[q] = qs_regroup(*reinterpret_cast<const uint4*>(static_cast<const T*>(p.norm_w) + 8 * q));
     xs[m * (K / 8) + qs_xs_index(q >> 2, q & 3)] = v;
   }
   named_barrier(kQsConsumerBar, kQsConsumerWarps * 32);
+  if (norm) {
+    // RMSNorm row scales: warp m sums the squares of row m in the order of the
+    // RMSNorm kernels (lane l: words l, l+32, ..., values 8q..8q+7 in turn),
+    // so the normalised x is bit-identical to theirs
+    if (warp < p.M) {
+      const uint4* xr = xs + warp * (K / 8);
+      float ss = 0.f;
+      for (int q = lane; q < K / 8; q += 32) {
+        const uint4 v = xr[qs_xs_index(q >> 2, q & 3)];
+        const uint32_t pr[4] = {v.x, v.y, v.z, v.w};
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 t = Elem<DT>::unpack2(*reinterpret_cast<const typename Elem<DT>::T2*>(&pr[e]));
+          f[e] = t.x;
+          f[e + 4] = t.y;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) rscale[warp] = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), p.eps));
+    }
+    named_barrier(kQsConsumerBar, kQsConsumerWarps * 32);
+  }
   for (int i = ct; i < MR * rowU; i += kQsConsumerWarps * 32) {
     const int m = i / rowU, u = i - m * rowU;
+    const bool nrm = norm && m < p.M;
+    const float sc = nrm ? rscale[m] : 0.f;
     float s = 0.f;
 #pragma unroll
     for (int wi = 0; wi < 4; ++wi) {
-      const uint4 v = xs[m * (K / 8) + qs_xs_index(u, wi)];
-      const uint32_t pr[4] = {v.x, v.y, v.z, v.w};
+      uint4* slotp = xs + m * (K / 8) + qs_xs_index(u, wi);
+      uint4 v = *slotp;
+      uint32_t pr[4] = {v.x, v.y, v.z, v.w};
+      const uint4 gv = nrm ? gw[4 * u + wi] : make_uint4(0, 0, 0, 0);
+      const uint32_t gp[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const typename Elem<DT>::T2 h = *reinterpret_cast<const typename Elem<DT>::T2*>(&pr[e]);
-        const float2 f = Elem<DT>::unpack2(h);
+        float2 f = Elem<DT>::unpack2(*reinterpret_cast<const typename Elem<DT>::T2*>(&pr[e]));
+        if (nrm) {
+          // y = (x * scale) * w rounded to the element type, as the RMSNorm kernels
+          const float2 g = Elem<DT>::unpack2(*reinterpret_cast<const typename Elem<DT>::T2*>(&gp[e]));
+          const typename Elem<DT>::T2 y =
+              Elem<DT>::pack2(__fmul_rn(__fmul_rn(f.x, sc), g.x), __fmul_rn(__fmul_rn(f.y, sc), g.y));
+          pr[e] = *reinterpret_cast<const uint32_t*>(&y);
+          f = Elem<DT>::unpack2(y);
+        }
         s += f.x + f.y;
       }
+      if (nrm) *slotp = make_uint4(pr[0], pr[1], pr[2], pr[3]);
     }
     xsum[i] = s;
   }
@@ -406,13 +458,14 @@ static QsGeometry qs_geometry(const QmmRequest& r, int sms) {
   g.spr = kQsStageBytes / static_cast<int>(r.K / 2) + 2;
   g.MR = r.M <= 1 ? 1 : r.M <= 2 ? 2 : 4;
   const int K = static_cast<int>(r.K), G = static_cast<int>(r.K / r.group);
+  const bool norm = r.norm_w != nullptr;
   g.NST = kQsMaxStages;
   // scales copied once when at least 4 stages fit next to them, else per stage
   for (g.stage_sc = 0; g.stage_sc < 2; ++g.stage_sc) {
     g.NST = kQsMaxStages;
-    while (g.NST > 4 && qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc).total + 128 > kQsSmemLimit)
+    while (g.NST > 4 && qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc, norm).total + 128 > kQsSmemLimit)
       --g.NST;
-    if (qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc).total + 128 <= kQsSmemLimit) return g;
+    if (qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc, norm).total + 128 <= kQsSmemLimit) return g;
   }
   g.NST = 0;
   return g;
@@ -423,6 +476,7 @@ bool qmv_stream_eligible(const QmmRequest& r) {
   if (r.dtype != MT_BF16 && r.dtype != MT_F16) return false;
   if (r.group != 32 && r.group != 64 && r.group != 128) return false;
   if (r.K % 32 != 0 || r.K > 16384 || !aligned(r.x, 16)) return false;
+  if (r.norm_w && !aligned(r.norm_w, 16)) return false;
   const int G = static_cast<int>(r.K / r.group);
   if ((G * 2) % 16 != 0) return false;  // scale rows must be 16-byte multiples for the bulk copies
   const int nsets = r.kind == QMM_SWIGLU ? 2 : 3;
@@ -438,7 +492,7 @@ bool qmv_stream_eligible(const QmmRequest& r) {
 
 template <int DT, int MR, int MODE>
 static int qs_launch(QsParams& p, cudaStream_t stream) {
-  const QsLayout L = qs_layout(p.K, p.G, p.max_rows, p.spr, MR, p.NST, p.stage_sc);
+  const QsLayout L = qs_layout(p.K, p.G, p.max_rows, p.spr, MR, p.NST, p.stage_sc, p.norm_w != nullptr);
   auto k = qmv_stream_kernel<DT, MR, MODE>;
   if (int e = ensure_smem(k, kQsSmemLimit)) return e;
   return launch(k, dim3(p.P), dim3(kQsThreads), static_cast<size_t>(L.total) + 128, stream, p);
@@ -457,6 +511,8 @@ int qmv_stream_run(const QmmRequest& r, cudaStream_t stream) {
   QsParams p = {};
   p.x = r.x;
   p.residual = r.residual;
+  p.norm_w = r.norm_w;
+  p.eps = r.norm_eps;
   p.M = static_cast<int>(r.M);
   p.K = static_cast<int>(r.K);
   p.G = static_cast<int>(r.K / r.group);

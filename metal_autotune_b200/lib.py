@@ -66,6 +66,10 @@ SIGNATURES = {
     "mt_quantized_matmul_swiglu": (C.c_int, [P, P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, SZ, P]),
     "mt_quantized_matmul_multi": (
         C.c_int, [P, P, P, P, P, I64, P, P, P, P, I64, P, P, P, P, I64, I64, I64, I32, I32, I32, P, SZ, P]),
+    "mt_rms_norm_quantized_matmul_multi": (
+        C.c_int, [P, P, F32, P, P, P, P, I64, P, P, P, P, I64, P, P, P, P, I64, I64, I64, I32, I32, I32, P]),
+    "mt_rms_norm_quantized_matmul_swiglu": (
+        C.c_int, [P, P, F32, P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P]),
     "mt_qmm_workspace_bytes": (C.c_size_t, [I64, I64, I64, I32, I32]),
     "mt_qmm_partition_check": (C.c_int, [I64, I32, I32, I32, P]),
     "mt_rms_norm": (C.c_int, [P, P, F32, P, I64, I64, I32, P]),
@@ -263,6 +267,38 @@ def quantized_matmul_multi(x, sets, *, group_size=64, bits=4, outs=None):
     call("mt_quantized_matmul_multi", _ptr(x), *args, M, K, group_size, bits, dtype_code(x.dtype), ws.ptr,
          ws.nbytes, _stream())
     return ys
+
+
+def rms_norm_quantized_matmul_multi(x, norm_w, eps, sets, *, group_size=64, bits=4, outs=None):
+    """Decode (M <= 4): quantized_matmul_multi(rms_norm(x, norm_w, eps), sets) in one launch."""
+    if not 1 <= len(sets) <= 3:
+        raise ValueError("one to three weight sets")
+    M, _, K = _qmm_common(x, sets[0][0], group_size, bits)
+    _dense(norm_w, "norm_w")
+    ys = []
+    args = []
+    for i in range(3):
+        if i < len(sets):
+            w, s, b = sets[i]
+            N = w.shape[0]
+            y = outs[i] if outs is not None else torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
+            ys.append(y)
+            args += [_ptr(w), _ptr(s), _ptr(b), _ptr(y), N]
+        else:
+            args += [None, None, None, None, 0]
+    call("mt_rms_norm_quantized_matmul_multi", _ptr(x), _ptr(norm_w), float(eps), *args, M, K, group_size, bits,
+         dtype_code(x.dtype), _stream())
+    return ys
+
+
+def rms_norm_quantized_matmul_swiglu(x, norm_w, eps, wg, sg, bg, wu, su, bu, *, group_size=64, bits=4, out=None):
+    """Decode (M <= 4): quantized_matmul_swiglu(rms_norm(x, norm_w, eps), ...) in one launch."""
+    M, N, K = _qmm_common(x, wg, group_size, bits)
+    _dense(norm_w, "norm_w")
+    y = out if out is not None else torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
+    call("mt_rms_norm_quantized_matmul_swiglu", _ptr(x), _ptr(norm_w), float(eps), _ptr(wg), _ptr(sg), _ptr(bg),
+         _ptr(wu), _ptr(su), _ptr(bu), _ptr(y), M, N, K, group_size, bits, dtype_code(x.dtype), _stream())
+    return y
 
 
 def rms_norm(x, w, eps, *, out=None):

@@ -215,7 +215,8 @@ def test_apply_bundle_installs_wrappers_on_tiny_qwen3():
     patched = apply(model, bundle)
     assert type(patched).__name__ == "W_qwen3_root"
     assert all(type(l).__name__ == "W_qwen3_layer" for l in patched.wrapped.layers)
-    assert set(patched._specs) == {"quantized_embedding", "rms_norm", "lm_head", "logits_pick"}
+    assert set(patched._specs) == {"quantized_embedding", "rms_norm", "lm_head", "logits_pick", "rms_norm_lm_head"}
+    assert "rms_norm_qkv_qmm" in patched.wrapped.layers[0]._specs
 
 
 # ------------------------------------------------------------ paired statistics
