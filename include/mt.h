@@ -248,6 +248,25 @@ int mt_qk_norm_rope_cache(const void* q, const void* k, const void* v,
                           int64_t offset, float rope_base, int dtype,
                           mt_stream_t stream);
 
+/*
+ * Decode (T <= 4 new tokens, (Hq/Hkv) * T <= 16): mt_qk_norm_rope_cache followed
+ * by causal GQA attention of the T rotated queries over the cache rows
+ * 0..offset+T-1, in one launch (one CTA per kv head). The caches receive the
+ * same rows as mt_qk_norm_rope_cache writes (bit-identical); o is
+ * [T, Hq*D] (heads concatenated per token, the layout of the layer's o_proj
+ * input). Replaces the qk_norm_rope_cache -> sdpa region pair of the
+ * decoder-layer wrapper (examples/lfm2_5_1_2b_prefill/.../patch/wrappers.py:
+ * 38-106) at decode; `scale` is the softmax scale (1/sqrt(D)).
+ */
+int mt_qk_norm_rope_sdpa_decode(const void* q, const void* k, const void* v,
+                                int64_t q_stride, int64_t kv_stride,
+                                const void* q_norm_w, const void* k_norm_w,
+                                float eps, void* o, void* k_cache,
+                                void* v_cache, int64_t T, int64_t Hq,
+                                int64_t Hkv, int64_t D, int64_t cache_cap,
+                                int64_t offset, float rope_base, float scale,
+                                int dtype, mt_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* a-5: SwiGLU                                                               */
 /* ------------------------------------------------------------------------ */

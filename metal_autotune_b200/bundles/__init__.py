@@ -70,6 +70,20 @@ def qwen3_specs(eps: float = 1e-6, rope_theta: float = 1e6, head_dim: int = 128)
             {"dtype": "in0"}, {"stream": True}]},
         output_shapes=(("in0.shape[1]", "in0.shape[0] * in0.shape[2]"),), output_dtypes=("in0",),
         fallback_predicate="in0.shape[2] != 128 and in0.shape[2] != 64", reassociates=True))
+    # decode: the q/k-norm + rope + cache prologue and the attention as one cut
+    S.append(KernelSpec(
+        kernel_id="qk_norm_rope_sdpa_decode", name="mt_qk_norm_rope_sdpa_decode",
+        input_names=tuple(f"in{i}" for i in range(7)), output_names=("out0",),
+        cuda={"symbol": "mt_qk_norm_rope_sdpa_decode", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"expr": "in0.shape[1]"}, {"expr": "in1.shape[1]"}, {"in": 3},
+            {"in": 4}, {"float": eps}, {"out": 0}, {"in": 5}, {"in": 6}, {"expr": "in0.shape[0]"},
+            {"expr": f"in0.shape[1] // {head_dim}"}, {"expr": f"in1.shape[1] // {head_dim}"}, {"int": head_dim},
+            {"expr": "in5.shape[1]"}, {"scalar": "offset"}, {"float": rope_theta},
+            {"float": 1.0 / math.sqrt(head_dim)}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]"),), output_dtypes=("in0",),
+        fallback_predicate=(f"in0.shape[0] > 4 or in0.shape[1] % {head_dim} != 0 or in5.shape[2] != {head_dim} or "
+                            f"(in0.shape[1] // in1.shape[1]) * in0.shape[0] > 16"),
+        reassociates=True))
     for kid in ("o_proj_residual", "down_proj_residual"):
         S.append(KernelSpec(
             kernel_id=kid, name="mt_quantized_matmul_residual", input_names=tuple(f"in{i}" for i in range(5)),
@@ -155,7 +169,8 @@ def qwen3_specs(eps: float = 1e-6, rope_theta: float = 1e6, head_dim: int = 128)
 
 
 LAYER_KERNELS = ["rms_norm", "qkv_qmm", "qk_norm_rope_cache", "sdpa_causal_gqa", "o_proj_residual",
-                 "gate_up_swiglu", "down_proj_residual", "rms_norm_qkv_qmm", "rms_norm_gate_up_swiglu"]
+                 "gate_up_swiglu", "down_proj_residual", "rms_norm_qkv_qmm", "rms_norm_gate_up_swiglu",
+                 "qk_norm_rope_sdpa_decode"]
 ROOT_KERNELS = ["quantized_embedding", "rms_norm", "lm_head", "logits_pick", "rms_norm_lm_head"]
 
 

@@ -9,8 +9,9 @@ MT_STRICT_REGIONS=1 a fallback raises instead, so a benchmark can prove every
 region ran on its kernel.
 
 At decode (at most 4 tokens) the RMSNorm and the matmul after it run as one
-fused cut (rms_norm_qkv_qmm, rms_norm_gate_up_swiglu, rms_norm_lm_head); its
-predicate sends prefill shapes to the two-region path, which is not a
+fused cut (rms_norm_qkv_qmm, rms_norm_gate_up_swiglu, rms_norm_lm_head), and
+the attention prologue and attention as one (qk_norm_rope_sdpa_decode); their
+predicates send prefill shapes to the two-region path, which is not a
 fallback.
 """
 import os
@@ -49,7 +50,8 @@ class W_qwen3_layer(_Counting):
     o_proj + residual | rms_norm | gate/up + swiglu | down + residual."""
 
     KERNEL_IDS = ["rms_norm", "qkv_qmm", "qk_norm_rope_cache", "sdpa_causal_gqa", "o_proj_residual",
-                  "gate_up_swiglu", "down_proj_residual", "rms_norm_qkv_qmm", "rms_norm_gate_up_swiglu"]
+                  "gate_up_swiglu", "down_proj_residual", "rms_norm_qkv_qmm", "rms_norm_gate_up_swiglu",
+                  "qk_norm_rope_sdpa_decode"]
 
     def __init__(self, wrapped, specs=None):
         super().__init__(wrapped, specs)
@@ -81,10 +83,15 @@ class W_qwen3_layer(_Counting):
             if r is None:
                 r = a.qkv(xn)
         q, k, v = r
-        r = self._call("qk_norm_rope_cache", [q, k, v, *W["qk_norm"], cache.k, cache.v], {"offset": off})
-        qh = r[0] if r is not None else a.prologue(q, k, v, cache)
-        r = self._call("sdpa_causal_gqa", [qh, cache.k, cache.v], {"offset": off, "kv_len": off + T})
-        o = r[0] if r is not None else a.attend(qh, cache, off + T)
+        r = _kernels.try_call(self._specs["qk_norm_rope_sdpa_decode"], [q, k, v, *W["qk_norm"], cache.k, cache.v],
+                              scalars={"offset": off})
+        if r is None:
+            r = self._call("qk_norm_rope_cache", [q, k, v, *W["qk_norm"], cache.k, cache.v], {"offset": off})
+            qh = r[0] if r is not None else a.prologue(q, k, v, cache)
+            r = self._call("sdpa_causal_gqa", [qh, cache.k, cache.v], {"offset": off, "kv_len": off + T})
+            if r is None:
+                r = [a.attend(qh, cache, off + T)]
+        o = r[0]
         r = self._call("o_proj_residual", [o, *W["o"], h])
         h2 = r[0] if r is not None else h + a.o_proj(o)
         r = self._fused("rms_norm_gate_up_swiglu", [h2, W["post_norm"], *W["gate_up"]])

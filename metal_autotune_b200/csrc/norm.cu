@@ -10,6 +10,7 @@
 // Products that the oracle computes without contraction use __fmul_rn /
 // __fadd_rn so the GPU and the CPU restatement round identically.
 #include "mt_common.cuh"
+#include "rope_common.cuh"
 
 namespace mt {
 
@@ -204,16 +205,6 @@ __global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict_
   }
 }
 
-struct RopeFreqs {
-  float inv_freq[128];  // base^(-2j/dims), j < dims/2, computed on the host in double
-};
-
-__device__ __forceinline__ void rope_pair(float a, float b, float c, float s, float& oa, float& ob) {
-  // first = a*c - b*s, second = b*c + a*s  (autotuner/scaffold/lower.py:1279)
-  oa = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-  ob = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
-}
-
 // x, y: [B*H, L, D]; one thread per (row, pair j < dims/2) plus tail copies.
 template <int DT>
 __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, void* __restrict__ yp,
@@ -269,52 +260,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
   const T* src = is_q ? static_cast<const T*>(qp) + t * q_stride + h * 128
                       : static_cast<const T*>(kp) + t * kv_stride + h * 128;
   const T* nw = static_cast<const T*>(is_q ? qwp : kwp);
-  // 4 values per lane: d = 4*lane .. 4*lane+3; a k head's v row is loaded
-  // together with the k row (one memory round trip)
+  // a k head's v row is loaded together with the k row (one memory round trip)
   uint2 vrow = make_uint2(0, 0);
   if (!is_q) vrow = *reinterpret_cast<const uint2*>(static_cast<const T*>(vp) + t * kv_stride + h * 128 + 4 * lane);
-  float v[4], g[4];
-  {
-    const uint2 u = *reinterpret_cast<const uint2*>(src + 4 * lane);
-    const T* e = reinterpret_cast<const T*>(&u);
-    const uint2 uw = *reinterpret_cast<const uint2*>(nw + 4 * lane);
-    const T* ew = reinterpret_cast<const T*>(&uw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[i] = Elem<DT>::to_f(e[i]);
-      g[i] = Elem<DT>::to_f(ew[i]);
-    }
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
-  ss = warp_sum(ss);
-  const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, 128.f), eps));
-  float n[4], p[4], o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) n[i] = round_to<DT>(__fmul_rn(__fmul_rn(v[i], scale), g[i]));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
-  const float pos = static_cast<float>(static_cast<int64_t>(t) + offset);
-  const bool first = lane < 16;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int j = (4 * lane + i) & 63;
-    float s, c;
-    sincosf(__fmul_rn(pos, f.inv_freq[j]), &s, &c);
-    float o0, o1;
-    if (first) {
-      rope_pair(n[i], p[i], c, s, o0, o1);
-      o[i] = o0;
-    } else {
-      rope_pair(p[i], n[i], c, s, o0, o1);
-      o[i] = o1;
-    }
-  }
-  uint2 out;
-  T* eo = reinterpret_cast<T*>(&out);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) eo[i] = Elem<DT>::from_f(o[i]);
+  const uint2 out = qk_norm_rope_row<DT>(src, nw, eps, static_cast<int64_t>(t) + offset, f, lane);
   if (is_q) {
     *reinterpret_cast<uint2*>(static_cast<T*>(qo) + (static_cast<int64_t>(h) * T_ + t) * 128 + 4 * lane) = out;
   } else {
@@ -322,13 +271,6 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
     *reinterpret_cast<uint2*>(static_cast<T*>(kc) + crow * 128 + 4 * lane) = out;
     *reinterpret_cast<uint2*>(static_cast<T*>(vc) + crow * 128 + 4 * lane) = vrow;
   }
-}
-
-static RopeFreqs make_freqs(int dims, double base) {
-  RopeFreqs f;
-  for (int j = 0; j < 128; ++j)
-    f.inv_freq[j] = j < dims / 2 ? static_cast<float>(pow(base, -2.0 * j / dims)) : 0.f;
-  return f;
 }
 
 }  // namespace mt

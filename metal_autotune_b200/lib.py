@@ -70,6 +70,8 @@ SIGNATURES = {
         C.c_int, [P, P, F32, P, P, P, P, I64, P, P, P, P, I64, P, P, P, P, I64, I64, I64, I32, I32, I32, P]),
     "mt_rms_norm_quantized_matmul_swiglu": (
         C.c_int, [P, P, F32, P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P]),
+    "mt_qk_norm_rope_sdpa_decode": (
+        C.c_int, [P, P, P, I64, I64, P, P, F32, P, P, P, I64, I64, I64, I64, I64, I64, F32, F32, I32, P]),
     "mt_qmm_workspace_bytes": (C.c_size_t, [I64, I64, I64, I32, I32]),
     "mt_qmm_partition_check": (C.c_int, [I64, I32, I32, I32, P]),
     "mt_rms_norm": (C.c_int, [P, P, F32, P, I64, I64, I32, P]),
@@ -347,6 +349,18 @@ def qk_norm_rope_cache(q, k, v, q_norm_w, k_norm_w, eps, q_out, k_cache, v_cache
     call("mt_qk_norm_rope_cache", _ptr(q), _ptr(k), _ptr(v), q.stride(0), k.stride(0), _ptr(q_norm_w),
          _ptr(k_norm_w), float(eps), _ptr(q_out), _ptr(k_cache), _ptr(v_cache), T, n_heads, n_kv_heads, head_dim,
          k_cache.shape[-2], int(offset), float(rope_base), dtype_code(q.dtype), _stream())
+
+
+def qk_norm_rope_sdpa_decode(q, k, v, q_norm_w, k_norm_w, eps, k_cache, v_cache, *, n_heads, n_kv_heads, offset,
+                             rope_base, scale, head_dim=128, out=None):
+    """Decode: qk_norm_rope_cache + causal GQA attention in one launch. q [T, Hq*D], k/v [T, Hkv*D]
+    rows; caches [Hkv, cap, D] get the new rows; returns o [T, Hq*D]."""
+    T = q.shape[0]
+    o = out if out is not None else torch.empty(T, n_heads * head_dim, dtype=q.dtype, device=q.device)
+    call("mt_qk_norm_rope_sdpa_decode", _ptr(q), _ptr(k), _ptr(v), q.stride(0), k.stride(0), _ptr(q_norm_w),
+         _ptr(k_norm_w), float(eps), _ptr(o), _ptr(k_cache), _ptr(v_cache), T, n_heads, n_kv_heads, head_dim,
+         k_cache.shape[-2], int(offset), float(rope_base), float(scale), dtype_code(q.dtype), _stream())
+    return o
 
 
 def swiglu(gate, up, *, out=None):
