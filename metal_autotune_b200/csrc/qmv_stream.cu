@@ -6,7 +6,7 @@
 // contiguous row range [c*R/P, (c+1)*R/P) of the output; the packed rows of
 // that range are one contiguous byte stream (rows of the same set are
 // adjacent in the MLX layout), which a producer warp copies into a ring of
-// 16 KB shared-memory stages with bulk copies. The CTA's scales and biases
+// 16-64 KB shared-memory stages with bulk copies. The CTA's scales and biases
 // are copied once up front; when they do not fit (row ranges of an lm_head),
 // each stage receives those of the rows it touches instead. Weights and
 // scales never depend
@@ -22,10 +22,11 @@
 // MLX qmv form): acc += scale * sum(x*q) + bias * sum(x), fp32. One logic op
 // turns nibbles i and i+4 of a packed word into the element-type pair
 // (C+q_i, C+q_{i+4}) (C = 128 for bf16, 1024 for fp16, both exact), and the
-// mixed-precision FMA (16-bit inputs, fp32 accumulator; one instruction on
-// sm_100) multiplies it with x staged as the matching pairs (x_i, x_{i+4}):
-// about two instructions per weight. Products are exact, the unit sum is
-// corrected by C * sum(x) with the unit sums of x precomputed once.
+// mixed-precision FMA (16-bit inputs, fp32 accumulator) multiplies it with x
+// staged as the matching pairs (x_i, x_{i+4}). Products are exact, the unit
+// sum is corrected by C * sum(x) with the unit sums of x precomputed once.
+// ncu (decode gate_up): 5.6 thread instructions per weight in all, ALU pipe
+// 54% and issue 62% active, DRAM 18%: issue-bound, not HBM-bound.
 #include "mt_common.cuh"
 #include "qmm_common.cuh"
 
@@ -33,8 +34,10 @@ namespace mt {
 
 constexpr int kQsConsumerWarps = 16;
 constexpr int kQsThreads = (kQsConsumerWarps + 1) * 32;  // + one producer warp
-constexpr int kQsStageBytes = 16384;
-constexpr int kQsStageUnits = kQsStageBytes / 16;
+// Ring stage sizes tried largest first: fewer, larger stages mean fewer
+// full/empty hand-offs per row walker (measured on B200, M = 1, K = 2560:
+// gate_up 13.3 / 12.1 / 11.5 us with 16 / 32 / 48-64 KB stages; 8 KB: 16.4).
+constexpr int kQsStageSizes[4] = {65536, 49152, 32768, 16384};
 constexpr int kQsMaxStages = 8;
 constexpr int kQsMaxMR = 4;
 constexpr int kQsConsumerBar = 1;  // named barrier of the 512 consumer threads
@@ -59,14 +62,15 @@ struct QsParams {
   int P;             // CTAs
   int NST;           // stages in the ring
   int max_rows;      // stream rows of one CTA, upper bound (SwiGLU row sums)
-  int spr;           // rows a stage can touch: 16 KB / row bytes + 2
+  int spr;           // rows a stage can touch: stage bytes / row bytes + 2
   int stage_sc;      // 1: scales and biases travel with each stage; 0: copied once up front
+  int stage_bytes;   // bytes of the weight stream per ring stage (a multiple of 16 KB)
   const void* norm_w;  // non-NULL: stage rms_norm(x, norm_w, eps) instead of x
   float eps;
 };
 
 // Byte offsets of the shared-memory regions (host and device agree on them).
-// A stage slot: 16 KB of the weight stream, then (stage_sc) the scales and
+// A stage slot: stage_bytes of the weight stream, then (stage_sc) the scales and
 // biases ([spr][G] each) of the rows those bytes belong to; without stage_sc
 // the CTA's scales and biases ([max_rows][G] each) follow the ring. With a
 // fused RMSNorm the norm weight row (K values) and the M row scales follow.
@@ -75,10 +79,10 @@ struct QsLayout {
 };
 
 __host__ __device__ inline QsLayout qs_layout(int K, int G, int max_rows, int spr, int MR, int NST, int stage_sc,
-                                              bool norm) {
+                                              bool norm, int stage_bytes) {
   QsLayout l;
-  l.sc = kQsStageBytes;  // G*2 is a multiple of 16
-  l.slot = stage_sc ? (kQsStageBytes + 2 * spr * G * 2 + 127) & ~127 : kQsStageBytes;
+  l.sc = stage_bytes;  // G*2 is a multiple of 16
+  l.slot = stage_sc ? (stage_bytes + 2 * spr * G * 2 + 127) & ~127 : stage_bytes;
   l.sbs = NST * l.slot;
   l.sbb = l.sbs + (stage_sc ? 0 : max_rows * G * 2);
   l.xs = l.sbb + (stage_sc ? 0 : max_rows * G * 2);
@@ -139,7 +143,8 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   const int rowB = K / 2;   // packed bytes per row
   const int rowU = K / 32;  // 16-byte units per row
   const bool norm = p.norm_w != nullptr;
-  const QsLayout L = qs_layout(K, G, p.max_rows, p.spr, MR, NST, p.stage_sc, norm);
+  const QsLayout L = qs_layout(K, G, p.max_rows, p.spr, MR, NST, p.stage_sc, norm, p.stage_bytes);
+  const int stage_bytes = p.stage_bytes, stage_units = p.stage_bytes / 16;
   uint8_t* ring = smem;
   T* sbS = reinterpret_cast<T*>(smem + L.sbs);
   T* sbB = reinterpret_cast<T*>(smem + L.sbb);
@@ -185,7 +190,7 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   }
   const int srows = seg_n[0] + seg_n[1] + seg_n[2];
   const int total_units = srows * rowU;
-  const int nstage = (total_units + kQsStageUnits - 1) / kQsStageUnits;
+  const int nstage = (total_units + stage_units - 1) / stage_units;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kQsMaxStages; ++i) {
@@ -219,8 +224,8 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
       for (int k = 0; k < nstage; ++k) {
         const int slot = k % NST;
         if (k >= NST && !mbar_wait(&empty[slot], ((k / NST) - 1) & 1, abort_flag, 0x501)) break;
-        long long off = static_cast<long long>(k) * kQsStageBytes;
-        const long long end = (off + kQsStageBytes < total) ? off + kQsStageBytes : total;
+        long long off = static_cast<long long>(k) * stage_bytes;
+        const long long end = (off + stage_bytes < total) ? off + stage_bytes : total;
         // stream rows [r_first, r_last] touched by this stage: their scales and biases
         const int r_first = p.stage_sc ? static_cast<int>(off) / rowB : 0;
         const int r_last = p.stage_sc ? static_cast<int>(end - 1) / rowB : -1;
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
           if (off < seg0 + seg_bytes) {
             const long long n = ((seg0 + seg_bytes) < end ? (seg0 + seg_bytes) : end) - off;
             const uint8_t* src = p.set[seg_set[sg]].w + static_cast<long long>(seg_row[sg]) * rowB + (off - seg0);
-            bulk_load_hint(dst + (off - static_cast<long long>(k) * kQsStageBytes), src, static_cast<uint32_t>(n),
+            bulk_load_hint(dst + (off - static_cast<long long>(k) * stage_bytes), src, static_cast<uint32_t>(n),
                            &full[slot], pol);
             off += n;
           }
@@ -353,10 +358,10 @@ __global__ void __launch_bounds__(kQsThreads, 1) qmv_stream_kernel(const __grid_
   for (int k = 0; ok && k < nstage; ++k) {
     const int slot = k % NST;
     if (!mbar_wait_warp(&full[slot], (k / NST) & 1, abort_flag, 0x503)) break;
-    const int u_lo = k * kQsStageUnits;
-    const int u_hi = (u_lo + kQsStageUnits < total_units) ? u_lo + kQsStageUnits : total_units;
+    const int u_lo = k * stage_units;
+    const int u_hi = (u_lo + stage_units < total_units) ? u_lo + stage_units : total_units;
     const uint8_t* stage = ring + slot * L.slot;
-    const int r_first = p.stage_sc ? (k * kQsStageBytes) / rowB : 0;  // stream offsets fit 32 bits
+    const int r_first = p.stage_sc ? (k * stage_bytes) / rowB : 0;  // stream offsets fit 32 bits
     // scale rows: the stage's own ([spr][G] from stream row r_first) or the CTA's
     const T* stS = p.stage_sc ? reinterpret_cast<const T*>(stage + L.sc) : sbS;
     const T* stB = p.stage_sc ? stS + p.spr * G : sbB;
@@ -450,12 +455,14 @@ static int qs_max_rows(int rows, int P, int mode) {
 }
 
 struct QsGeometry {
-  int mode, rows, P, max_rows, spr, MR, NST, stage_sc;
+  int mode, rows, P, max_rows, spr, MR, NST, stage_sc, stage_bytes;
 };
 
-// Grid and ring depth of a request; NST = 0 when at least 4 stages do not fit
-// next to the CTA's scales, biases and staged x (then the register-streaming
-// qmv kernel serves the request).
+// Grid, stage size and ring depth of a request: the largest stage size whose
+// ring of at least 3 stages (4 at 16 KB) fits next to the CTA's scales,
+// biases and staged x, scales copied once when they fit, else per stage;
+// NST = 0 when nothing fits (then the register-streaming qmv kernel serves
+// the request).
 static QsGeometry qs_geometry(const QmmRequest& r, int sms) {
   QsGeometry g = {};
   g.mode = r.kind == QMM_SWIGLU ? 2 : r.kind == QMM_RESIDUAL ? 1 : 0;
@@ -463,17 +470,20 @@ static QsGeometry qs_geometry(const QmmRequest& r, int sms) {
   if (g.rows <= 0) return g;
   g.P = g.rows < sms ? g.rows : sms;
   g.max_rows = qs_max_rows(g.rows, g.P, g.mode);
-  g.spr = kQsStageBytes / static_cast<int>(r.K / 2) + 2;
   g.MR = r.M <= 1 ? 1 : r.M <= 2 ? 2 : 4;
   const int K = static_cast<int>(r.K), G = static_cast<int>(r.K / r.group);
   const bool norm = r.norm_w != nullptr;
-  g.NST = kQsMaxStages;
-  // scales copied once when at least 4 stages fit next to them, else per stage
-  for (g.stage_sc = 0; g.stage_sc < 2; ++g.stage_sc) {
-    g.NST = kQsMaxStages;
-    while (g.NST > 4 && qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc, norm).total + 128 > kQsSmemLimit)
-      --g.NST;
-    if (qs_layout(K, G, g.max_rows, g.spr, g.MR, g.NST, g.stage_sc, norm).total + 128 <= kQsSmemLimit) return g;
+  for (int sb : kQsStageSizes) {
+    g.stage_bytes = sb;
+    g.spr = sb / static_cast<int>(r.K / 2) + 2;
+    const int min_st = sb > 16384 ? 3 : 4;
+    for (g.stage_sc = 0; g.stage_sc < 2; ++g.stage_sc) {
+      auto fits = [&](int nst) {
+        return qs_layout(K, G, g.max_rows, g.spr, g.MR, nst, g.stage_sc, norm, sb).total + 128 <= kQsSmemLimit;
+      };
+      for (g.NST = kQsMaxStages; g.NST >= min_st; --g.NST)
+        if (fits(g.NST)) return g;
+    }
   }
   g.NST = 0;
   return g;
@@ -500,7 +510,7 @@ bool qmv_stream_eligible(const QmmRequest& r) {
 
 template <int DT, int MR, int MODE>
 static int qs_launch(QsParams& p, cudaStream_t stream) {
-  const QsLayout L = qs_layout(p.K, p.G, p.max_rows, p.spr, MR, p.NST, p.stage_sc, p.norm_w != nullptr);
+  const QsLayout L = qs_layout(p.K, p.G, p.max_rows, p.spr, MR, p.NST, p.stage_sc, p.norm_w != nullptr, p.stage_bytes);
   // half-warp rows up to 128 units (K <= 4096); longer rows keep whole warps,
   // since 32 walkers over long rows would span more stages than the ring holds
   // (measured at K = 2560: gate_up 14.8 -> 13.2 us; K = 9728: 8.6 -> 10.2 us)
@@ -551,6 +561,7 @@ int qmv_stream_run(const QmmRequest& r, cudaStream_t stream) {
   p.max_rows = g.max_rows;
   p.spr = g.spr;
   p.stage_sc = g.stage_sc;
+  p.stage_bytes = g.stage_bytes;
   p.NST = g.NST;
   if (r.dtype == MT_BF16) {
     if (mode == 2) return qs_dispatch_mr<MT_BF16, 2>(p, stream);
