@@ -449,6 +449,25 @@ def run_kernels(args, cfg):
                   2 * M * (q + 2 * kv) * h, (q + 2 * kv) * h * bpp)
             bench(f"{tag}_norm_gate_up", lambda: lib.rms_norm_quantized_matmul_swiglu(xh, nw, 1e-6, *W["g"], *W["u"]),
                   4 * M * ff * h, 2 * ff * h * bpp)
+    # attention regions: prefill prologue + sdpa (two launches), decode fused prologue + attention
+    D, Hq, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+    kc = torch.randn(Hkv, cfg.max_len, D, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(Hkv, cfg.max_len, D, device="cuda").to(torch.bfloat16)
+    qn = torch.ones(D, device="cuda", dtype=torch.bfloat16)
+    sc = 1.0 / math.sqrt(D)
+    qp = torch.randn(PROMPT, Hq * D, device="cuda").to(torch.bfloat16)
+    kp = torch.randn(PROMPT, Hkv * D, device="cuda").to(torch.bfloat16)
+    vp = torch.randn(PROMPT, Hkv * D, device="cuda").to(torch.bfloat16)
+    qh = torch.empty(Hq, PROMPT, D, device="cuda", dtype=torch.bfloat16)
+    bench("prefill_qk_norm_rope_cache", lambda: lib.qk_norm_rope_cache(
+        qp, kp, vp, qn, qn, cfg.eps, qh, kc, vc, n_heads=Hq, n_kv_heads=Hkv, offset=0, rope_base=cfg.rope_theta),
+        0, 2 * PROMPT * (Hq + 3 * Hkv) * D * 2)
+    bench("prefill_sdpa", lambda: lib.sdpa(qh[None], kc[None, :, :PROMPT], vc[None, :, :PROMPT], scale=sc,
+                                           causal=True, q_offset=0, out_layout="blhd"),
+          2 * Hq * PROMPT * PROMPT * D, 0)
+    bench("decode_attention", lambda: lib.qk_norm_rope_sdpa_decode(
+        qp[:1], kp[:1], vp[:1], qn, qn, cfg.eps, kc, vc, n_heads=Hq, n_kv_heads=Hkv, offset=PROMPT,
+        rope_base=cfg.rope_theta, scale=sc), 0, 2 * (PROMPT + 1) * Hkv * D * 2)
     print(json.dumps({"kernels": rows, "peaks": peaks}), flush=True)
     return 0
 

@@ -247,12 +247,26 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
     void* __restrict__ qo, void* __restrict__ kc, void* __restrict__ vc, int T_, int Hq, int Hkv,
     int64_t cap, int64_t offset, const __grid_constant__ RopeFreqs f) {
   using T = typename Elem<DT>::T;
+  // (sin, cos) of the CTA's token positions: its 8 rows span at most
+  // kRopeTok tokens, and each angle is computed once instead of once per head
+  constexpr int kRopeTok = 9;
+  __shared__ float2 sc_tab[kRopeTok][64];
   griddep_wait();
   griddep_launch();  // dependents may launch now; their own wait covers this grid
-  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
   const int heads = Hq + Hkv;
-  if (wid >= static_cast<int64_t>(T_) * heads) return;
+  const int64_t rows = static_cast<int64_t>(T_) * heads;
+  const int64_t w0 = static_cast<int64_t>(blockIdx.x) * 8;
+  const int t0 = static_cast<int>(w0 / heads);
+  const int ntok = static_cast<int>(((w0 + 7 < rows ? w0 + 7 : rows - 1) / heads)) - t0 + 1;
+  for (int i = threadIdx.x; i < ntok * 64; i += blockDim.x) {
+    float s, c;
+    rope_angle(static_cast<int64_t>(t0 + i / 64) + offset, f, i % 64, s, c);
+    sc_tab[i / 64][i % 64] = make_float2(s, c);
+  }
+  __syncthreads();
+  const int64_t wid = w0 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid >= rows) return;
   const int t = static_cast<int>(wid / heads);
   const int hh = static_cast<int>(wid % heads);
   const bool is_q = hh < Hq;
@@ -263,7 +277,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
   // a k head's v row is loaded together with the k row (one memory round trip)
   uint2 vrow = make_uint2(0, 0);
   if (!is_q) vrow = *reinterpret_cast<const uint2*>(static_cast<const T*>(vp) + t * kv_stride + h * 128 + 4 * lane);
-  const uint2 out = qk_norm_rope_row<DT>(src, nw, eps, static_cast<int64_t>(t) + offset, f, lane);
+  const float2* tab = sc_tab[t - t0];
+  const uint2 out = qk_norm_rope_vals<DT>(*reinterpret_cast<const uint2*>(src + 4 * lane),
+                                          *reinterpret_cast<const uint2*>(nw + 4 * lane), eps,
+                                          [&](int j, float& s, float& c) {
+                                            s = tab[j].x;
+                                            c = tab[j].y;
+                                          },
+                                          lane);
   if (is_q) {
     *reinterpret_cast<uint2*>(static_cast<T*>(qo) + (static_cast<int64_t>(h) * T_ + t) * 128 + 4 * lane) = out;
   } else {

@@ -26,14 +26,20 @@ __device__ __forceinline__ void rope_pair(float a, float b, float c, float s, fl
   ob = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
 }
 
+// sin and cos of the RoPE angle pos * inv_freq[j]: every caller derives them
+// from this one expression, so a table of them and a direct call agree bitwise
+__device__ __forceinline__ void rope_angle(int64_t pos, const RopeFreqs& f, int j, float& s, float& c) {
+  sincosf(__fmul_rn(static_cast<float>(pos), f.inv_freq[j]), &s, &c);
+}
+
 // One head row of 128 values, one warp: lane l holds values 4l..4l+3 (`u`,
 // and the norm weights in `uw`, as loaded). rms_norm(row, nw, eps) rounded to
 // the element type (mx.fast.rms_norm), then rope (non-traditional: pairs
-// (d, d+64)) at position `pos`, rounded. Returns the lane's 4 output values
-// packed (8 bytes).
-template <int DT>
-__device__ __forceinline__ uint2 qk_norm_rope_vals(const uint2 u, const uint2 uw, float eps, int64_t pos,
-                                                   const RopeFreqs& f, int lane) {
+// (d, d+64)) with the angles angle(j, s, c), j < 64, rounded. Returns the
+// lane's 4 output values packed (8 bytes).
+template <int DT, class Angle>
+__device__ __forceinline__ uint2 qk_norm_rope_vals(const uint2 u, const uint2 uw, float eps, const Angle& angle,
+                                                   int lane) {
   using T = typename Elem<DT>::T;
   float v[4], g[4];
   {
@@ -55,13 +61,12 @@ __device__ __forceinline__ uint2 qk_norm_rope_vals(const uint2 u, const uint2 uw
   for (int i = 0; i < 4; ++i) n[i] = round_to<DT>(__fmul_rn(__fmul_rn(v[i], scale), g[i]));
 #pragma unroll
   for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
-  const float fpos = static_cast<float>(pos);
   const bool first = lane < 16;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int j = (4 * lane + i) & 63;
     float s, c;
-    sincosf(__fmul_rn(fpos, f.inv_freq[j]), &s, &c);
+    angle(j, s, c);
     float o0, o1;
     if (first) {
       rope_pair(n[i], p[i], c, s, o0, o1);
@@ -78,12 +83,11 @@ __device__ __forceinline__ uint2 qk_norm_rope_vals(const uint2 u, const uint2 uw
   return out;
 }
 
-// qk_norm_rope_vals of the row at `src` with the weights at `nw`
+// qk_norm_rope_vals at position `pos`, the angles computed in place
 template <int DT>
-__device__ __forceinline__ uint2 qk_norm_rope_row(const typename Elem<DT>::T* src, const typename Elem<DT>::T* nw,
-                                                  float eps, int64_t pos, const RopeFreqs& f, int lane) {
-  return qk_norm_rope_vals<DT>(*reinterpret_cast<const uint2*>(src + 4 * lane),
-                               *reinterpret_cast<const uint2*>(nw + 4 * lane), eps, pos, f, lane);
+__device__ __forceinline__ uint2 qk_norm_rope_vals(const uint2 u, const uint2 uw, float eps, int64_t pos,
+                                                   const RopeFreqs& f, int lane) {
+  return qk_norm_rope_vals<DT>(u, uw, eps, [&](int j, float& s, float& c) { rope_angle(pos, f, j, s, c); }, lane);
 }
 
 }  // namespace mt
