@@ -80,3 +80,22 @@ def test_product_import_does_not_touch_the_oracle():
             "metal_autotune_b200.targets.qwen3; "
             "assert not any(m == 'oracle' or m.startswith('oracle.') for m in sys.modules), 'oracle imported'")
     subprocess.run([sys.executable, "-c", code], check=True, cwd=str(HEADER.parents[1]))
+
+
+def test_fused_decode_cuts_check_arguments_without_gpu(mt):
+    """The fused decode entry points refuse what only the unfused pair serves,
+    before any CUDA call: more than 4 tokens (attention), a missing or
+    misaligned norm weight (norm + matmul)."""
+    p = C.c_void_p(256)  # never dereferenced: the checks come first
+    rc = mt.mt_qk_norm_rope_sdpa_decode(p, p, p, 4096, 1024, p, p, 1e-6, p, p, p, 5, 32, 8, 128, 160, 0, 1e6,
+                                        0.088, 0, None)
+    assert rc == -1 and b"at most 4 tokens" in mt.mt_last_error_string()
+    rc = mt.mt_qk_norm_rope_sdpa_decode(p, p, p, 4096, 1024, p, p, 1e-6, p, p, p, 1, 32, 8, 128, 128, 128, 1e6,
+                                        0.088, 0, None)
+    assert rc == -1 and b"exceeds cache capacity" in mt.mt_last_error_string()
+    rc = mt.mt_rms_norm_quantized_matmul_multi(p, None, 1e-6, p, p, p, p, 256, None, None, None, None, 0, None, None,
+                                               None, None, 0, 1, 1024, 64, 4, 0, None)
+    assert rc == -1 and b"norm weight is NULL" in mt.mt_last_error_string()
+    rc = mt.mt_rms_norm_quantized_matmul_swiglu(p, C.c_void_p(258), 1e-6, p, p, p, p, p, p, p, 1, 256, 1024, 64, 4,
+                                                0, None)
+    assert rc == -1 and b"16-byte aligned" in mt.mt_last_error_string()
