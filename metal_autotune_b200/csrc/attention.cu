@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kDaWarps * 32, 1)
     }
     cp_async_commit();
   };
-  // the first round of blocks (one per warp) is fetched while the prologue runs
+  // the first pass of blocks (one per warp) is fetched while the prologue runs
   if (warp < nkb) load_block(warp, true);
 
   // prologue: items i = warp, warp + 8, ... over the R q rows, then the T
@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(kDaWarps * 32, 1)
       *reinterpret_cast<uint2*>(static_cast<T*>(p.v_cache) + crow * kDaD + 4 * lane) = vr[j];
       const int kb = key / kDaKeys;
       if (kb < kDaWarps) {
-        // the block is in the first round: straight into its warp's buffers
+        // the block is in the first pass: straight into its warp's buffers
         uint8_t* bk = skv + kb * kDaWarpKV;
         const int r = key - kb * kDaKeys;
         *reinterpret_cast<uint2*>(bk + swz<kDaD>(r, lane >> 1) + (lane & 1) * 8) = kr;
@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kDaWarps * 32, 1)
   }
   for (int i = R + warp; i < 16; i += kDaWarps)  // q-tile rows past the group's rows
     *reinterpret_cast<uint2*>(sq + swz<kDaD>(i, lane >> 1) + (lane & 1) * 8) = make_uint2(0, 0);
-  // later rounds read new keys back from the caches
+  // later passes read new keys back from the caches
   if (nkb > kDaWarps) __threadfence();
   __syncthreads();
 
