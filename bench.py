@@ -468,6 +468,17 @@ def run_kernels(args, cfg):
     bench("decode_attention", lambda: lib.qk_norm_rope_sdpa_decode(
         qp[:1], kp[:1], vp[:1], qn, qn, cfg.eps, kc, vc, n_heads=Hq, n_kv_heads=Hkv, offset=PROMPT,
         rope_base=cfg.rope_theta, scale=sc), 0, 2 * (PROMPT + 1) * Hkv * D * 2)
+    # mlx-whisper encoder conv stem (fp16, 8 x 3000 frames): conv1 128 -> 1280 (k3 s1),
+    # conv2 1280 -> 1280 (k3 s2), each with its bias and GELU
+    xw = torch.randn(8, 3000, 128, device="cuda").to(torch.float16)
+    w1 = (torch.randn(1280, 3, 128, device="cuda") / 20).to(torch.float16)
+    w2 = (torch.randn(1280, 3, 1280, device="cuda") / 60).to(torch.float16)
+    bw = torch.zeros(1280, device="cuda", dtype=torch.float16)
+    h1 = lib.conv1d(xw, w1, bw, stride=1, padding=1, act=1)
+    bench("whisper_conv1", lambda: lib.conv1d(xw, w1, bw, stride=1, padding=1, act=1), 2 * 8 * 3000 * 1280 * 3 * 128,
+          8 * 3000 * (128 + 1280) * 2)
+    bench("whisper_conv2", lambda: lib.conv1d(h1, w2, bw, stride=2, padding=1, act=1), 2 * 8 * 1500 * 1280 * 3 * 1280,
+          8 * (3000 + 1500) * 1280 * 2)
     print(json.dumps({"kernels": rows, "peaks": peaks}), flush=True)
     return 0
 

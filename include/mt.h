@@ -391,6 +391,19 @@ int mt_linear(const void* x, const void* w, const void* bias, void* y,
 /* ------------------------------------------------------------------------ */
 /* a-8: LayerNorm                                                            */
 /* ------------------------------------------------------------------------ */
+/*
+ * mx.conv1d for the Whisper encoder's conv stem (mlx-whisper conv1 / conv2:
+ * nn.Conv1d with bias, then GELU): channels-last x [N, L, Cin], w
+ * [Cout, K, Cin] (mlx layouts), y [N, Lout, Cout] with
+ * Lout = (L + 2*padding - K) / stride + 1, zero padding on both sides. The
+ * conv sums in fp32; conv, + bias (NULL: none) and GELU (act = 1; 0: none)
+ * are each rounded to dtype as the separate MLX ops would. Cin must be a
+ * multiple of 32 (MT_ERR_UNSUPPORTED otherwise); bf16 or f16.
+ */
+int mt_conv1d(const void* x, const void* w, const void* bias, void* y, int64_t N,
+              int64_t L, int64_t Cin, int64_t Cout, int K, int stride,
+              int padding, int act, int dtype, mt_stream_t stream);
+
 /* mx.fast.layer_norm(x, w, b, eps): two-pass mean / centred variance, then
  * the optional affine (autotuner/scaffold/lower.py:448-466, :1357-1410).
  * w and b may be NULL. */

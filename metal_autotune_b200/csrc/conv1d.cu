@@ -1,0 +1,197 @@
+// mx.conv1d for the Whisper encoder's conv stem (mlx-whisper conv1: 128 ->
+// 1280, k3 s1 p1; conv2: 1280 -> 1280, k3 s2 p1; each followed by its bias and
+// GELU), as one implicit GEMM with the bias and GELU in the epilogue.
+//
+// Channels-last x [N, L, Cin], w [Cout, K, Cin] (mlx layouts), y [N, Lout, Cout].
+// GEMM view: rows m = (n, t) over N*Lout output positions, columns = Cout, and
+// the reduction runs over (tap k, input channel ci): row m's slice for tap k is
+// x[n, t*stride + k - pad, :], contiguous in ci (zero outside [0, L)), and
+// column co's slice is w[co, k, :], contiguous too. A CTA computes a 128 x 128
+// output tile over 32-wide reduction chunks (each inside one tap, so Cin must
+// be a multiple of 32): both operand tiles are copied with cp.async into
+// double-buffered, XOR-swizzled shared memory and multiplied with mma.sync
+// m16n8k16 (bf16/f16 in, fp32 accumulate; 8 warps of 64 x 32). The epilogue
+// rounds as the separate MLX ops would: conv, + bias, GELU, each to the
+// element type (GELU evaluated in fp32 on the rounded input, mt_math.h).
+#include "mma_sync.cuh"
+#include "mt_common.cuh"
+#include "mt_math.h"
+
+namespace mt {
+
+constexpr int kCvBM = 128, kCvBN = 128, kCvBK = 32;
+constexpr int kCvThreads = 256;
+constexpr int kCvTileBytes = kCvBM * kCvBK * 2;  // one operand tile: 128 rows x 64 bytes
+
+struct Conv1dParams {
+  const void* x;
+  const void* w;
+  const void* bias;
+  void* y;
+  int64_t M;  // N * Lout
+  int L, Lout, Cin, Cout, K, stride, pad;
+};
+
+// byte offset of 16-byte chunk c (0..3) of row r in a tile of 64-byte rows:
+// the XOR spreads the 8 rows an ldmatrix reads over all 32 banks
+__device__ __forceinline__ int cv_swz(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
+
+template <int DT, int ACT>
+__global__ void __launch_bounds__(kCvThreads) conv1d_kernel(const Conv1dParams p) {
+  using T = typename Elem<DT>::T;
+  __shared__ __align__(128) uint8_t sa[2][kCvTileBytes];
+  __shared__ __align__(128) uint8_t sb[2][kCvTileBytes];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wm = warp >> 2, wn = warp & 3;  // warp tile: rows wm*64.., columns wn*32..
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kCvBM;
+  const int n0 = blockIdx.x * kCvBN;
+  const T* x = static_cast<const T*>(p.x);
+  const T* w = static_cast<const T*>(p.w);
+
+  griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
+
+  // per-thread copy slots: 2 chunks of A and 2 of B per reduction step
+  // (512 16-byte chunks each), fixed rows for the whole K loop
+  int a_r[2], a_c[2];
+  int64_t a_base[2];  // element offset of (n, t*stride - pad, 0), or -1 past the last row
+  int a_t0[2];        // t*stride - pad of the row
+  for (int i = 0; i < 2; ++i) {
+    const int idx = tid + i * kCvThreads;
+    a_r[i] = idx >> 2;
+    a_c[i] = idx & 3;
+    const int64_t m = m0 + a_r[i];
+    if (m < p.M) {
+      const int64_t n = m / p.Lout;
+      const int t = static_cast<int>(m - n * p.Lout);
+      a_t0[i] = t * p.stride - p.pad;
+      a_base[i] = n * p.L;
+    } else {
+      a_t0[i] = 0;
+      a_base[i] = -1;
+    }
+  }
+  const int nk = p.K * p.Cin / kCvBK;
+  auto load = [&](int kc, int buf) {
+    const int e0 = kc * kCvBK;
+    const int tap = e0 / p.Cin, ci0 = e0 - tap * p.Cin;
+    for (int i = 0; i < 2; ++i) {
+      const int src = a_t0[i] + tap;
+      const bool ok = a_base[i] >= 0 && src >= 0 && src < p.L;
+      const T* g = ok ? x + (a_base[i] + src) * p.Cin + ci0 + a_c[i] * 8 : x;
+      cp_async16(sa[buf] + cv_swz(a_r[i], a_c[i]), g, ok);
+      const int co = n0 + a_r[i];
+      const bool okb = co < p.Cout;
+      const T* gb = okb ? w + (static_cast<int64_t>(co) * p.K + tap) * p.Cin + ci0 + a_c[i] * 8 : w;
+      cp_async16(sb[buf] + cv_swz(a_r[i], a_c[i]), gb, okb);
+    }
+  };
+
+  float acc[4][4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
+
+  load(0, 0);
+  cp_async_commit();
+  for (int kc = 0; kc < nk; ++kc) {
+    const int buf = kc & 1;
+    if (kc + 1 < nk) load(kc + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t abase = smem_addr(sa[buf]), bbase = smem_addr(sb[buf]);
+#pragma unroll
+    for (int ks = 0; ks < kCvBK / 16; ++ks) {
+      uint32_t af[4][4];
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi) {
+        const int r = wm * 64 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = ks * 2 + (lane >> 4);
+        ldsm_x4(abase + cv_swz(r, c), af[mi][0], af[mi][1], af[mi][2], af[mi][3]);
+      }
+#pragma unroll
+      for (int nj = 0; nj < 4; nj += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = wn * 32 + nj * 8 + (lane & 7) + (lane >> 4) * 8;
+        const int c = ks * 2 + ((lane >> 3) & 1);
+        ldsm_x4(bbase + cv_swz(r, c), b0, b1, b2, b3);
+#pragma unroll
+        for (int mi = 0; mi < 4; ++mi) {
+          mma16816<DT>(acc[mi][nj], af[mi], b0, b1);
+          mma16816<DT>(acc[mi][nj + 1], af[mi], b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // epilogue: conv -> round, + bias -> round, GELU -> round
+  const T* bias = static_cast<const T*>(p.bias);
+  T* y = static_cast<T*>(p.y);
+  const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t m = m0 + wm * 64 + mi * 16 + g + h * 8;
+      if (m >= p.M) continue;
+#pragma unroll
+      for (int nj = 0; nj < 4; ++nj) {
+        const int co = n0 + wn * 32 + nj * 8 + 2 * t4;
+        float v[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float u = round_to<DT>(acc[mi][nj][h * 2 + e]);
+          if (bias && co + e < p.Cout) u = round_to<DT>(u + Elem<DT>::to_f(bias[co + e]));
+          if (ACT == 1) u = round_to<DT>(mt_gelu_f32(u));
+          v[e] = u;
+        }
+        T* dst = y + m * p.Cout + co;
+        if (co + 1 < p.Cout && (p.Cout & 1) == 0) {
+          *reinterpret_cast<typename Elem<DT>::T2*>(dst) = Elem<DT>::pack2(v[0], v[1]);
+        } else {
+          if (co < p.Cout) dst[0] = Elem<DT>::from_f(v[0]);
+          if (co + 1 < p.Cout) dst[1] = Elem<DT>::from_f(v[1]);
+        }
+      }
+    }
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" int mt_conv1d(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
+                         int64_t Cout, int K, int stride, int padding, int act, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && w && y, "mt_conv1d: null pointer");
+  MT_CHECK_ARG(N >= 0 && L >= 1 && Cin >= 1 && Cout >= 1 && K >= 1 && stride >= 1 && padding >= 0,
+               "mt_conv1d: N=%lld L=%lld Cin=%lld Cout=%lld K=%d stride=%d padding=%d", (long long)N, (long long)L,
+               (long long)Cin, (long long)Cout, K, stride, padding);
+  MT_CHECK_ARG(act == 0 || act == 1, "mt_conv1d: act=%d (0 none, 1 GELU)", act);
+  MT_CHECK_ARG(L + 2 * static_cast<int64_t>(padding) >= K, "mt_conv1d: input of %lld + 2*%d is shorter than the kernel %d",
+               (long long)L, padding, K);
+  MT_CHECK_ARG(L < (1 << 30) && Cout < (1 << 30) && static_cast<int64_t>(K) * Cin < (1 << 30), "mt_conv1d: too large");
+  if (dtype != MT_BF16 && dtype != MT_F16) {
+    set_error("mt_conv1d: dtype %d is not built (bf16 or f16)", dtype);
+    return MT_ERR_UNSUPPORTED;
+  }
+  if (Cin % kCvBK != 0) {
+    set_error("mt_conv1d: Cin=%lld must be a multiple of %d", (long long)Cin, kCvBK);
+    return MT_ERR_UNSUPPORTED;
+  }
+  MT_CHECK_ARG(aligned(x, 16) && aligned(w, 16) && aligned(y, 4), "mt_conv1d: x and w must be 16-byte aligned");
+  const int64_t Lout = (L + 2 * padding - K) / stride + 1;
+  if (N == 0) return MT_OK;
+  Conv1dParams p = {x, w, bias, y, N * Lout, (int)L, (int)Lout, (int)Cin, (int)Cout, K, stride, padding};
+  MT_CHECK_ARG(p.M / kCvBM < 65535, "mt_conv1d: %lld output rows exceed the grid", (long long)p.M);
+  const dim3 grid(static_cast<unsigned>((Cout + kCvBN - 1) / kCvBN), static_cast<unsigned>((p.M + kCvBM - 1) / kCvBM));
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == MT_BF16)
+    return act ? launch(conv1d_kernel<MT_BF16, 1>, grid, dim3(kCvThreads), 0, s, p)
+               : launch(conv1d_kernel<MT_BF16, 0>, grid, dim3(kCvThreads), 0, s, p);
+  return act ? launch(conv1d_kernel<MT_F16, 1>, grid, dim3(kCvThreads), 0, s, p)
+             : launch(conv1d_kernel<MT_F16, 0>, grid, dim3(kCvThreads), 0, s, p);
+}

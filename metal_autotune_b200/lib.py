@@ -72,6 +72,7 @@ SIGNATURES = {
         C.c_int, [P, P, F32, P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P]),
     "mt_qk_norm_rope_sdpa_decode": (
         C.c_int, [P, P, P, I64, I64, P, P, F32, P, P, P, I64, I64, I64, I64, I64, I64, F32, F32, I32, P]),
+    "mt_conv1d": (C.c_int, [P, P, P, P, I64, I64, I64, I64, I32, I32, I32, I32, I32, P]),
     "mt_qmm_workspace_bytes": (C.c_size_t, [I64, I64, I64, I32, I32]),
     "mt_qmm_partition_check": (C.c_int, [I64, I32, I32, I32, P]),
     "mt_rms_norm": (C.c_int, [P, P, F32, P, I64, I64, I32, P]),
@@ -361,6 +362,19 @@ def qk_norm_rope_sdpa_decode(q, k, v, q_norm_w, k_norm_w, eps, k_cache, v_cache,
          _ptr(k_norm_w), float(eps), _ptr(o), _ptr(k_cache), _ptr(v_cache), T, n_heads, n_kv_heads, head_dim,
          k_cache.shape[-2], int(offset), float(rope_base), float(scale), dtype_code(q.dtype), _stream())
     return o
+
+
+def conv1d(x, w, bias=None, *, stride=1, padding=0, act=0, out=None):
+    """mx.conv1d (channels-last x [N, L, Cin], w [Cout, K, Cin]) + optional bias and GELU (act=1)."""
+    _dense(x, "x")
+    _dense(w, "w")
+    N, L, Cin = x.shape
+    Cout, K, _ = w.shape
+    Lout = (L + 2 * padding - K) // stride + 1
+    y = out if out is not None else torch.empty(N, Lout, Cout, dtype=x.dtype, device=x.device)
+    call("mt_conv1d", _ptr(x), _ptr(w), _ptr(bias) if bias is not None else None, _ptr(y), N, L, Cin, Cout, K,
+         stride, padding, act, dtype_code(x.dtype), _stream())
+    return y
 
 
 def swiglu(gate, up, *, out=None):

@@ -395,3 +395,31 @@ void orc_causal_conv1d(const float* x, const float* wt, const float* bias, const
       y[l * C + c] = round_dt(v, dt);
     }
 }
+
+/* mx.conv1d over channels-last x [N, L, Cin] with w [Cout, K, Cin]
+ * (stride, zero padding `pad` on both sides), as mlx.nn.Conv1d with its bias
+ * and the encoder's GELU after it (mlx-whisper conv1/conv2): the conv sum in
+ * fp32 over (tap, channel) in order, each of conv / +bias / gelu rounded to
+ * the element type as the separate MLX ops materialise them. act: 0 none,
+ * 1 GELU (erf form, evaluated in fp32 on the rounded input). */
+void orc_conv1d(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t L, int64_t Cin,
+                int64_t Cout, int K, int stride, int pad, int act, int dt) {
+  const int64_t Lout = (L + 2 * pad - K) / stride + 1;
+#pragma omp parallel for collapse(3) schedule(static)
+  for (int64_t n = 0; n < N; ++n)
+    for (int64_t t = 0; t < Lout; ++t)
+      for (int64_t co = 0; co < Cout; ++co) {
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k) {
+          const int64_t src = t * stride + k - pad;
+          if (src < 0 || src >= L) continue;
+          const float* xr = x + (n * L + src) * Cin;
+          const float* wr = w + (co * K + k) * Cin;
+          for (int64_t ci = 0; ci < Cin; ++ci) acc = fmaf(xr[ci], wr[ci], acc);
+        }
+        float v = round_dt(acc, dt);
+        if (bias) v = round_dt(v + bias[co], dt);
+        if (act == 1) v = round_dt(mt_gelu_f32(v), dt);
+        y[(n * Lout + t) * Cout + co] = v;
+      }
+}

@@ -46,6 +46,7 @@ def lib() -> C.CDLL:
             "orc_mamba_scan": (None, [f32p, f32p, C.c_void_p, f32p, f32p, f32p, C.c_void_p, f32p, f32p,
                                       C.c_void_p, I64, I64, I64, I]),
             "orc_causal_conv1d": (None, [f32p, f32p, C.c_void_p, C.c_void_p, f32p, I64, I64, I, I, I]),
+            "orc_conv1d": (None, [f32p, f32p, C.c_void_p, f32p, I64, I64, I64, I64, I, I, I, I, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -266,4 +267,16 @@ def causal_conv1d(x, w, bias=None, state=None, silu=True, dtype="float16"):
     W = np.asarray(w).shape[-1]
     y = np.empty_like(x)
     lib().orc_causal_conv1d(x, _f32(w), _opt(bias), _opt(state), y, L, Cn, W, int(silu), DT[dtype])
+    return y
+
+
+def conv1d(x, w, bias=None, stride=1, padding=0, act=0, dtype="float16"):
+    """mx.conv1d (channels-last x [N, L, Cin], w [Cout, K, Cin]) + bias + optional GELU
+    (mlx-whisper's conv stem), each op rounded to dtype."""
+    x, w = _f32(x), _f32(w)
+    N, L, Cin = x.shape
+    Cout, K, _ = w.shape
+    Lout = (L + 2 * padding - K) // stride + 1
+    y = np.empty((N, Lout, Cout), np.float32)
+    lib().orc_conv1d(x, w, _opt(bias), y, N, L, Cin, Cout, K, stride, padding, act, DT[dtype])
     return y

@@ -99,3 +99,11 @@ def test_fused_decode_cuts_check_arguments_without_gpu(mt):
     rc = mt.mt_rms_norm_quantized_matmul_swiglu(p, C.c_void_p(258), 1e-6, p, p, p, p, p, p, p, 1, 256, 1024, 64, 4,
                                                 0, None)
     assert rc == -1 and b"16-byte aligned" in mt.mt_last_error_string()
+
+
+def test_conv1d_checks_arguments_without_gpu(mt):
+    p = C.c_void_p(256)
+    rc = mt.mt_conv1d(p, p, None, p, 1, 100, 48, 64, 3, 1, 1, 1, 1, None)  # Cin not a multiple of 32
+    assert rc == -2 and b"multiple of 32" in mt.mt_last_error_string()
+    rc = mt.mt_conv1d(p, p, None, p, 1, 1, 64, 64, 5, 1, 1, 0, 1, None)  # input shorter than the kernel
+    assert rc == -1 and b"shorter than the kernel" in mt.mt_last_error_string()

@@ -364,3 +364,35 @@ def test_bitwise_and_cosine(cuda):
     assert not exact.bitwise_equal(z, -z)
     c = numeric.cosine(a, b)
     assert c == pytest.approx(NR.cosine(n(a), n(b)), abs=1e-6)
+
+
+# --------------------------------------------------------------- conv1d (Whisper conv stem)
+CONV_CASES = [
+    # N, L, Cin, Cout, K, stride, padding, act, bias, dtype
+    (1, 40, 32, 64, 3, 1, 1, 0, False, "float16"),
+    (2, 301, 128, 256, 3, 1, 1, 1, True, "float16"),       # conv1 form, odd length
+    (1, 300, 256, 192, 3, 2, 1, 1, True, "bfloat16"),      # conv2 form, Cout not a multiple of 128
+    (1, 50, 64, 129, 3, 1, 1, 0, True, "bfloat16"),        # odd Cout: scalar tail stores
+    (1, 3000, 128, 1280, 3, 1, 1, 1, True, "float16"),     # mlx-whisper conv1 at full length
+    (1, 600, 1280, 1280, 3, 2, 1, 1, True, "float16"),     # conv2 channels, shortened
+]
+
+
+@pytest.mark.parametrize("N,L,Cin,Cout,K,stride,pad,act,bias,dtype", CONV_CASES)
+def test_conv1d(cuda, oracle, N, L, Cin, Cout, K, stride, pad, act, bias, dtype):
+    tdt = BF if dtype == "bfloat16" else torch.float16
+    r = np.random.default_rng(L + Cout)
+    x = oracle.round_to(r.standard_normal((N, L, Cin)).astype(np.float32), dtype)
+    w = oracle.round_to(r.standard_normal((Cout, K, Cin)).astype(np.float32) / np.sqrt(K * Cin), dtype)
+    b = oracle.round_to(r.standard_normal(Cout).astype(np.float32) * 0.1, dtype) if bias else None
+    y = lib.conv1d(t(x, tdt), t(w, tdt), t(b, tdt) if bias else None, stride=stride, padding=pad, act=act)
+    torch.cuda.synchronize()
+    ref = oracle.conv1d(x, w, b, stride, pad, act, dtype)
+    assert tuple(y.shape) == ref.shape
+    # fp32 sums in another order than the oracle's sequential one: a rounding
+    # step of the element type at most, after each of conv / bias / GELU
+    ulp = 2.0 ** (-7 if dtype == "bfloat16" else -10)
+    got, refd = n(y).astype(np.float64), ref.astype(np.float64)
+    tol = 3 * ulp * np.abs(refd) + 2 * ulp * np.abs(refd).max()
+    bad = np.abs(got - refd) > tol
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance; worst {np.abs(got - refd).max():.4g}"
