@@ -37,7 +37,7 @@ struct Conv1dParams {
 __device__ __forceinline__ int cv_swz(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
 
 template <int DT, int ACT>
-__global__ void __launch_bounds__(kCvThreads) conv1d_kernel(const Conv1dParams p) {
+__global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParams p) {
   using T = typename Elem<DT>::T;
   __shared__ __align__(128) uint8_t sa[2][kCvTileBytes];
   __shared__ __align__(128) uint8_t sb[2][kCvTileBytes];
