@@ -8,8 +8,8 @@
 // x[n, t*stride + k - pad, :], contiguous in ci (zero outside [0, L)), and
 // column co's slice is w[co, k, :], contiguous too. A CTA computes a 128 x 128
 // output tile over 32-wide reduction chunks (each inside one tap, so Cin must
-// be a multiple of 32): both operand tiles are copied with cp.async into
-// double-buffered, XOR-swizzled shared memory and multiplied with mma.sync
+// be a multiple of 32): both operand tiles are copied with cp.async into a
+// 4-stage ring of XOR-swizzled shared memory and multiplied with mma.sync
 // m16n8k16 (bf16/f16 in, fp32 accumulate; 8 warps of 64 x 32). The epilogue
 // rounds as the separate MLX ops would: conv, + bias, GELU, each to the
 // element type (GELU evaluated in fp32 on the rounded input, mt_math.h).
@@ -22,6 +22,8 @@ namespace mt {
 constexpr int kCvBM = 128, kCvBN = 128, kCvBK = 32;
 constexpr int kCvThreads = 256;
 constexpr int kCvTileBytes = kCvBM * kCvBK * 2;  // one operand tile: 128 rows x 64 bytes
+constexpr int kCvStages = 4;                        // cp.async ring depth
+constexpr int kCvSmem = kCvStages * 2 * kCvTileBytes;
 
 struct Conv1dParams {
   const void* x;
@@ -39,8 +41,9 @@ __device__ __forceinline__ int cv_swz(int r, int c) { return r * 64 + ((c ^ ((r 
 template <int DT, int ACT>
 __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParams p) {
   using T = typename Elem<DT>::T;
-  __shared__ __align__(128) uint8_t sa[2][kCvTileBytes];
-  __shared__ __align__(128) uint8_t sb[2][kCvTileBytes];
+  extern __shared__ __align__(128) uint8_t cv_smem[];
+  auto sa = [&](int s) { return cv_smem + s * 2 * kCvTileBytes; };
+  auto sb = [&](int s) { return cv_smem + s * 2 * kCvTileBytes + kCvTileBytes; };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int wm = warp >> 2, wn = warp & 3;  // warp tile: rows wm*64.., columns wn*32..
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kCvBM;
@@ -79,11 +82,11 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
       const int src = a_t0[i] + tap;
       const bool ok = a_base[i] >= 0 && src >= 0 && src < p.L;
       const T* g = ok ? x + (a_base[i] + src) * p.Cin + ci0 + a_c[i] * 8 : x;
-      cp_async16(sa[buf] + cv_swz(a_r[i], a_c[i]), g, ok);
+      cp_async16(sa(buf) + cv_swz(a_r[i], a_c[i]), g, ok);
       const int co = n0 + a_r[i];
       const bool okb = co < p.Cout;
       const T* gb = okb ? w + (static_cast<int64_t>(co) * p.K + tap) * p.Cin + ci0 + a_c[i] * 8 : w;
-      cp_async16(sb[buf] + cv_swz(a_r[i], a_c[i]), gb, okb);
+      cp_async16(sb(buf) + cv_swz(a_r[i], a_c[i]), gb, okb);
     }
   };
 
@@ -93,15 +96,20 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
 
-  load(0, 0);
-  cp_async_commit();
-  for (int kc = 0; kc < nk; ++kc) {
-    const int buf = kc & 1;
-    if (kc + 1 < nk) load(kc + 1, buf ^ 1);
+  // ring of kCvStages chunks: chunk kc lives in stage kc % kCvStages; the
+  // copies of the next kCvStages - 1 chunks are in flight while one is used
+#pragma unroll
+  for (int s = 0; s < kCvStages - 1; ++s) {
+    if (s < nk) load(s, s);
     cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const uint32_t abase = smem_addr(sa[buf]), bbase = smem_addr(sb[buf]);
+  }
+  for (int kc = 0; kc < nk; ++kc) {
+    const int buf = kc % kCvStages;
+    cp_async_wait<kCvStages - 2>();
+    __syncthreads();  // chunk kc landed for every thread; stage (kc - 1) % kCvStages is free
+    if (kc + kCvStages - 1 < nk) load(kc + kCvStages - 1, (kc + kCvStages - 1) % kCvStages);
+    cp_async_commit();
+    const uint32_t abase = smem_addr(sa(buf)), bbase = smem_addr(sb(buf));
 #pragma unroll
     for (int ks = 0; ks < kCvBK / 16; ++ks) {
       uint32_t af[4][4];
@@ -124,8 +132,8 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
         }
       }
     }
-    __syncthreads();
   }
+  cp_async_wait<0>();
 
   // epilogue: conv -> round, + bias -> round, GELU -> round
   const T* bias = static_cast<const T*>(p.bias);
@@ -189,9 +197,10 @@ extern "C" int mt_conv1d(const void* x, const void* w, const void* bias, void* y
   MT_CHECK_ARG(p.M / kCvBM < 65535, "mt_conv1d: %lld output rows exceed the grid", (long long)p.M);
   const dim3 grid(static_cast<unsigned>((Cout + kCvBN - 1) / kCvBN), static_cast<unsigned>((p.M + kCvBM - 1) / kCvBM));
   const cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == MT_BF16)
-    return act ? launch(conv1d_kernel<MT_BF16, 1>, grid, dim3(kCvThreads), 0, s, p)
-               : launch(conv1d_kernel<MT_BF16, 0>, grid, dim3(kCvThreads), 0, s, p);
-  return act ? launch(conv1d_kernel<MT_F16, 1>, grid, dim3(kCvThreads), 0, s, p)
-             : launch(conv1d_kernel<MT_F16, 0>, grid, dim3(kCvThreads), 0, s, p);
+  auto run = [&](auto kern) -> int {
+    if (int e = ensure_smem(kern, kCvSmem)) return e;
+    return launch(kern, grid, dim3(kCvThreads), kCvSmem, s, p);
+  };
+  if (dtype == MT_BF16) return act ? run(conv1d_kernel<MT_BF16, 1>) : run(conv1d_kernel<MT_BF16, 0>);
+  return act ? run(conv1d_kernel<MT_F16, 1>) : run(conv1d_kernel<MT_F16, 0>);
 }
