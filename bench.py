@@ -479,6 +479,16 @@ def run_kernels(args, cfg):
           8 * 3000 * (128 + 1280) * 2)
     bench("whisper_conv2", lambda: lib.conv1d(h1, w2, bw, stride=2, padding=1, act=1), 2 * 8 * 1500 * 1280 * 3 * 1280,
           8 * (3000 + 1500) * 1280 * 2)
+    # mlx-whisper encoder MLP (fp16, 8 clips x 1500 frames): fc1 1280 -> 5120 + GELU, fc2 5120 -> 1280
+    xm = torch.randn(8 * 1500, 1280, device="cuda").to(torch.float16)
+    f1 = (torch.randn(5120, 1280, device="cuda") / 36).to(torch.float16)
+    f2 = (torch.randn(1280, 5120, device="cuda") / 72).to(torch.float16)
+    b1 = torch.zeros(5120, device="cuda", dtype=torch.float16)
+    hm = lib.linear(xm, f1, b1, act=1)
+    bench("whisper_fc1_gelu", lambda: lib.linear(xm, f1, b1, act=1), 2 * 12000 * 5120 * 1280,
+          (12000 * (1280 + 5120) + 5120 * 1280) * 2)
+    bench("whisper_fc2", lambda: lib.linear(hm, f2, bw, act=0), 2 * 12000 * 1280 * 5120,
+          (12000 * (1280 + 5120) + 5120 * 1280) * 2)
     print(json.dumps({"kernels": rows, "peaks": peaks}), flush=True)
     return 0
 

@@ -382,7 +382,10 @@ int mt_diff_reduce_noalloc(const void* a, const void* b, int64_t n, int dtype,
  * autotuner/scaffold/lower.py:1109-1142), act 0 = identity, 1 = GELU exact
  * erf form 0.5 x (1 + erf(x / sqrt 2)) (mlx.nn.GELU default;
  * examples/tiny_mlp.py:5-6). Bit-reproducible against the CPU oracle.
- * bias may be NULL. dtype must be MT_F32.
+ * bias may be NULL. dtype MT_F32; MT_BF16 / MT_F16 run the tensor-core
+ * implicit GEMM of mt_conv1d (the Whisper MLP sizes: K a multiple of 32),
+ * fp32 sums with the bias added before the one rounding (mx.addmm) and GELU
+ * rounded after it (not bit-reproducible: the sums run in tiles).
  */
 int mt_linear(const void* x, const void* w, const void* bias, void* y,
               int64_t M, int64_t N, int64_t K, int act, int dtype,

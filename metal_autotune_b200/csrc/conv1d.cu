@@ -32,6 +32,7 @@ struct Conv1dParams {
   void* y;
   int64_t M;  // N * Lout
   int L, Lout, Cin, Cout, K, stride, pad;
+  int bias_fused;  // 1: round(sum + bias) once (mx.addmm, nn.Linear); 0: round(round(sum) + bias) (conv, then + bias)
 };
 
 // byte offset of 16-byte chunk c (0..3) of row r in a tile of 64-byte rows:
@@ -151,8 +152,9 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
         float v[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          float u = round_to<DT>(acc[mi][nj][h * 2 + e]);
-          if (bias && co + e < p.Cout) u = round_to<DT>(u + Elem<DT>::to_f(bias[co + e]));
+          const float b = (bias && co + e < p.Cout) ? Elem<DT>::to_f(bias[co + e]) : 0.f;
+          float u = p.bias_fused ? round_to<DT>(acc[mi][nj][h * 2 + e] + b)
+                                 : round_to<DT>(round_to<DT>(acc[mi][nj][h * 2 + e]) + b);
           if (ACT == 1) u = round_to<DT>(mt_gelu_f32(u));
           v[e] = u;
         }
@@ -171,9 +173,22 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
 
 using namespace mt;
 
+namespace mt {
+int conv1d_run(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
+               int64_t Cout, int K, int stride, int padding, int act, int dtype, int bias_fused, cudaStream_t stream);
+}
+
 extern "C" int mt_conv1d(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
                          int64_t Cout, int K, int stride, int padding, int act, int dtype, mt_stream_t stream) {
   clear_error();
+  return conv1d_run(x, w, bias, y, N, L, Cin, Cout, K, stride, padding, act, dtype, 0, (cudaStream_t)stream);
+}
+
+// The implicit GEMM for mt_conv1d and the 16-bit mt_linear (one tap, bias
+// fused before the rounding as mx.addmm does).
+int mt::conv1d_run(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
+                   int64_t Cout, int K, int stride, int padding, int act, int dtype, int bias_fused,
+                   cudaStream_t stream) {
   MT_CHECK_ARG(x && w && y, "mt_conv1d: null pointer");
   MT_CHECK_ARG(N >= 0 && L >= 1 && Cin >= 1 && Cout >= 1 && K >= 1 && stride >= 1 && padding >= 0,
                "mt_conv1d: N=%lld L=%lld Cin=%lld Cout=%lld K=%d stride=%d padding=%d", (long long)N, (long long)L,
@@ -193,10 +208,10 @@ extern "C" int mt_conv1d(const void* x, const void* w, const void* bias, void* y
   MT_CHECK_ARG(aligned(x, 16) && aligned(w, 16) && aligned(y, 4), "mt_conv1d: x and w must be 16-byte aligned");
   const int64_t Lout = (L + 2 * padding - K) / stride + 1;
   if (N == 0) return MT_OK;
-  Conv1dParams p = {x, w, bias, y, N * Lout, (int)L, (int)Lout, (int)Cin, (int)Cout, K, stride, padding};
+  Conv1dParams p = {x, w, bias, y, N * Lout, (int)L, (int)Lout, (int)Cin, (int)Cout, K, stride, padding, bias_fused};
   MT_CHECK_ARG(p.M / kCvBM < 65535, "mt_conv1d: %lld output rows exceed the grid", (long long)p.M);
   const dim3 grid(static_cast<unsigned>((Cout + kCvBN - 1) / kCvBN), static_cast<unsigned>((p.M + kCvBM - 1) / kCvBM));
-  const cudaStream_t s = (cudaStream_t)stream;
+  const cudaStream_t s = stream;
   auto run = [&](auto kern) -> int {
     if (int e = ensure_smem(kern, kCvSmem)) return e;
     return launch(kern, grid, dim3(kCvThreads), kCvSmem, s, p);

@@ -54,11 +54,25 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(const float* __restrict
 
 using namespace mt;
 
+namespace mt {
+int conv1d_run(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
+               int64_t Cout, int K, int stride, int padding, int act, int dtype, int bias_fused, cudaStream_t stream);
+}
+
 extern "C" int mt_linear(const void* x, const void* w, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
                          int act, int dtype, mt_stream_t stream) {
   clear_error();
   MT_CHECK_ARG(x && w && y, "mt_linear: null pointer");
-  MT_CHECK_ARG(dtype == MT_F32, "mt_linear: only fp32 is built (dtype %d)", dtype);
+  if (dtype == MT_BF16 || dtype == MT_F16) {
+    // tensor-core path (the Whisper MLP sizes): x [M, K] @ w[N, K]^T as a
+    // one-tap conv over M positions, bias added before the single rounding
+    // (mx.addmm), GELU rounded after it
+    MT_CHECK_ARG(act == 0 || act == 1, "mt_linear: act must be 0 (identity) or 1 (gelu)");
+    MT_CHECK_ARG(M >= 0 && N > 0 && K > 0, "mt_linear: bad shape");
+    if (M == 0) return MT_OK;
+    return conv1d_run(x, w, bias, y, 1, M, K, N, 1, 1, 0, act, dtype, 1, (cudaStream_t)stream);
+  }
+  MT_CHECK_ARG(dtype == MT_F32, "mt_linear: dtype %d is not built (fp32, bf16, f16)", dtype);
   MT_CHECK_ARG(act == 0 || act == 1, "mt_linear: act must be 0 (identity) or 1 (gelu)");
   MT_CHECK_ARG(M >= 0 && N > 0 && K > 0 && M < (1 << 30) && N < (1 << 30) && K < (1 << 30),
                "mt_linear: bad shape");

@@ -423,3 +423,18 @@ void orc_conv1d(const float* x, const float* w, const float* bias, float* y, int
         y[(n * Lout + t) * Cout + co] = v;
       }
 }
+
+/* nn.Linear in a 16-bit dtype (mx.addmm(bias, x, w.T) then nn.gelu):
+ * y = round(sum_k x w + bias), GELU in fp32 on that rounded value, rounded. */
+void orc_linear_lp(const float* x, const float* w, const float* bias, float* y, int64_t M, int64_t N, int64_t K,
+                   int act, int dt) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t m = 0; m < M; ++m)
+    for (int64_t n = 0; n < N; ++n) {
+      float acc = 0.0f;
+      for (int64_t k = 0; k < K; ++k) acc = fmaf(x[m * K + k], w[n * K + k], acc);
+      float v = round_dt(bias ? acc + bias[n] : acc, dt);
+      if (act == 1) v = round_dt(mt_gelu_f32(v), dt);
+      y[m * N + n] = v;
+    }
+}

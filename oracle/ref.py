@@ -47,6 +47,7 @@ def lib() -> C.CDLL:
                                       C.c_void_p, I64, I64, I64, I]),
             "orc_causal_conv1d": (None, [f32p, f32p, C.c_void_p, C.c_void_p, f32p, I64, I64, I, I, I]),
             "orc_conv1d": (None, [f32p, f32p, C.c_void_p, f32p, I64, I64, I64, I64, I, I, I, I, I]),
+            "orc_linear_lp": (None, [f32p, f32p, C.c_void_p, f32p, I64, I64, I64, I, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -280,3 +281,14 @@ def conv1d(x, w, bias=None, stride=1, padding=0, act=0, dtype="float16"):
     y = np.empty((N, Lout, Cout), np.float32)
     lib().orc_conv1d(x, w, _opt(bias), y, N, L, Cin, Cout, K, stride, padding, act, DT[dtype])
     return y
+
+
+def linear_lp(x, w, bias=None, act=0, dtype="float16"):
+    """nn.Linear in a 16-bit dtype: round(x w^T + bias), then GELU (act=1) rounded."""
+    x, w = _f32(x), _f32(w)
+    K = x.shape[-1]
+    M = x.size // K
+    N = w.shape[0]
+    y = np.empty((M, N), np.float32)
+    lib().orc_linear_lp(x.reshape(M, K), w, _opt(bias), y, M, N, K, act, DT[dtype])
+    return y.reshape(*x.shape[:-1], N)

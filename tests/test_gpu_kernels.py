@@ -396,3 +396,26 @@ def test_conv1d(cuda, oracle, N, L, Cin, Cout, K, stride, pad, act, bias, dtype)
     tol = 3 * ulp * np.abs(refd) + 2 * ulp * np.abs(refd).max()
     bad = np.abs(got - refd) > tol
     assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance; worst {np.abs(got - refd).max():.4g}"
+
+
+# --------------------------------------------------------------- 16-bit linear (Whisper MLP)
+@pytest.mark.parametrize("M,N,K,act,bias,dtype", [
+    (100, 320, 256, 1, True, "float16"),
+    (37, 130, 64, 0, False, "bfloat16"),
+    (1500, 5120, 1280, 1, True, "float16"),   # mlx-whisper fc1 for one 1500-frame clip
+    (1500, 1280, 5120, 0, True, "float16"),   # fc2
+])
+def test_linear_16bit(cuda, oracle, M, N, K, act, bias, dtype):
+    tdt = BF if dtype == "bfloat16" else torch.float16
+    r = np.random.default_rng(M + N + K)
+    x = oracle.round_to(r.standard_normal((M, K)).astype(np.float32), dtype)
+    w = oracle.round_to(r.standard_normal((N, K)).astype(np.float32) / np.sqrt(K), dtype)
+    b = oracle.round_to(r.standard_normal(N).astype(np.float32) * 0.1, dtype) if bias else None
+    y = lib.linear(t(x, tdt), t(w, tdt), t(b, tdt) if bias else None, act=act)
+    torch.cuda.synchronize()
+    ref = oracle.linear_lp(x, w, b, act, dtype)
+    ulp = 2.0 ** (-7 if dtype == "bfloat16" else -10)
+    got, refd = n(y).astype(np.float64), ref.astype(np.float64)
+    tol = 3 * ulp * np.abs(refd) + 2 * ulp * np.abs(refd).max()
+    bad = np.abs(got - refd) > tol
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance; worst {np.abs(got - refd).max():.4g}"
