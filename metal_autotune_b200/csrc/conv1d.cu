@@ -12,7 +12,8 @@
 // 4-stage ring of XOR-swizzled shared memory and multiplied with mma.sync
 // m16n8k16 (bf16/f16 in, fp32 accumulate; 8 warps of 64 x 32). The epilogue
 // rounds as the separate MLX ops would: conv, + bias, GELU, each to the
-// element type (GELU evaluated in fp32 on the rounded input, mt_math.h).
+// element type (GELU evaluated in fp32 on the rounded input, mt_math.h), and
+// stages the tile in shared memory for 16-byte coalesced stores.
 #include "mma_sync.cuh"
 #include "mt_common.cuh"
 #include "mt_math.h"
@@ -24,6 +25,7 @@ constexpr int kCvThreads = 256;
 constexpr int kCvTileBytes = kCvBM * kCvBK * 2;  // one operand tile: 128 rows x 64 bytes
 constexpr int kCvStages = 4;                        // cp.async ring depth
 constexpr int kCvSmem = kCvStages * 2 * kCvTileBytes;
+static_assert(kCvBM * (kCvBN + 8) * 2 <= kCvSmem, "the staged output tile reuses the ring");
 
 struct Conv1dParams {
   const void* x;
@@ -135,20 +137,23 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
     }
   }
   cp_async_wait<0>();
+  __syncthreads();  // every warp is done with the ring: it now stages the output tile
 
-  // epilogue: conv -> round, + bias -> round, GELU -> round
+  // epilogue: conv -> round, + bias -> round, GELU -> round, into a shared
+  // 128 x 128 tile (rows padded by 16 bytes), then 16-byte coalesced stores
+  constexpr int kPitch = kCvBN + 8;  // elements per staged row
+  T* tile = reinterpret_cast<T*>(cv_smem);
   const T* bias = static_cast<const T*>(p.bias);
-  T* y = static_cast<T*>(p.y);
   const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
   for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int64_t m = m0 + wm * 64 + mi * 16 + g + h * 8;
-      if (m >= p.M) continue;
+      const int rl = wm * 64 + mi * 16 + g + h * 8;
 #pragma unroll
       for (int nj = 0; nj < 4; ++nj) {
-        const int co = n0 + wn * 32 + nj * 8 + 2 * t4;
+        const int cl = wn * 32 + nj * 8 + 2 * t4;
+        const int co = n0 + cl;
         float v[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
@@ -158,15 +163,25 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
           if (ACT == 1) u = round_to<DT>(mt_gelu_f32(u));
           v[e] = u;
         }
-        T* dst = y + m * p.Cout + co;
-        if (co + 1 < p.Cout && (p.Cout & 1) == 0) {
-          *reinterpret_cast<typename Elem<DT>::T2*>(dst) = Elem<DT>::pack2(v[0], v[1]);
-        } else {
-          if (co < p.Cout) dst[0] = Elem<DT>::from_f(v[0]);
-          if (co + 1 < p.Cout) dst[1] = Elem<DT>::from_f(v[1]);
-        }
+        *reinterpret_cast<typename Elem<DT>::T2*>(tile + rl * kPitch + cl) = Elem<DT>::pack2(v[0], v[1]);
       }
     }
+  __syncthreads();
+  T* y = static_cast<T*>(p.y);
+  const bool vec = (p.Cout & 7) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 15) == 0;
+  for (int i = tid; i < kCvBM * (kCvBN / 8); i += kCvThreads) {
+    const int rl = i / (kCvBN / 8), c8 = (i % (kCvBN / 8)) * 8;
+    const int64_t m = m0 + rl;
+    const int co = n0 + c8;
+    if (m >= p.M || co >= p.Cout) continue;
+    const T* src = tile + rl * kPitch + c8;
+    T* dst = y + m * p.Cout + co;
+    if (vec && co + 8 <= p.Cout) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    } else {
+      for (int e = 0; e < 8 && co + e < p.Cout; ++e) dst[e] = src[e];
+    }
+  }
 }
 
 }  // namespace mt
