@@ -479,6 +479,14 @@ def run_kernels(args, cfg):
           8 * 3000 * (128 + 1280) * 2)
     bench("whisper_conv2", lambda: lib.conv1d(h1, w2, bw, stride=2, padding=1, act=1), 2 * 8 * 1500 * 1280 * 3 * 1280,
           8 * (3000 + 1500) * 1280 * 2)
+    # attention at the other targets' sizes: mlx-whisper encoder (8 clips, 20 heads, 1500 frames,
+    # head_dim 64, non-causal) and Llama-3-8B prefill (8 x 2048 tokens, 32/8 heads, causal)
+    qw_ = torch.randn(8, 20, 1500, 64, device="cuda").to(torch.float16)
+    bench("whisper_sdpa", lambda: lib.sdpa(qw_, qw_, qw_, scale=0.125, causal=False), 4 * 8 * 20 * 1500 * 1500 * 64, 0)
+    ql_ = torch.randn(8, 32, 2048, 128, device="cuda").to(torch.bfloat16)
+    kl_ = torch.randn(8, 8, 2048, 128, device="cuda").to(torch.bfloat16)
+    bench("llama_sdpa", lambda: lib.sdpa(ql_, kl_, kl_, scale=1.0 / math.sqrt(128), causal=True),
+          2 * 8 * 32 * 2048 * 2048 * 128, 0)
     # mlx-whisper encoder MLP (fp16, 8 clips x 1500 frames): fc1 1280 -> 5120 + GELU, fc2 5120 -> 1280
     xm = torch.randn(8 * 1500, 1280, device="cuda").to(torch.float16)
     f1 = (torch.randn(5120, 1280, device="cuda") / 36).to(torch.float16)

@@ -199,6 +199,10 @@ def test_qk_norm_rope_cache(cuda, oracle, T, offset):
     (2, 16, 4, 4, 77, 128, False),
     (1, 4, 4, 3, 1000, 128, True),
     (1, 32, 8, 1, 2048, 128, True),
+    # mlx-whisper encoder self-attention for one clip (non-causal MHA, head_dim 64)
+    (1, 20, 20, 1500, 1500, 64, False),
+    # Llama-3-8B prefill heads over 1024 of its 2048 positions (GQA 32/8)
+    (1, 32, 8, 1024, 1024, 128, True),
 ])
 def test_sdpa(cuda, oracle, B, Hq, Hkv, Lq, Lk, D, causal):
     q = oracle.round_to(rng.standard_normal((B, Hq, Lq, D)).astype(np.float32), "bfloat16")
