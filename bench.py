@@ -26,6 +26,7 @@ metric. --mode kernels prints per-region kernel timings (profiling entry).
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import json
 import math
 import os
@@ -479,6 +480,25 @@ def run_kernels(args, cfg):
           8 * 3000 * (128 + 1280) * 2)
     bench("whisper_conv2", lambda: lib.conv1d(h1, w2, bw, stride=2, padding=1, act=1), 2 * 8 * 1500 * 1280 * 3 * 1280,
           8 * (3000 + 1500) * 1280 * 2)
+    # Mamba-370m layer at 512 steps (d_inner 2048, d_state 16, fp16): depthwise causal conv + selective scan
+    Lm, Dm, NSm = 512, 2048, 16
+    xm_ = torch.randn(Lm, Dm, device="cuda").to(torch.float16)
+    dtm = torch.randn(Lm, Dm, device="cuda").to(torch.float16)
+    zm = torch.randn(Lm, Dm, device="cuda").to(torch.float16)
+    Bm_ = torch.randn(Lm, NSm, device="cuda").to(torch.float16)
+    Cm_ = torch.randn(Lm, NSm, device="cuda").to(torch.float16)
+    Am = -torch.arange(1, NSm + 1, device="cuda", dtype=torch.float32).repeat(Dm, 1)
+    dtb = torch.zeros(Dm, device="cuda")
+    Dv = torch.ones(Dm, device="cuda")
+    cw = (torch.randn(Dm, 4, device="cuda") / 2).to(torch.float16)
+    bench("mamba_conv1d", lambda: lib.causal_conv1d(xm_, cw, None), 0, 2 * Lm * Dm * 2)
+    bench("mamba_scan", lambda: lib.mamba_scan(xm_, dtm, dtb, Am, Bm_, Cm_, Dv, zm), 0,
+          (4 * Lm * Dm + 2 * Lm * NSm) * 2)
+    # output-diff reduction of the verification ladder on Llama-size hidden states ([8, 2048, 4096] bf16)
+    da = torch.randn(8 * 2048 * 4096, device="cuda").to(torch.bfloat16)
+    db = (da.float() + 1e-3).to(torch.bfloat16)
+    st_ = torch.zeros(C.sizeof(lib.DiffStats), dtype=torch.uint8, device="cuda")
+    bench("diff_reduce", lambda: lib.diff_reduce(da, db, rtol=1e-2, atol=1e-2, stats=st_), 0, 2 * da.numel() * 2)
     # attention at the other targets' sizes: mlx-whisper encoder (8 clips, 20 heads, 1500 frames,
     # head_dim 64, non-causal) and Llama-3-8B prefill (8 x 2048 tokens, 32/8 heads, causal)
     qw_ = torch.randn(8, 20, 1500, 64, device="cuda").to(torch.float16)

@@ -6,10 +6,12 @@
 // The per-element excess is computed in fp32 exactly as the policy states it
 // (allowed = max(atol + rtol*|b|, wobble); excess = |a-b| - allowed, with the
 // overflow-safe scaled form where that is NaN), so max/argmax/count match a
-// CPU restatement bit for bit. Block partials go to the workspace in block
-// order and the last block to finish (atomic counter) folds them in that
-// order, so the fp64 cosine sums do not depend on scheduling either. The
-// block count depends only on n.
+// CPU restatement bit for bit. Block partials go to the workspace and the
+// last block to finish (atomic counter) folds them with all its threads in a
+// fixed order (thread t: blocks t, t+256, ...; then a fixed warp and block
+// merge), so the fp64 cosine sums do not depend on scheduling either. The
+// block count depends only on n. Inputs are read as 16-byte vectors when both
+// are 16-byte aligned, the next vectors in flight while one is visited.
 #include "mt_common.cuh"
 
 namespace mt {
@@ -124,7 +126,7 @@ constexpr int kDiffThreads = 256;
 
 static inline int diff_blocks(int64_t n) {
   const int64_t b = (n + 8191) / 8192;
-  return static_cast<int>(b < 1 ? 1 : (b > 512 ? 512 : b));
+  return static_cast<int>(b < 1 ? 1 : (b > 1184 ? 1184 : b));  // at most 8 blocks per SM of 148
 }
 
 template <typename T, bool FLOAT>
@@ -138,69 +140,119 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict_
   griddep_launch();  // dependents may launch now; their own wait covers this grid
   DiffPartial p;
   init(p);
-  // contiguous slice per block, strided by thread inside it: every index is
-  // visited once and each thread's indices increase (first-index tracking)
-  const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  // contiguous slice per block (a multiple of one 16-byte vector), strided by
+  // thread inside it: every index is visited once and each thread's indices
+  // increase (first-index tracking)
+  constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
+  int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  per = (per + V - 1) / V * V;
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * per;
   const int64_t hi = lo + per < n ? lo + per : n;
-  for (int64_t i = lo + threadIdx.x; i < hi; i += kDiffThreads) {
-    if constexpr (FLOAT) visit_float<T>(a[i], b[i], i, rtol, atol, wobble, p);
-    else visit_bits<T>(a[i], b[i], i, p);
+  const bool vec = FLOAT && ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+  if (vec) {
+    // one 16-byte vector of each input per step, the next step's vectors
+    // loaded before this one is visited (two steps of loads in flight)
+    const int64_t step = static_cast<int64_t>(kDiffThreads) * V;
+    int64_t i = lo + static_cast<int64_t>(threadIdx.x) * V;
+    uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
+    if (i + V <= hi) {
+      va = *reinterpret_cast<const uint4*>(a + i);
+      vb = *reinterpret_cast<const uint4*>(b + i);
+    }
+    while (i < hi) {
+      const int64_t nx = i + step;
+      uint4 na = make_uint4(0, 0, 0, 0), nb = make_uint4(0, 0, 0, 0);
+      if (nx + V <= hi) {
+        na = *reinterpret_cast<const uint4*>(a + nx);
+        nb = *reinterpret_cast<const uint4*>(b + nx);
+      }
+      if (i + V <= hi) {
+        const T* ea = reinterpret_cast<const T*>(&va);
+        const T* eb = reinterpret_cast<const T*>(&vb);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          if constexpr (FLOAT) visit_float<T>(ea[e], eb[e], i + e, rtol, atol, wobble, p);
+        }
+      } else {
+        for (int64_t j = i; j < hi; ++j) {
+          if constexpr (FLOAT) visit_float<T>(a[j], b[j], j, rtol, atol, wobble, p);
+        }
+      }
+      va = na;
+      vb = nb;
+      i = nx;
+    }
+  } else {
+    for (int64_t i = lo + threadIdx.x; i < hi; i += kDiffThreads) {
+      if constexpr (FLOAT) visit_float<T>(a[i], b[i], i, rtol, atol, wobble, p);
+      else visit_bits<T>(a[i], b[i], i, p);
+    }
   }
-  // warp then block merge, fixed order
-  for (int o = 1; o < 32; o <<= 1) {
-    DiffPartial q;
-    q.max_excess = __shfl_down_sync(0xffffffffu, p.max_excess, o);
-    q.max_abs = __shfl_down_sync(0xffffffffu, p.max_abs, o);
-    q.amax_a = __shfl_down_sync(0xffffffffu, p.amax_a, o);
-    q.amax_b = __shfl_down_sync(0xffffffffu, p.amax_b, o);
-    q.excess_index = __shfl_down_sync(0xffffffffu, p.excess_index, o);
-    q.over = __shfl_down_sync(0xffffffffu, p.over, o);
-    q.viol = __shfl_down_sync(0xffffffffu, p.viol, o);
-    q.first_viol = __shfl_down_sync(0xffffffffu, p.first_viol, o);
-    q.mism = __shfl_down_sync(0xffffffffu, p.mism, o);
-    q.first_mism = __shfl_down_sync(0xffffffffu, p.first_mism, o);
-    q.nan_ex = __shfl_down_sync(0xffffffffu, p.nan_ex, o);
-    q.dab = __shfl_down_sync(0xffffffffu, p.dab, o);
-    q.daa = __shfl_down_sync(0xffffffffu, p.daa, o);
-    q.dbb = __shfl_down_sync(0xffffffffu, p.dbb, o);
-    if ((threadIdx.x & 31) + o < 32) merge(p, q);
-  }
-  const int warp = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) sp[warp] = p;
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  // warp then block merge, fixed order; the block's result is valid in thread 0
+  auto block_merge = [&](DiffPartial v) {
+    for (int o = 1; o < 32; o <<= 1) {
+      DiffPartial q;
+      q.max_excess = __shfl_down_sync(0xffffffffu, v.max_excess, o);
+      q.max_abs = __shfl_down_sync(0xffffffffu, v.max_abs, o);
+      q.amax_a = __shfl_down_sync(0xffffffffu, v.amax_a, o);
+      q.amax_b = __shfl_down_sync(0xffffffffu, v.amax_b, o);
+      q.excess_index = __shfl_down_sync(0xffffffffu, v.excess_index, o);
+      q.over = __shfl_down_sync(0xffffffffu, v.over, o);
+      q.viol = __shfl_down_sync(0xffffffffu, v.viol, o);
+      q.first_viol = __shfl_down_sync(0xffffffffu, v.first_viol, o);
+      q.mism = __shfl_down_sync(0xffffffffu, v.mism, o);
+      q.first_mism = __shfl_down_sync(0xffffffffu, v.first_mism, o);
+      q.nan_ex = __shfl_down_sync(0xffffffffu, v.nan_ex, o);
+      q.dab = __shfl_down_sync(0xffffffffu, v.dab, o);
+      q.daa = __shfl_down_sync(0xffffffffu, v.daa, o);
+      q.dbb = __shfl_down_sync(0xffffffffu, v.dbb, o);
+      if ((threadIdx.x & 31) + o < 32) merge(v, q);
+    }
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) sp[warp] = v;
+    __syncthreads();
     DiffPartial acc = sp[0];
-    for (int w = 1; w < kDiffThreads / 32; ++w) merge(acc, sp[w]);
-    parts[blockIdx.x] = acc;
+    if (threadIdx.x == 0)
+      for (int w = 1; w < kDiffThreads / 32; ++w) merge(acc, sp[w]);
+    __syncthreads();  // sp is reused by a second merge
+    return acc;
+  };
+  const DiffPartial mine = block_merge(p);
+  if (threadIdx.x == 0) {
+    parts[blockIdx.x] = mine;
     __threadfence();
     const uint32_t prev = atomicAdd(counter, 1u);
     am_last = prev == gridDim.x - 1;
   }
   __syncthreads();
-  if (am_last && threadIdx.x == 0) {
+  if (am_last) {
+    // the last block folds every block's partial: thread t takes blocks t,
+    // t + 256, ... in order, then the same fixed-order merge (partials read
+    // from L2: they were written by other SMs)
     __threadfence();
-    DiffPartial acc;
-    init(acc);
-    for (unsigned blk = 0; blk < gridDim.x; ++blk) {
+    DiffPartial v;
+    init(v);
+    for (unsigned blk = threadIdx.x; blk < gridDim.x; blk += kDiffThreads) {
+      const DiffPartial* src = parts + blk;
       DiffPartial q;
-      const volatile DiffPartial* src = parts + blk;
-      q.max_excess = src->max_excess;
-      q.max_abs = src->max_abs;
-      q.amax_a = src->amax_a;
-      q.amax_b = src->amax_b;
-      q.excess_index = src->excess_index;
-      q.over = src->over;
-      q.viol = src->viol;
-      q.first_viol = src->first_viol;
-      q.mism = src->mism;
-      q.first_mism = src->first_mism;
-      q.nan_ex = src->nan_ex;
-      q.dab = src->dab;
-      q.daa = src->daa;
-      q.dbb = src->dbb;
-      merge(acc, q);
+      q.max_excess = __ldcg(&src->max_excess);
+      q.max_abs = __ldcg(&src->max_abs);
+      q.amax_a = __ldcg(&src->amax_a);
+      q.amax_b = __ldcg(&src->amax_b);
+      q.excess_index = __ldcg(reinterpret_cast<const long long*>(&src->excess_index));
+      q.over = __ldcg(reinterpret_cast<const long long*>(&src->over));
+      q.viol = __ldcg(reinterpret_cast<const long long*>(&src->viol));
+      q.first_viol = __ldcg(reinterpret_cast<const long long*>(&src->first_viol));
+      q.mism = __ldcg(reinterpret_cast<const long long*>(&src->mism));
+      q.first_mism = __ldcg(reinterpret_cast<const long long*>(&src->first_mism));
+      q.nan_ex = __ldcg(reinterpret_cast<const long long*>(&src->nan_ex));
+      q.dab = __ldcg(&src->dab);
+      q.daa = __ldcg(&src->daa);
+      q.dbb = __ldcg(&src->dbb);
+      merge(v, q);
     }
+    const DiffPartial acc = block_merge(v);
+    if (threadIdx.x != 0) return;
     out->max_excess = acc.max_excess;
     out->max_abs = acc.max_abs;
     out->dot_ab = acc.dab;
