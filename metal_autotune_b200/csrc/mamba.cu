@@ -5,8 +5,11 @@
 // order; y_t = sum_s C[t,s] h[s] is a shuffle reduction inside the channel's
 // lane group. The recurrence is sequential in t, so one channel's latency
 // is L dependent steps; channels are independent (2048 per Mamba-370m
-// layer) and fill the GPU. Inputs of step t+1 are loaded while step t
-// computes.
+// layer) and fill the GPU. Steps run in chunks of 8: the chunk's inputs load
+// while the previous chunk computes; inside a chunk the step-independent
+// arithmetic (softplus and gate once per channel, spread over the group's
+// lanes; exp(dt A), dt B x) runs for all 8 steps side by side, then the
+// recurrence in h, then 8 interleaved reductions over the states.
 #include "mt_common.cuh"
 
 namespace mt {
@@ -39,28 +42,82 @@ __global__ void __launch_bounds__(256) mamba_scan_kernel(const void* __restrict_
   const float bias = dt_bias ? dt_bias[cc] : 0.f;
   const float dd = Dv ? Dv[cc] : 0.f;
   float h = (hstate && active) ? hstate[static_cast<int64_t>(cc) * NS + s] : 0.f;
-  float nx = Elem<DT>::to_f(x[cc]), ndt = Elem<DT>::to_f(dtr[cc]), nz = Elem<DT>::to_f(z[cc]);
-  float nb = Elem<DT>::to_f(Bm[s]), nc = Elem<DT>::to_f(Cm[s]);
-  for (int t = 0; t < L; ++t) {
-    const float xv = nx, dv = ndt, zv = nz, bv = nb, cv = nc;
-    if (t + 1 < L) {
-      const int64_t r = static_cast<int64_t>(t + 1);
-      nx = Elem<DT>::to_f(x[r * d_inner + cc]);
-      ndt = Elem<DT>::to_f(dtr[r * d_inner + cc]);
-      nz = Elem<DT>::to_f(z[r * d_inner + cc]);
-      nb = Elem<DT>::to_f(Bm[r * NS + s]);
-      nc = Elem<DT>::to_f(Cm[r * NS + s]);
-    }
-    const float dt = softplus_f32(__fadd_rn(dv, bias));
-    const float dA = expf(__fmul_rn(dt, a));
-    h = __fadd_rn(__fmul_rn(dA, h), __fmul_rn(__fmul_rn(dt, bv), xv));
-    float part = __fmul_rn(cv, h);
+  // the inputs of the next kCh steps load while the current kCh steps run
+  // (one step's arithmetic is far shorter than a memory round trip)
+  constexpr int kCh = 8;
+  float cx[kCh], cdt[kCh], cz[kCh], cb[kCh], ccv[kCh];
+  auto fetch = [&](int t0, float (&fx)[kCh], float (&fdt)[kCh], float (&fz)[kCh], float (&fb)[kCh],
+                   float (&fc)[kCh]) {
 #pragma unroll
-    for (int o = NS / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (s == 0 && active) {
-      const float yv = __fadd_rn(part, __fmul_rn(dd, xv));
-      const float sg = 1.0f / (1.0f + expf(-zv));
-      y[static_cast<int64_t>(t) * d_inner + c] = Elem<DT>::from_f(__fmul_rn(yv, __fmul_rn(zv, sg)));
+    for (int j = 0; j < kCh; ++j) {
+      const int64_t r = t0 + j;
+      if (r < L) {
+        fx[j] = Elem<DT>::to_f(x[r * d_inner + cc]);
+        fdt[j] = Elem<DT>::to_f(dtr[r * d_inner + cc]);
+        fz[j] = Elem<DT>::to_f(z[r * d_inner + cc]);
+        fb[j] = Elem<DT>::to_f(Bm[r * NS + s]);
+        fc[j] = Elem<DT>::to_f(Cm[r * NS + s]);
+      } else {
+        fx[j] = fdt[j] = fz[j] = fb[j] = fc[j] = 0.f;
+      }
+    }
+  };
+  fetch(0, cx, cdt, cz, cb, ccv);
+  for (int t0 = 0; t0 < L; t0 += kCh) {
+    float px[kCh], pdt[kCh], pz[kCh], pb[kCh], pc[kCh];
+    fetch(t0 + kCh, px, pdt, pz, pb, pc);
+    // the step-independent arithmetic of the chunk first (kCh steps side by
+    // side), then the short recurrence in h, then kCh interleaved reductions
+    // over the states; each step's operations and roundings are the same as
+    // in one step at a time
+    // lane s of a channel's group evaluates the per-channel softplus (and
+    // below the output gate) of step s mod kCh only; the group shares them
+    // by shuffles
+    const int jm = s % kCh;
+    const int gbase = lane - s;  // first lane of the channel's group
+    float dtm = cdt[0], xm = cx[0], zm = cz[0];
+#pragma unroll
+    for (int j = 1; j < kCh; ++j)
+      if (j == jm) {
+        dtm = cdt[j];
+        xm = cx[j];
+        zm = cz[j];
+      }
+    dtm = softplus_f32(__fadd_rn(dtm, bias));
+    float dA[kCh], u[kCh], part[kCh];
+#pragma unroll
+    for (int j = 0; j < kCh; ++j) {
+      const float dt = __shfl_sync(0xffffffffu, dtm, gbase + j);
+      dA[j] = expf(__fmul_rn(dt, a));
+      u[j] = __fmul_rn(__fmul_rn(dt, cb[j]), cx[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < kCh; ++j) {
+      if (t0 + j < L) h = __fadd_rn(__fmul_rn(dA[j], h), u[j]);
+      part[j] = __fmul_rn(ccv[j], h);
+    }
+#pragma unroll
+    for (int o = NS / 2; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < kCh; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j], o);
+    // lane s < kCh of the group finishes and stores step s of the chunk
+    float pm = part[0];
+#pragma unroll
+    for (int j = 1; j < kCh; ++j)
+      if (j == jm) pm = part[j];
+    const int t = t0 + jm;
+    if (s < kCh && active && t < L) {
+      const float yv = __fadd_rn(pm, __fmul_rn(dd, xm));
+      const float sg = 1.0f / (1.0f + expf(-zm));
+      y[static_cast<int64_t>(t) * d_inner + c] = Elem<DT>::from_f(__fmul_rn(yv, __fmul_rn(zm, sg)));
+    }
+#pragma unroll
+    for (int j = 0; j < kCh; ++j) {
+      cx[j] = px[j];
+      cdt[j] = pdt[j];
+      cz[j] = pz[j];
+      cb[j] = pb[j];
+      ccv[j] = pc[j];
     }
   }
   if (hstate && active) hstate[static_cast<int64_t>(c) * NS + s] = h;
