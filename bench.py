@@ -480,6 +480,20 @@ def run_kernels(args, cfg):
           8 * 3000 * (128 + 1280) * 2)
     bench("whisper_conv2", lambda: lib.conv1d(h1, w2, bw, stride=2, padding=1, act=1), 2 * 8 * 1500 * 1280 * 3 * 1280,
           8 * (3000 + 1500) * 1280 * 2)
+    # the elementwise and normalisation regions at the other targets' sizes (HBM-bound)
+    xl = torch.randn(8 * 2048, 4096, device="cuda").to(torch.bfloat16)
+    wl = torch.ones(4096, device="cuda", dtype=torch.bfloat16)
+    bench("llama_rms_norm", lambda: lib.rms_norm(xl, wl, 1e-5), 0, 2 * xl.numel() * 2)
+    xr = torch.randn(8, 32, 2048, 128, device="cuda").to(torch.bfloat16)
+    bench("llama_rope", lambda: lib.rope(xr, 128, base=5e5, offset=0), 0, 2 * xr.numel() * 2)
+    gl = torch.randn(8 * 2048, 14336, device="cuda").to(torch.bfloat16)
+    ul = torch.randn(8 * 2048, 14336, device="cuda").to(torch.bfloat16)
+    bench("llama_swiglu", lambda: lib.swiglu(gl, ul), 0, 3 * gl.numel() * 2)
+    del gl, ul
+    xln = torch.randn(8 * 1500, 1280, device="cuda").to(torch.float16)
+    wln = torch.ones(1280, device="cuda", dtype=torch.float16)
+    bln = torch.zeros(1280, device="cuda", dtype=torch.float16)
+    bench("whisper_layer_norm", lambda: lib.layer_norm(xln, wln, bln, 1e-5), 0, 2 * xln.numel() * 2)
     # Mamba-370m layer at 512 steps (d_inner 2048, d_state 16, fp16): depthwise causal conv + selective scan
     Lm, Dm, NSm = 512, 2048, 16
     xm_ = torch.randn(Lm, Dm, device="cuda").to(torch.float16)

@@ -17,7 +17,28 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const void* __restrict__ gp
   const T* u = static_cast<const T*>(up);
   T* y = static_cast<T*>(yp);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
+  if (((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
+    // 16-byte vectors, the same per-element arithmetic; the tail past the
+    // last whole vector element by element
+    const int64_t nv = n / V;
+    for (int64_t v = tid; v < nv; v += stride) {
+      const uint4 gv = *reinterpret_cast<const uint4*>(g + v * V);
+      const uint4 uv = *reinterpret_cast<const uint4*>(u + v * V);
+      uint4 yv;
+      const T* ge = reinterpret_cast<const T*>(&gv);
+      const T* ue = reinterpret_cast<const T*>(&uv);
+      T* ye = reinterpret_cast<T*>(&yv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) ye[e] = Elem<DT>::from_f(swiglu_rounded<DT>(Elem<DT>::to_f(ge[e]), Elem<DT>::to_f(ue[e])));
+      *reinterpret_cast<uint4*>(y + v * V) = yv;
+    }
+    for (int64_t i = nv * V + tid; i < n; i += stride)
+      y[i] = Elem<DT>::from_f(swiglu_rounded<DT>(Elem<DT>::to_f(g[i]), Elem<DT>::to_f(u[i])));
+    return;
+  }
+  for (int64_t i = tid; i < n; i += stride)
     y[i] = Elem<DT>::from_f(swiglu_rounded<DT>(Elem<DT>::to_f(g[i]), Elem<DT>::to_f(u[i])));
 }
 
@@ -195,7 +216,7 @@ int mt_swiglu(const void* gate, const void* up, void* y, int64_t n, int dtype, m
   int rc = device_sm_count(&sms);
   if (rc) return rc;
   const int64_t want = (n + 255) / 256;
-  const dim3 grid(static_cast<unsigned>(want < sms * 16 ? want : sms * 16));
+  const dim3 grid(static_cast<unsigned>(want < sms * 16 ? want : sms * 16));  // grid-stride loops
   switch (dtype) {
     case MT_BF16: return launch(swiglu_kernel<MT_BF16>, grid, dim3(256), 0, (cudaStream_t)stream, gate, up, y, n);
     case MT_F16: return launch(swiglu_kernel<MT_F16>, grid, dim3(256), 0, (cudaStream_t)stream, gate, up, y, n);

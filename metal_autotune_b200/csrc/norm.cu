@@ -205,38 +205,49 @@ __global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict_
   }
 }
 
-// x, y: [B*H, L, D]; one thread per (row, pair j < dims/2) plus tail copies.
+// x, y: [B*H, L, D]. One CTA per position l and group of kRopeRows of the
+// B*H rows at that position: the CTA computes the angles of its position once
+// (dims/2 of them, shared memory), then its threads take (row, pair j) items
+// plus the tail copies past `dims`. The angle expression is the per-element
+// one, so the result does not depend on the grouping.
+constexpr int kRopeRows = 32;
 template <int DT>
 __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, void* __restrict__ yp,
-                                                   int64_t rows, int L, int D, int dims, int traditional,
+                                                   int64_t BH, int L, int D, int dims, int traditional,
                                                    float scale, int64_t offset, const RopeFreqs f) {
   using T = typename Elem<DT>::T;
+  __shared__ float2 cs[128];
   griddep_wait();
   griddep_launch();  // dependents may launch now; their own wait covers this grid
+  const int l = blockIdx.x;
   const int half = dims / 2;
-  const int per_row = half + (D - dims);
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= rows * per_row) return;
-  const int64_t row = idx / per_row;
-  const int j = static_cast<int>(idx % per_row);
-  const int l = static_cast<int>(row % L);
-  const T* x = static_cast<const T*>(xp) + row * D;
-  T* y = static_cast<T*>(yp) + row * D;
-  if (j >= half) {  // tail beyond `dims` copies through
-    const int d = dims + (j - half);
-    y[d] = x[d];
-    return;
-  }
   const float pos = __fmul_rn(static_cast<float>(static_cast<int64_t>(l) + offset), scale);
-  const float th = __fmul_rn(pos, f.inv_freq[j]);
-  float s, c;
-  sincosf(th, &s, &c);
-  const int d0 = traditional ? 2 * j : j;
-  const int d1 = traditional ? 2 * j + 1 : j + half;
-  float o0, o1;
-  rope_pair(Elem<DT>::to_f(x[d0]), Elem<DT>::to_f(x[d1]), c, s, o0, o1);
-  y[d0] = Elem<DT>::from_f(o0);
-  y[d1] = Elem<DT>::from_f(o1);
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    float sn, cn;
+    sincosf(__fmul_rn(pos, f.inv_freq[j]), &sn, &cn);
+    cs[j] = make_float2(sn, cn);
+  }
+  __syncthreads();
+  const int per_row = half + (D - dims);
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRopeRows;
+  const int64_t nr = (BH - r0) < kRopeRows ? (BH - r0) : kRopeRows;
+  for (int64_t i = threadIdx.x; i < nr * per_row; i += blockDim.x) {
+    const int64_t row = (r0 + i / per_row) * L + l;
+    const int j = static_cast<int>(i % per_row);
+    const T* x = static_cast<const T*>(xp) + row * D;
+    T* y = static_cast<T*>(yp) + row * D;
+    if (j >= half) {  // tail beyond `dims` copies through
+      const int d = dims + (j - half);
+      y[d] = x[d];
+      continue;
+    }
+    const int d0 = traditional ? 2 * j : j;
+    const int d1 = traditional ? 2 * j + 1 : j + half;
+    float o0, o1;
+    rope_pair(Elem<DT>::to_f(x[d0]), Elem<DT>::to_f(x[d1]), cs[j].y, cs[j].x, o0, o1);
+    y[d0] = Elem<DT>::from_f(o0);
+    y[d1] = Elem<DT>::from_f(o1);
+  }
 }
 
 // Qwen3 attention prologue, D = 128: warp per (token, head) over Hq + Hkv heads.
@@ -384,11 +395,12 @@ int mt_rope(const void* x, void* y, int64_t B, int64_t H, int64_t L, int64_t D, 
   MT_CHECK_ARG(base > 0.f, "mt_rope: base must be positive");
   const int64_t rows = B * H * L;
   if (rows == 0) return MT_OK;
+  MT_CHECK_ARG(L < (int64_t(1) << 31) && (B * H + kRopeRows - 1) / kRopeRows < 65536,
+               "mt_rope: L=%lld or B*H=%lld too large for the grid", (long long)L, (long long)(B * H));
   const RopeFreqs f = make_freqs(dims, base);
-  const int64_t total = rows * (dims / 2 + (D - dims));
-  const dim3 grid(static_cast<unsigned>((total + 255) / 256));
+  const dim3 grid(static_cast<unsigned>(L), static_cast<unsigned>((B * H + kRopeRows - 1) / kRopeRows));
   int rc = MT_OK;
-  MT_DT_SWITCH(dtype, rc = launch(rope_kernel<DT>, grid, dim3(256), 0, (cudaStream_t)stream, x, y, rows, (int)L,
+  MT_DT_SWITCH(dtype, rc = launch(rope_kernel<DT>, grid, dim3(256), 0, (cudaStream_t)stream, x, y, B * H, (int)L,
                                   (int)D, dims, traditional, scale, offset, f));
   return rc;
 }
