@@ -214,7 +214,7 @@ constexpr int kRopeRows = 32;
 template <int DT>
 __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, void* __restrict__ yp,
                                                    int64_t BH, int L, int D, int dims, int traditional,
-                                                   float scale, int64_t offset, const RopeFreqs f) {
+                                                   float scale, int64_t offset, const RopeFreqs f, int vec) {
   using T = typename Elem<DT>::T;
   __shared__ float2 cs[128];
   griddep_wait();
@@ -228,9 +228,63 @@ __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, 
     cs[j] = make_float2(sn, cn);
   }
   __syncthreads();
-  const int per_row = half + (D - dims);
   const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRopeRows;
   const int64_t nr = (BH - r0) < kRopeRows ? (BH - r0) : kRopeRows;
+  if (vec) {
+    // 4 pairs per item (8-byte accesses), then the tail copies
+    const int hv = half / 4, per_row = hv + (D - dims);
+    for (int64_t i = threadIdx.x; i < nr * per_row; i += blockDim.x) {
+      const int64_t row = (r0 + i / per_row) * L + l;
+      const int q = static_cast<int>(i % per_row);
+      const T* x = static_cast<const T*>(xp) + row * D;
+      T* y = static_cast<T*>(yp) + row * D;
+      if (q >= hv) {
+        const int d = dims + (q - hv);
+        y[d] = x[d];
+        continue;
+      }
+      const int j0 = 4 * q;
+      T a[4], b[4];
+      if (traditional) {  // pairs (2j, 2j+1): 8 consecutive values
+        const uint2 lo = *reinterpret_cast<const uint2*>(x + 2 * j0), hi = *reinterpret_cast<const uint2*>(x + 2 * j0 + 4);
+        const T* e0 = reinterpret_cast<const T*>(&lo);
+        const T* e1 = reinterpret_cast<const T*>(&hi);
+        a[0] = e0[0]; b[0] = e0[1]; a[1] = e0[2]; b[1] = e0[3];
+        a[2] = e1[0]; b[2] = e1[1]; a[3] = e1[2]; b[3] = e1[3];
+      } else {  // pairs (j, j + half)
+        const uint2 va = *reinterpret_cast<const uint2*>(x + j0), vb = *reinterpret_cast<const uint2*>(x + j0 + half);
+        const T* ea = reinterpret_cast<const T*>(&va);
+        const T* eb = reinterpret_cast<const T*>(&vb);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          a[e] = ea[e];
+          b[e] = eb[e];
+        }
+      }
+      T oa[4], ob[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float o0, o1;
+        rope_pair(Elem<DT>::to_f(a[e]), Elem<DT>::to_f(b[e]), cs[j0 + e].y, cs[j0 + e].x, o0, o1);
+        oa[e] = Elem<DT>::from_f(o0);
+        ob[e] = Elem<DT>::from_f(o1);
+      }
+      if (traditional) {
+        uint2 lo, hi;
+        T* e0 = reinterpret_cast<T*>(&lo);
+        T* e1 = reinterpret_cast<T*>(&hi);
+        e0[0] = oa[0]; e0[1] = ob[0]; e0[2] = oa[1]; e0[3] = ob[1];
+        e1[0] = oa[2]; e1[1] = ob[2]; e1[2] = oa[3]; e1[3] = ob[3];
+        *reinterpret_cast<uint2*>(y + 2 * j0) = lo;
+        *reinterpret_cast<uint2*>(y + 2 * j0 + 4) = hi;
+      } else {
+        *reinterpret_cast<uint2*>(y + j0) = *reinterpret_cast<const uint2*>(oa);
+        *reinterpret_cast<uint2*>(y + j0 + half) = *reinterpret_cast<const uint2*>(ob);
+      }
+    }
+    return;
+  }
+  const int per_row = half + (D - dims);
   for (int64_t i = threadIdx.x; i < nr * per_row; i += blockDim.x) {
     const int64_t row = (r0 + i / per_row) * L + l;
     const int j = static_cast<int>(i % per_row);
@@ -400,8 +454,10 @@ int mt_rope(const void* x, void* y, int64_t B, int64_t H, int64_t L, int64_t D, 
   const RopeFreqs f = make_freqs(dims, base);
   const dim3 grid(static_cast<unsigned>(L), static_cast<unsigned>((B * H + kRopeRows - 1) / kRopeRows));
   int rc = MT_OK;
+  // 4 pairs per thread when every row and both halves start on 8 bytes
+  const int vec = dtype != MT_F32 && (dims / 2) % 4 == 0 && D % 4 == 0 && aligned(x, 8) && aligned(y, 8);
   MT_DT_SWITCH(dtype, rc = launch(rope_kernel<DT>, grid, dim3(256), 0, (cudaStream_t)stream, x, y, B * H, (int)L,
-                                  (int)D, dims, traditional, scale, offset, f));
+                                  (int)D, dims, traditional, scale, offset, f, vec));
   return rc;
 }
 
