@@ -171,6 +171,59 @@ static int rms_norm_reg_launch(const void* x, const void* res, const void* w, fl
   }
 }
 
+// layer norm with the row held in registers (dim = 256 * NC, bf16/f16): lane
+// l owns the 8-value chunks l, l+32, ...; one read of the row, then the same
+// two passes (mean, centred variance) and affine as layer_norm_kernel, with
+// each lane's partial sums taken over its chunks.
+template <int DT, int NC>
+__global__ void __launch_bounds__(128) layer_norm_reg_kernel(const void* __restrict__ xp, const void* __restrict__ wp,
+                                                             const void* __restrict__ bp, float eps,
+                                                             void* __restrict__ yp, int64_t rows) {
+  using T = typename Elem<DT>::T;
+  constexpr int dim = 256 * NC;
+  griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* x = static_cast<const T*>(xp) + row * dim;
+  float v[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) load8<DT>(x + lane * 8 + c * 256, v[c]);
+  float sx = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sx += v[c][e];
+  sx = warp_sum(sx);
+  const float mean = __fdiv_rn(sx, static_cast<float>(dim));
+  float sv = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float d = __fsub_rn(v[c][e], mean);
+      sv = fmaf(d, d, sv);
+    }
+  sv = warp_sum(sv);
+  const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sv, static_cast<float>(dim)), eps));
+  T* y = static_cast<T*>(yp) + row * dim;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    float g[8], bb[8], o[8];
+    if (wp) load8<DT>(static_cast<const T*>(wp) + lane * 8 + c * 256, g);
+    if (bp) load8<DT>(static_cast<const T*>(bp) + lane * 8 + c * 256, bb);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float u = __fmul_rn(__fsub_rn(v[c][e], mean), scale);
+      if (wp) u = __fmul_rn(u, g[e]);
+      if (bp) u = __fadd_rn(u, bb[e]);
+      o[e] = u;
+    }
+    store8<DT>(y + lane * 8 + c * 256, o);
+  }
+}
+
 // two-pass layer norm: mean, centred variance, optional affine
 template <int DT>
 __global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict__ xp, const void* __restrict__ wp,
@@ -432,6 +485,28 @@ int mt_layer_norm(const void* x, const void* w, const void* b, float eps, void* 
   MT_CHECK_ARG(rows >= 0 && dim > 0 && dim <= (1 << 24), "mt_layer_norm: rows=%lld dim=%lld", (long long)rows,
                (long long)dim);
   if (rows == 0) return MT_OK;
+  const bool vec = (dtype == MT_BF16 || dtype == MT_F16) && dim % 256 == 0 && dim <= 4096 && aligned(x, 16) &&
+                   aligned(y, 16) && (!w || aligned(w, 16)) && (!b || aligned(b, 16));
+  if (vec) {
+    const dim3 g4(static_cast<unsigned>((rows + 3) / 4)), blk(128);
+    const cudaStream_t s = (cudaStream_t)stream;
+#define MT_LN_REG(DTV)                                                                                         \
+  switch (dim / 256) {                                                                                         \
+    case 1: return launch(layer_norm_reg_kernel<DTV, 1>, g4, blk, 0, s, x, w, b, eps, y, rows);                \
+    case 2: return launch(layer_norm_reg_kernel<DTV, 2>, g4, blk, 0, s, x, w, b, eps, y, rows);                \
+    case 3: return launch(layer_norm_reg_kernel<DTV, 3>, g4, blk, 0, s, x, w, b, eps, y, rows);                \
+    case 4: return launch(layer_norm_reg_kernel<DTV, 4>, g4, blk, 0, s, x, w, b, eps, y, rows);                \
+    case 5: return launch(layer_norm_reg_kernel<DTV, 5>, g4, blk, 0, s, x, w, b, eps, y, rows);                \
+    case 6: return launch(layer_norm_reg_kernel<DTV, 6>, g4, blk, 0, s, x, w, b, eps, y, rows);                \
+    case 8: return launch(layer_norm_reg_kernel<DTV, 8>, g4, blk, 0, s, x, w, b, eps, y, rows);                \
+    case 10: return launch(layer_norm_reg_kernel<DTV, 10>, g4, blk, 0, s, x, w, b, eps, y, rows);              \
+    case 12: return launch(layer_norm_reg_kernel<DTV, 12>, g4, blk, 0, s, x, w, b, eps, y, rows);              \
+    case 16: return launch(layer_norm_reg_kernel<DTV, 16>, g4, blk, 0, s, x, w, b, eps, y, rows);              \
+    default: break;                                                                                            \
+  }
+    if (dtype == MT_BF16) { MT_LN_REG(MT_BF16) } else { MT_LN_REG(MT_F16) }
+#undef MT_LN_REG
+  }
   const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
   int rc = MT_OK;
   MT_DT_SWITCH(dtype, rc = launch(layer_norm_kernel<DT>, grid, dim3(256), 0, (cudaStream_t)stream, x, w, b, eps, y,
