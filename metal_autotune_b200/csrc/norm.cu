@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(128) rms_norm_reg_kernel(const void* __restric
   constexpr int dim = 256 * NC;
   griddep_wait();
   griddep_launch();  // dependents may launch now; their own wait covers this grid
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const T* x = static_cast<const T*>(xp) + row * dim;
@@ -160,7 +160,10 @@ __global__ void __launch_bounds__(128) rms_norm_reg_kernel(const void* __restric
 template <int DT, bool HAS_RES>
 static int rms_norm_reg_launch(const void* x, const void* res, const void* w, float eps, void* h, void* y,
                                int64_t rows, int64_t dim, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>((rows + 3) / 4)), block(128);
+  // up to 1024 rows: a warp per CTA, so the rows spread over more SMs (each
+  // row is one memory round trip); more rows: 4 warps per CTA
+  const int wpb = rows <= 1024 ? 1 : 4;
+  const dim3 grid(static_cast<unsigned>((rows + wpb - 1) / wpb)), block(32 * wpb);
   switch (dim) {
     case 1024: return launch(rms_norm_reg_kernel<DT, HAS_RES, 4>, grid, block, 0, stream, x, res, w, eps, h, y, rows);
     case 2048: return launch(rms_norm_reg_kernel<DT, HAS_RES, 8>, grid, block, 0, stream, x, res, w, eps, h, y, rows);
