@@ -240,7 +240,9 @@ struct DecodeAttnParams {
   float scale_log2;
 };
 
-template <int DT>
+// ITEMS: prologue rows per warp (R + T rows over 8 warps: 1 when R + T <= 8,
+// the Qwen3 decode case, which keeps one inlined copy of the norm + RoPE code)
+template <int DT, int ITEMS>
 __global__ void __launch_bounds__(kDaWarps * 32, 1)
     decode_attn_kernel(const __grid_constant__ DecodeAttnParams p, const __grid_constant__ RopeFreqs f) {
   using T = typename Elem<DT>::T;
@@ -282,7 +284,7 @@ __global__ void __launch_bounds__(kDaWarps * 32, 1)
 
   // prologue: items i = warp, warp + 8, ... over the R q rows, then the T
   // new k rows; every item's loads are issued before any is computed
-  constexpr int kItems = (16 + 4 + kDaWarps - 1) / kDaWarps;  // R + T <= 20
+  constexpr int kItems = ITEMS;  // R + T <= ITEMS * kDaWarps
   uint2 xr[kItems], wr[kItems], vr[kItems];
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
@@ -532,7 +534,9 @@ extern "C" int mt_qk_norm_rope_sdpa_decode(const void* q, const void* k, const v
     if (int e = ensure_smem(kern, kDaSmem)) return e;
     return launch(kern, dim3(static_cast<unsigned>(Hkv)), dim3(kDaWarps * 32), kDaSmem, (cudaStream_t)stream, p, f);
   };
-  return dtype == MT_BF16 ? run(decode_attn_kernel<MT_BF16>) : run(decode_attn_kernel<MT_F16>);
+  const bool one = (Hq / Hkv) * T + T <= kDaWarps;
+  if (dtype == MT_BF16) return one ? run(decode_attn_kernel<MT_BF16, 1>) : run(decode_attn_kernel<MT_BF16, 3>);
+  return one ? run(decode_attn_kernel<MT_F16, 1>) : run(decode_attn_kernel<MT_F16, 3>);
 }
 
 extern "C" int mt_sdpa(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv,
