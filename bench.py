@@ -536,13 +536,123 @@ def run_kernels(args, cfg):
 
 
 # ------------------------------------------------------------------ main
+LLAMA_B, LLAMA_L = 8, 2048
+
+
+def run_llama_tp(args):
+    """Llama-3-8B 8-bit, batch 8 x prefill 2048, tensor-parallel over the
+    ranks (one shard per GPU, NCCL all-reduce after o_proj and down).
+
+      value  prompt tokens/s of the whole job (8 x 2048 / forward time),
+             CUDA events around K forwards, max over ranks
+      e2e    the same with pinned host tokens copied in and rank 0's
+             last-position logits read back every forward
+      roofline  the whole forward per GPU: its algorithmic FLOPs / tp over
+             the forward time, against the sustained bf16 peak; plus the
+             gate/up qmm+SwiGLU (the largest kernel) timed alone."""
+    import torch
+
+    from metal_autotune_b200 import build, lib, workload
+    from metal_autotune_b200.targets import llama_tp
+    build.build_library()
+    rank, world, local = dist_setup()
+    cfg = llama_tp.LLAMA3_8B if args.config == "llama3_8b_tp" else llama_tp.TINY
+    B, L = (LLAMA_B, LLAMA_L) if cfg.layers == 32 else (2, 128)
+    comm = llama_tp.ProcessGroupComm() if world > 1 else llama_tp.LocalComm()
+    t0 = time.time()
+    model = llama_tp.LlamaTP(cfg, world, [rank], comm, seed=0, device="cuda")
+    torch.cuda.synchronize()
+    log(f"rank {rank}: built Llama shard {rank}/{world} ({cfg.layers} layers) in {time.time() - t0:.1f}s, "
+        f"{torch.cuda.memory_allocated() / 2**30:.1f} GiB")
+    tokens = workload.seeded_tokens((B, L), 0, cfg.vocab, seed=0)
+    host_tokens = tokens.cpu().pin_memory()
+    host_logits = torch.empty(B, cfg.vocab, dtype=torch.bfloat16).pin_memory()
+    out = {}
+
+    def step():
+        out["logits"] = model(tokens)
+
+    def e2e_step():
+        tokens.copy_(host_tokens, non_blocking=True)
+        out["logits"] = model(tokens)
+        host_logits.copy_(out["logits"], non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    calls0 = lib.CALLS[0]
+    with ClockSampler(local) as clk:
+        ms_total = time_region(step, args.steps, world)
+        ms_e2e_total = time_region(e2e_step, args.steps, world)
+    launches = lib.CALLS[0] - calls0
+    ms = max_over_ranks(ms_total / args.steps, world)
+    ms_e2e = max_over_ranks(ms_e2e_total / args.steps, world)
+    status = lib.device_status(clear=True)
+    if status != 0:
+        raise RuntimeError(f"device status {status:#x}: a kernel's bounded wait expired")
+    if not bool(torch.isfinite(out["logits"].float()).all()):
+        raise RuntimeError("non-finite logits")
+
+    # the largest kernel alone: gate/up qmm + SwiGLU of layer 0 on this shard
+    peaks = measured_peaks()
+    sl = model.shards[0].layers[0]
+    xn = torch.randn(B * L, cfg.hidden, device="cuda", dtype=torch.bfloat16)
+    act = torch.empty(B * L, sl.gate[0].shape[0], device="cuda", dtype=torch.bfloat16)
+    run = lambda: lib.quantized_matmul_swiglu(xn, *sl.gate, *sl.up, group_size=cfg.group, bits=cfg.bits, out=act)
+    for _ in range(3):
+        run()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda.synchronize()
+    ev[0].record()
+    for _ in range(10):
+        run()
+    ev[1].record()
+    torch.cuda.synchronize()
+    k_ms = ev[0].elapsed_time(ev[1]) / 10
+    k_flops = 2 * B * L * 2 * sl.gate[0].shape[0] * cfg.hidden
+    fwd_flops = llama_tp.forward_flops(cfg, B, L)
+    sustained = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
+    achieved = fwd_flops / world / (ms / 1e3) / 1e12
+    roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": sustained, "unit": "TFLOP/s",
+            "frac": round(achieved / sustained, 4), "traffic": None, "peak_source": f"{peaks['source']} sustained",
+            "what": "whole forward per GPU (algorithmic FLOPs / tp / forward time)",
+            "forward_tflop": round(fwd_flops / 1e12, 3),
+            "gate_up_swiglu": {"ms": round(k_ms, 4), "tflops": round(k_flops / (k_ms / 1e3) / 1e12, 2),
+                               "frac_of_burst": round(k_flops / (k_ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
+                               "M": B * L, "N": 2 * sl.gate[0].shape[0], "K": cfg.hidden}}
+    if rank != 0:
+        barrier(world)
+        return 0
+    line = {
+        "metric": "Llama-3-8B-8bit prefill tok/s (batch 8 x 2048), tensor-parallel",
+        "value": round(B * L / (ms / 1e3), 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "llama3_8b_prefill_8x2048" if cfg.layers == 32 else "llama_tiny",
+                   "model": "Llama-3-8B 8-bit affine g64, random init" if cfg.layers == 32 else "tiny Llama",
+                   "batch": B, "prompt_tokens": L, "parallelism": f"tp{world}",
+                   "collective": "NCCL all-reduce (bf16) after o_proj and down, all-gather of lm_head rows",
+                   "l2": "inputs larger than L2 (8.5 GB of packed weights per forward / tp)"},
+        "e2e": {"value": round(B * L / (ms_e2e / 1e3), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": B * L * 4, "d2h_bytes_per_step": B * cfg.vocab * 2},
+        "roofline": roof, "clocks": clk.summary(), "gpu_launches": launches,
+    }
+    barrier(world)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None, help="default 300 (Qwen3 request), 5 (Llama forward)")
+    ap.add_argument("--warmup", type=int, default=None, help="default 10 (Qwen3 request), 3 (Llama forward)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3_4b", choices=["qwen3_4b", "qwen3_tiny"])
+    ap.add_argument("--config", default="qwen3_4b", choices=["qwen3_4b", "qwen3_tiny", "llama3_8b_tp", "llama_tiny_tp"],
+                    help="llama*_tp: Llama-3-8B 8-bit prefill 8 x 2048, tensor-parallel over the ranks")
     ap.add_argument("--mode", default="request", choices=["request", "kernels"])
     ap.add_argument("--only", default="", help="kernels mode: comma-separated kernel names")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -550,9 +660,20 @@ def main():
                     help="replay the request W + K times, the K inside an NVTX range 'request', and exit "
                          "(for ncu --nvtx --nvtx-include request/)")
     args = ap.parse_args()
+    llama = args.config.startswith("llama")
+    if args.steps is None:
+        args.steps = 5 if llama else 300
+    if args.warmup is None:
+        args.warmup = 3 if llama else 10
     if args.warmup < 3 and args.mode == "request":
         args.warmup = 3
 
+    if args.config.startswith("llama"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the Llama TP line has no CPU arm; the default "
+                              "Qwen3 line carries the reference arm"}), flush=True)
+            return 0
+        return run_llama_tp(args)
     from metal_autotune_b200.targets import qwen3
     cfg = qwen3.QWEN3_4B if args.config == "qwen3_4b" else qwen3.TINY
 
