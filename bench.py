@@ -521,6 +521,17 @@ def run_kernels(args, cfg):
     kl_ = torch.randn(8, 8, 2048, 128, device="cuda").to(torch.bfloat16)
     bench("llama_sdpa", lambda: lib.sdpa(ql_, kl_, kl_, scale=1.0 / math.sqrt(128), causal=True),
           2 * 8 * 32 * 2048 * 2048 * 128, 0)
+    # Llama-3-8B 8-bit projections at batch 8 x 2048 (tp = 1): the prefill qmm at large M
+    if not only or any(k.startswith("llama_qmm") for k in only):
+        TL = 8 * 2048
+        xl_ = torch.randn(TL, 4096, device="cuda").to(torch.bfloat16)
+        gl_, ul_ = (workload.random_quantized(14336, 4096, bits=8, generator=g) for _ in range(2))
+        dl_ = workload.random_quantized(4096, 14336, bits=8, generator=g)
+        al_ = torch.empty(TL, 14336, device="cuda", dtype=torch.bfloat16)
+        yl_ = torch.empty(TL, 4096, device="cuda", dtype=torch.bfloat16)
+        bench("llama_qmm_gate_up_swiglu", lambda: lib.quantized_matmul_swiglu(xl_, *gl_, *ul_, bits=8, out=al_),
+              2 * TL * 2 * 14336 * 4096, 0)
+        bench("llama_qmm_down", lambda: lib.quantized_matmul(al_, *dl_, bits=8, out=yl_), 2 * TL * 4096 * 14336, 0)
     # mlx-whisper encoder MLP (fp16, 8 clips x 1500 frames): fc1 1280 -> 5120 + GELU, fc2 5120 -> 1280
     xm = torch.randn(8 * 1500, 1280, device="cuda").to(torch.float16)
     f1 = (torch.randn(5120, 1280, device="cuda") / 36).to(torch.float16)
