@@ -2,6 +2,8 @@
 // the choice between the vector kernel (M <= 8, decode) and the tcgen05
 // matrix kernel (prefill).
 #include "mt_common.cuh"
+#include <cstdlib>
+
 #include "qmm_common.cuh"
 
 namespace mt {
@@ -37,13 +39,85 @@ static int check_common(const QmmRequest& r, const char* who) {
   return MT_OK;
 }
 
+// Operand bytes a tensor-core launch keeps live: its block of x rows and its
+// block of weight rows are each held under this, so both stay in the 126 MB
+// L2 while the launch's tiles stream them. One launch over a large M x N
+// spreads its CTAs' contiguous tile ranges over every token tile and every
+// weight tile at once and misses L2 on both (Llama-3-8B gate/up at M = 16384:
+// 20.9 GB read from DRAM per launch for 0.26 GB of operands). The environment
+// variable MT_QMM_L2_BLOCK_BYTES overrides the 40 MB default (tests use a
+// small value to reach the blocked path at small sizes).
+static int64_t l2_block_bytes() {
+  const char* e = getenv("MT_QMM_L2_BLOCK_BYTES");
+  const long long v = e ? atoll(e) : 0;
+  return v > 0 ? static_cast<int64_t>(v) : (int64_t(40) << 20);
+}
+
+// The tensor-core path over blocks of at most mc token rows x nc weight rows,
+// weight blocks outermost so each stays in L2 while the token blocks pass.
+// Only one projection or the SwiGLU pair is split by weight rows (the q/k/v
+// triple only by token rows); outputs and residual keep the full row pitch.
+static int run_tc_blocked(const QmmRequest& r, cudaStream_t stream) {
+  const int64_t esz = 2;
+  const int64_t budget = l2_block_bytes();
+  const bool dual = r.kind == QMM_SWIGLU;
+  int nsets = 0;
+  for (int s = 0; s < 3; ++s) nsets += r.set[s].N > 0 ? 1 : 0;
+  const bool split_n = dual || nsets == 1;
+  int64_t mc = budget / (r.K * esz) / 128 * 128;
+  if (mc < 128) mc = 128;
+  const int64_t sets_n = dual ? 2 : 1;
+  const int64_t row_bytes = sets_n * (r.K * r.bits / 8 + (r.K / r.group) * 2 * esz);
+  const int64_t N0 = r.set[0].N;
+  int64_t nc = N0;
+  if (split_n) {
+    nc = budget / row_bytes / 128 * 128;
+    if (nc < 128) nc = 128;
+    if (nc > N0) nc = N0;
+  }
+  if (r.M <= mc && nc == N0) return qmm_tc_run(r, stream);
+  // equal blocks (multiples of 128) rather than full ones and a small remainder
+  const int64_t nbm = (r.M + mc - 1) / mc, nbn = (N0 + nc - 1) / nc;
+  mc = ((r.M + nbm - 1) / nbm + 127) / 128 * 128;
+  nc = ((N0 + nbn - 1) / nbn + 127) / 128 * 128;
+  const int64_t words = r.K * r.bits / 32, G = r.K / r.group;
+  for (int64_t n0 = 0; n0 < N0; n0 += nc) {
+    for (int64_t m0 = 0; m0 < r.M; m0 += mc) {
+      QmmRequest c = r;
+      c.M = r.M - m0 < mc ? r.M - m0 : mc;
+      c.x = static_cast<const char*>(r.x) + m0 * r.K * esz;
+      int64_t ldy0 = 0;
+      for (int s = 0; s < 3; ++s) {
+        const QmmSetReq& q = r.set[s];
+        if (q.N == 0) continue;
+        QmmSetReq& o = c.set[s];
+        const int64_t ldy = q.ldy > 0 ? q.ldy : q.N;
+        if (s == 0) ldy0 = ldy;
+        o.ldy = ldy;
+        const int64_t col = split_n ? n0 : 0;
+        if (split_n) {
+          o.N = N0 - n0 < nc ? N0 - n0 : nc;
+          o.w = q.w + n0 * words;
+          o.s = static_cast<const char*>(q.s) + n0 * G * esz;
+          o.b = static_cast<const char*>(q.b) + n0 * G * esz;
+        }
+        if (q.y) o.y = static_cast<char*>(q.y) + (m0 * ldy + col) * esz;
+      }
+      if (r.residual) c.residual = static_cast<const char*>(r.residual) + (m0 * ldy0 + (split_n ? n0 : 0)) * esz;
+      const int rc = qmm_tc_run(c, stream);
+      if (rc != MT_OK) return rc;
+    }
+  }
+  return MT_OK;
+}
+
 static int run(const QmmRequest& r, cudaStream_t stream, const char* who) {
   clear_error();
   const int rc = check_common(r, who);
   if (rc != MT_OK) return rc;
   if (r.M == 0) return MT_OK;
   if (r.M <= kQmvMaxRows) return qmv_run(r, stream);
-  return qmm_tc_run(r, stream);
+  return run_tc_blocked(r, stream);
 }
 
 }  // namespace mt

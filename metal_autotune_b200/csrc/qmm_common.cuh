@@ -12,6 +12,7 @@ struct QmmSetReq {
   const void* b;
   void* y;
   int64_t N;
+  int64_t ldy;  // elements between output rows (and residual rows); 0 means N
 };
 
 // One quantized-matmul launch request as the entry points describe it.

@@ -95,6 +95,7 @@ struct QmmTcParams {
   long long units;
   uint64_t c_magic;    // ceil(2^64 / C), 0 when C == 1
   int N[3];
+  int ldy[3];          // output (and residual) row pitch of each set, in elements
   int tile_start[4];   // prefix sums of feature tiles per set
   int M, K, G, group;
   int TN, SS, nk, kind, n_tt, tiles, S, C, acc_slots, vec, sb_vec, gshift;
@@ -402,13 +403,14 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     const TileInfo ti = tile_info(p, tile, DUAL);
     T* y = static_cast<T*>(p.y[DUAL ? 0 : ti.set]);
     const int N = p.N[DUAL ? 0 : ti.set];
+    const int ldy = p.ldy[DUAL ? 0 : ti.set];
     const int n8 = (n_hi - n_lo) >> 3;
     for (int idx = gt; idx < TN * n8; idx += gsize) {
       const int tok = idx / n8, cc = idx - tok * n8;
       const int token = ti.tok0 + tok, nr = n_lo + cc * 8, n = ti.n0 + nr;
       if (token >= p.M || n >= N) continue;
       const T* src = src_tile + tok * pitch + nr;
-      const long long off = static_cast<long long>(token) * N + n;
+      const long long off = static_cast<long long>(token) * ldy + n;
       if (p.vec && n + 8 <= N) {
         uint4 val = *reinterpret_cast<const uint4*>(src);
         if (!DUAL && p.kind == QMM_RESIDUAL) {
@@ -1277,6 +1279,7 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
   for (int s = 0; s < 3; ++s) {
     const QmmSetReq& q = r.set[s];
     p.N[s] = static_cast<int>(q.N);
+    p.ldy[s] = static_cast<int>(q.ldy > 0 ? q.ldy : q.N);
     if (s < nsets && q.N > 0) {
       MT_CHECK_ARG(aligned(q.w, 16), "qmm: packed weights must be 16-byte aligned");
       rc = make_tmap_2d(&p.tmw[s], q.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, words, q.N,
@@ -1287,13 +1290,14 @@ int qmm_tc_run(const QmmRequest& r, cudaStream_t stream) {
       p.b[s] = q.b;
       p.y[s] = q.y;
       if (!dual) ftiles += static_cast<int>((q.N + kBM - 1) / kBM);
-      if (q.y && (!aligned(q.y, 16) || q.N % 8 != 0)) vec = false;
+      if (q.y && (!aligned(q.y, 16) || q.N % 8 != 0 || p.ldy[s] % 8 != 0)) vec = false;
     }
     p.tile_start[s + 1] = ftiles;
   }
   if (dual) {
     ftiles = static_cast<int>((r.set[0].N + kBM - 1) / kBM);
     p.N[1] = p.N[0];
+    p.ldy[1] = p.ldy[0];
   }
   p.vec = vec ? 1 : 0;
   {
