@@ -100,6 +100,10 @@ int mt_sm_count(int* sm_count_out);
  * which may split K and then needs `workspace` (see mt_qmm_workspace_bytes;
  * the workspace must be zero-filled once before first use and is left
  * zeroed by every call that completes).
+ * A product whose x rows or weight rows exceed an L2-sized block (60 MB of
+ * operand bytes; environment variable MT_QMM_L2_BLOCK_BYTES overrides it) is
+ * issued as several launches on `stream`, one per block, reusing the same
+ * workspace in turn.
  */
 int mt_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
                         const void* biases, void* y, int64_t M, int64_t N,
