@@ -22,6 +22,8 @@ request is captured once in a CUDA graph and replayed.
 --impl reference times the CPU implementation of the path (the oracle port;
 the reference's own path is MLX on Apple GPUs, unavailable here) on the same
 metric. --mode kernels prints per-region kernel timings (profiling entry).
+--config llama3_8b_tp times the Llama-3-8B 8-bit prefill forward (batch 8 x
+2048), tensor-parallel over the torchrun ranks with NCCL (run_llama_tp).
 """
 from __future__ import annotations
 

@@ -235,6 +235,18 @@ int mt_rope(const void* x, void* y, int64_t B, int64_t H, int64_t L,
             int64_t D, int dims, int traditional, float base, float scale,
             int64_t offset, int dtype, mt_stream_t stream);
 
+/* mt_rope over strided x and y: element (b, h, l, d) of x sits at
+ * x_sb*b + x_sh*h + x_sl*l + d (in elements), of y likewise. MLX applies rope
+ * to the transposed view of the q/k projections (mlx-lm llama: reshape
+ * [B, L, H, D] then transpose to [B, H, L, D] before rope); one call reads the
+ * token-major projection output and writes the head-major rotated tensor.
+ * y must not overlap x unless both have the same strides. */
+int mt_rope_strided(const void* x, void* y, int64_t B, int64_t H, int64_t L,
+                    int64_t D, int dims, int traditional, float base,
+                    float scale, int64_t offset, int64_t x_sb, int64_t x_sh,
+                    int64_t x_sl, int64_t y_sb, int64_t y_sh, int64_t y_sl,
+                    int dtype, mt_stream_t stream);
+
 /*
  * Qwen3 attention prologue as one region: per token t and head h,
  * q' = rope(rms_norm(q[t,h,:], q_norm_w), offset+t), k' likewise with

@@ -267,10 +267,15 @@ __global__ void __launch_bounds__(256) layer_norm_kernel(const void* __restrict_
 // plus the tail copies past `dims`. The angle expression is the per-element
 // one, so the result does not depend on the grouping.
 constexpr int kRopeRows = 32;
-template <int DT>
+// Element strides of x and y over (batch, head, position); D is contiguous.
+struct RopeStrides {
+  int64_t H, xb, xh, xl, yb, yh, yl;
+};
+template <int DT, bool STRIDED>
 __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, void* __restrict__ yp,
                                                    int64_t BH, int L, int D, int dims, int traditional,
-                                                   float scale, int64_t offset, const RopeFreqs f, int vec) {
+                                                   float scale, int64_t offset, const RopeFreqs f, int vec,
+                                                   const RopeStrides st) {
   using T = typename Elem<DT>::T;
   __shared__ float2 cs[128];
   griddep_wait();
@@ -286,14 +291,23 @@ __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, 
   __syncthreads();
   const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRopeRows;
   const int64_t nr = (BH - r0) < kRopeRows ? (BH - r0) : kRopeRows;
+  const int hdiv = static_cast<int>(st.H);  // B*H < 2^21 (grid.y limit), so rows fit 32 bits
   if (vec) {
     // 4 pairs per item (8-byte accesses), then the tail copies
     const int hv = half / 4, per_row = hv + (D - dims);
     for (int64_t i = threadIdx.x; i < nr * per_row; i += blockDim.x) {
-      const int64_t row = (r0 + i / per_row) * L + l;
       const int q = static_cast<int>(i % per_row);
-      const T* x = static_cast<const T*>(xp) + row * D;
-      T* y = static_cast<T*>(yp) + row * D;
+      const T* x;
+      T* y;
+      if constexpr (STRIDED) {
+        const int bh = static_cast<int>(r0 + i / per_row), bb = bh / hdiv, hh = bh - bb * hdiv;
+        x = static_cast<const T*>(xp) + bb * st.xb + hh * st.xh + l * st.xl;
+        y = static_cast<T*>(yp) + bb * st.yb + hh * st.yh + l * st.yl;
+      } else {
+        const int64_t row = (r0 + i / per_row) * L + l;
+        x = static_cast<const T*>(xp) + row * D;
+        y = static_cast<T*>(yp) + row * D;
+      }
       if (q >= hv) {
         const int d = dims + (q - hv);
         y[d] = x[d];
@@ -342,10 +356,18 @@ __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ xp, 
   }
   const int per_row = half + (D - dims);
   for (int64_t i = threadIdx.x; i < nr * per_row; i += blockDim.x) {
-    const int64_t row = (r0 + i / per_row) * L + l;
     const int j = static_cast<int>(i % per_row);
-    const T* x = static_cast<const T*>(xp) + row * D;
-    T* y = static_cast<T*>(yp) + row * D;
+    const T* x;
+    T* y;
+    if constexpr (STRIDED) {
+      const int bh = static_cast<int>(r0 + i / per_row), bb = bh / hdiv, hh = bh - bb * hdiv;
+      x = static_cast<const T*>(xp) + bb * st.xb + hh * st.xh + l * st.xl;
+      y = static_cast<T*>(yp) + bb * st.yb + hh * st.yh + l * st.yl;
+    } else {
+      const int64_t row = (r0 + i / per_row) * L + l;
+      x = static_cast<const T*>(xp) + row * D;
+      y = static_cast<T*>(yp) + row * D;
+    }
     if (j >= half) {  // tail beyond `dims` copies through
       const int d = dims + (j - half);
       y[d] = x[d];
@@ -517,26 +539,48 @@ int mt_layer_norm(const void* x, const void* w, const void* b, float eps, void* 
   return rc;
 }
 
-int mt_rope(const void* x, void* y, int64_t B, int64_t H, int64_t L, int64_t D, int dims, int traditional,
-            float base, float scale, int64_t offset, int dtype, mt_stream_t stream) {
+static int rope_run(const void* x, void* y, int64_t B, int64_t H, int64_t L, int64_t D, int dims, int traditional,
+                    float base, float scale, int64_t offset, const RopeStrides& st, bool strided, int dtype,
+                    mt_stream_t stream, const char* who) {
   clear_error();
-  MT_CHECK_ARG(x && y, "mt_rope: null pointer");
-  MT_CHECK_ARG(B >= 0 && H >= 0 && L >= 0 && D > 0, "mt_rope: bad shape");
-  MT_CHECK_ARG(dims >= 2 && dims % 2 == 0 && dims <= D && dims <= 256, "mt_rope: dims=%d vs D=%lld", dims,
+  MT_CHECK_ARG(x && y, "%s: null pointer", who);
+  MT_CHECK_ARG(B >= 0 && H >= 0 && L >= 0 && D > 0, "%s: bad shape", who);
+  MT_CHECK_ARG(dims >= 2 && dims % 2 == 0 && dims <= D && dims <= 256, "%s: dims=%d vs D=%lld", who, dims,
                (long long)D);
-  MT_CHECK_ARG(base > 0.f, "mt_rope: base must be positive");
+  MT_CHECK_ARG(base > 0.f, "%s: base must be positive", who);
   const int64_t rows = B * H * L;
   if (rows == 0) return MT_OK;
   MT_CHECK_ARG(L < (int64_t(1) << 31) && (B * H + kRopeRows - 1) / kRopeRows < 65536,
-               "mt_rope: L=%lld or B*H=%lld too large for the grid", (long long)L, (long long)(B * H));
+               "%s: L=%lld or B*H=%lld too large for the grid", who, (long long)L, (long long)(B * H));
   const RopeFreqs f = make_freqs(dims, base);
   const dim3 grid(static_cast<unsigned>(L), static_cast<unsigned>((B * H + kRopeRows - 1) / kRopeRows));
   int rc = MT_OK;
   // 4 pairs per thread when every row and both halves start on 8 bytes
-  const int vec = dtype != MT_F32 && (dims / 2) % 4 == 0 && D % 4 == 0 && aligned(x, 8) && aligned(y, 8);
-  MT_DT_SWITCH(dtype, rc = launch(rope_kernel<DT>, grid, dim3(256), 0, (cudaStream_t)stream, x, y, B * H, (int)L,
-                                  (int)D, dims, traditional, scale, offset, f, vec));
+  const bool rows8 = st.xb % 4 == 0 && st.xh % 4 == 0 && st.xl % 4 == 0 && st.yb % 4 == 0 && st.yh % 4 == 0 &&
+                     st.yl % 4 == 0;
+  const int vec = dtype != MT_F32 && (dims / 2) % 4 == 0 && D % 4 == 0 && rows8 && aligned(x, 8) && aligned(y, 8);
+  if (strided) {
+    MT_DT_SWITCH(dtype, rc = launch((rope_kernel<DT, true>), grid, dim3(256), 0, (cudaStream_t)stream, x, y, B * H,
+                                    (int)L, (int)D, dims, traditional, scale, offset, f, vec, st));
+  } else {
+    MT_DT_SWITCH(dtype, rc = launch((rope_kernel<DT, false>), grid, dim3(256), 0, (cudaStream_t)stream, x, y, B * H,
+                                    (int)L, (int)D, dims, traditional, scale, offset, f, vec, st));
+  }
   return rc;
+}
+
+int mt_rope(const void* x, void* y, int64_t B, int64_t H, int64_t L, int64_t D, int dims, int traditional,
+            float base, float scale, int64_t offset, int dtype, mt_stream_t stream) {
+  const RopeStrides st = {H > 0 ? H : 1, H * L * D, L * D, D, H * L * D, L * D, D};
+  return rope_run(x, y, B, H, L, D, dims, traditional, base, scale, offset, st, false, dtype, stream, "mt_rope");
+}
+
+int mt_rope_strided(const void* x, void* y, int64_t B, int64_t H, int64_t L, int64_t D, int dims, int traditional,
+                    float base, float scale, int64_t offset, int64_t x_sb, int64_t x_sh, int64_t x_sl, int64_t y_sb,
+                    int64_t y_sh, int64_t y_sl, int dtype, mt_stream_t stream) {
+  const RopeStrides st = {H > 0 ? H : 1, x_sb, x_sh, x_sl, y_sb, y_sh, y_sl};
+  return rope_run(x, y, B, H, L, D, dims, traditional, base, scale, offset, st, true, dtype, stream,
+                  "mt_rope_strided");
 }
 
 int mt_qk_norm_rope_cache(const void* q, const void* k, const void* v, int64_t q_stride, int64_t kv_stride,

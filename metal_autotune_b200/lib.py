@@ -78,6 +78,8 @@ SIGNATURES = {
     "mt_rms_norm": (C.c_int, [P, P, F32, P, I64, I64, I32, P]),
     "mt_add_rms_norm": (C.c_int, [P, P, P, F32, P, P, I64, I64, I32, P]),
     "mt_rope": (C.c_int, [P, P, I64, I64, I64, I64, I32, I32, F32, F32, I64, I32, P]),
+    "mt_rope_strided": (C.c_int, [P, P, I64, I64, I64, I64, I32, I32, F32, F32, I64, I64, I64, I64, I64, I64, I64,
+                                  I32, P]),
     "mt_qk_norm_rope_cache": (
         C.c_int, [P, P, P, I64, I64, P, P, F32, P, P, P, I64, I64, I64, I64, I64, I64, F32, I32, P]),
     "mt_swiglu": (C.c_int, [P, P, P, I64, I32, P]),
@@ -340,6 +342,21 @@ def rope(x, dims, *, traditional=False, base=10000.0, scale=1.0, offset=0, out=N
     lead = x.numel() // (L * D) if L * D else 0
     call("mt_rope", _ptr(x), _ptr(y), 1, lead, L, D, int(dims), int(bool(traditional)), float(base), float(scale),
          int(offset), dtype_code(x.dtype), _stream())
+    return y
+
+
+def rope_bhld(x, dims, *, traditional=False, base=10000.0, scale=1.0, offset=0, out=None):
+    """mx.fast.rope over a 4-D view x [B, H, L, D] of any strides (D contiguous), e.g. the
+    transposed [B, L, H, D] projection output; out is a dense [B, H, L, D] by default."""
+    if x.dim() != 4 or x.stride(3) != 1:
+        raise ValueError("x must be a 4-D view [B, H, L, D] with D contiguous")
+    B, H, L, D = x.shape
+    y = out if out is not None else torch.empty((B, H, L, D), dtype=x.dtype, device=x.device)
+    if y.shape != x.shape or y.stride(3) != 1:
+        raise ValueError("out must have x's shape with D contiguous")
+    call("mt_rope_strided", _ptr(x), _ptr(y), B, H, L, D, int(dims), int(bool(traditional)), float(base),
+         float(scale), int(offset), x.stride(0), x.stride(1), x.stride(2), y.stride(0), y.stride(1), y.stride(2),
+         dtype_code(x.dtype), _stream())
     return y
 
 

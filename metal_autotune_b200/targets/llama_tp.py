@@ -5,9 +5,9 @@ llama at 8 bits): batch 8 x 2048 prompt tokens, random-initialised. Per layer:
 rms_norm -> q/k/v qmm -> rope(theta 5e5) -> causal GQA SDPA -> o qmm ->
 +residual -> rms_norm -> gate/up qmm + swiglu -> down qmm -> +residual; final
 rms_norm; lm_head on each sequence's last position. Every op is a libmt.so
-entry point; the only torch work is the head-major copy of q and k before
-rope (MLX transposes the same way, models/llama.py in mlx-lm) and the
-collectives.
+entry point (rope reads the token-major q/k projections and writes them
+head-major, the transpose MLX applies before its rope in mlx-lm's llama);
+the only torch work is the collectives.
 
 Tensor parallel over `tp` shards:
   - q/k/v and gate/up are column-parallel: shard r holds output rows
@@ -183,10 +183,9 @@ class LlamaTP:
     def _attn(self, sl: ShardLayer, xn, B, L):
         cfg, D = self.cfg, self.cfg.head_dim
         q, k, v = lib.quantized_matmul_multi(xn, list(sl.qkv), group_size=cfg.group, bits=cfg.bits)
-        qh = q.view(B, L, self.hq, D).transpose(1, 2).contiguous()
-        kh = k.view(B, L, self.hkv, D).transpose(1, 2).contiguous()
-        qr = lib.rope(qh, D, base=cfg.rope_theta)
-        kr = lib.rope(kh, D, base=cfg.rope_theta)
+        # rope reads the token-major projections and writes head-major q and k
+        qr = lib.rope_bhld(q.view(B, L, self.hq, D).transpose(1, 2), D, base=cfg.rope_theta)
+        kr = lib.rope_bhld(k.view(B, L, self.hkv, D).transpose(1, 2), D, base=cfg.rope_theta)
         vh = v.view(B, L, self.hkv, D).transpose(1, 2)
         o = lib.sdpa(qr, kr, vh, scale=1.0 / math.sqrt(D), causal=True, out_layout="blhd")
         return lib.quantized_matmul(o.view(B * L, self.hq * D), *sl.o, group_size=cfg.group, bits=cfg.bits)

@@ -98,3 +98,15 @@ def test_forward_is_deterministic(tp1):
     tok = _tokens(1, 128)
     a, b = tp1(tok), tp1(tok)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dims,traditional,H", [(128, False, 6), (64, False, 5), (128, True, 3)])
+def test_rope_strided_equals_dense(cuda, dims, traditional, H):
+    """mt_rope_strided on the transposed token-major view equals mt_rope on its dense copy, bit for bit."""
+    g = torch.Generator(device="cuda").manual_seed(H)
+    x = torch.randn(2, 96, H, 128, device="cuda", generator=g).to(torch.bfloat16)  # [B, L, H, D]
+    view = x.transpose(1, 2)
+    a = lib.rope_bhld(view, dims, traditional=traditional, base=5e5, offset=3)
+    b = lib.rope(view.contiguous(), dims, traditional=traditional, base=5e5, offset=3)
+    torch.cuda.synchronize()
+    assert a.is_contiguous() and torch.equal(a, b)
