@@ -649,6 +649,8 @@ def run_llama_tp(args):
         "e2e": {"value": round(B * L / (ms_e2e / 1e3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": B * L * 4, "d2h_bytes_per_step": B * cfg.vocab * 2},
         "roofline": roof, "clocks": clk.summary(), "gpu_launches": launches,
+        "gpu_launches_note": "libmt entry-point calls in the timed region; a blocked prefill qmm call issues "
+                             "one launch per L2-sized block, so kernel launches are at least this many",
     }
     barrier(world)
     print(json.dumps(line), flush=True)

@@ -107,3 +107,14 @@ def test_conv1d_checks_arguments_without_gpu(mt):
     assert rc == -2 and b"multiple of 32" in mt.mt_last_error_string()
     rc = mt.mt_conv1d(p, p, None, p, 1, 1, 64, 64, 5, 1, 1, 0, 1, None)  # input shorter than the kernel
     assert rc == -1 and b"shorter than the kernel" in mt.mt_last_error_string()
+
+
+def test_rope_strided_checks_arguments_without_gpu(mt):
+    import torch
+    p = C.c_void_p(256)
+    bf = lib.dtype_code(torch.bfloat16)
+    rc = mt.mt_rope_strided(None, p, 1, 2, 4, 128, 128, 0, 1e4, 1.0, 0, 1024, 128, 256, 1024, 512, 128, bf, None)
+    assert rc == -1 and b"mt_rope_strided: null pointer" in mt.mt_last_error_string()
+    rc = mt.mt_rope_strided(p, p, 1, 2, 4, 64, 128, 0, 1e4, 1.0, 0, 512, 64, 128, 512, 256, 64, bf, None)
+    assert rc == -1 and b"dims=128" in mt.mt_last_error_string()
+    assert mt.mt_rope_strided(p, p, 0, 2, 4, 128, 128, 0, 1e4, 1.0, 0, 0, 0, 0, 0, 0, 0, bf, None) == 0  # empty
