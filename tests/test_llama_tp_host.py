@@ -92,3 +92,27 @@ def test_forward_flops_llama_8b():
     # projections 2*T*218.1M*32 + causal attention + lm_head
     f = llama_tp.forward_flops(llama_tp.LLAMA3_8B, 8, 2048)
     assert 2.3e14 < f < 2.5e14, f
+
+
+def test_llama_shards_are_slices_of_one_model():
+    """The model-level split on the host: every tp=2 shard of every projection is the
+    matching slice of the tp=1 weights (column shards along N, row shards along K),
+    heads and lm_head rows divide as the config says."""
+    cfg = llama_tp.LlamaConfig(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=384)
+    full = llama_tp.LlamaTP(cfg, 1, [0], llama_tp.LocalComm(), seed=9, device="cpu")
+    split = llama_tp.LlamaTP(cfg, 2, [0, 1], llama_tp.LocalComm(), seed=9, device="cpu")
+    assert (split.hq, split.hkv) == (2, 1)
+    per = 32 // cfg.bits
+    for li in range(cfg.layers):
+        f = full.shards[0].layers[li]
+        s0, s1 = (sh.layers[li] for sh in split.shards)
+        for a, b0, b1 in [(f.qkv[0], s0.qkv[0], s1.qkv[0]), (f.qkv[1], s0.qkv[1], s1.qkv[1]),
+                          (f.qkv[2], s0.qkv[2], s1.qkv[2]), (f.gate, s0.gate, s1.gate), (f.up, s0.up, s1.up)]:
+            for t, u0, u1 in zip(a, b0, b1):
+                assert torch.equal(torch.cat([u0, u1], dim=0), t)
+        for a, b0, b1 in [(f.o, s0.o, s1.o), (f.down, s0.down, s1.down)]:
+            assert b0[0].shape[1] * per * 2 == a[0].shape[1] * per
+            for t, u0, u1 in zip(a, b0, b1):
+                assert torch.equal(torch.cat([u0, u1], dim=1), t)
+    assert torch.equal(torch.cat([sh.lm_head[0] for sh in split.shards]), full.shards[0].lm_head[0])
+    assert split.shards[0].lm_head[0].shape[0] == cfg.vocab // 2
