@@ -377,9 +377,11 @@ int mt_diff_reduce(const void* a, const void* b, int64_t n, int dtype,
  * until the process exits. n may be at most MT_DIFF_NOALLOC_MAX_ELEMS;
  * larger inputs are rejected with MT_ERR_INVALID_ARGUMENT (use
  * mt_diff_reduce). Same kernel and block partition as mt_diff_reduce, so the
- * statistics are identical. The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress) with that device current; make that
- * first call before any stream capture. Every call on a device shares the
+ * statistics are identical. Every call looks up the array's device address
+ * (cudaGetSymbolAddress) in the current context, so a call after a
+ * cudaDeviceReset or a primary-context reset uses the array's new address;
+ * the first call on a device also loads the library's module there, so make
+ * that first call before any stream capture. Every call on a device shares the
  * array: calls whose kernels overlap on the GPU (other streams, other host
  * threads) race and must be serialised by the caller. Each call zeroes the
  * counter on its stream before its kernel runs.

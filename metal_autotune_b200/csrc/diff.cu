@@ -282,24 +282,17 @@ constexpr int kNoAllocBlocks = 128;
 constexpr int64_t kNoAllocMaxN = static_cast<int64_t>(kNoAllocBlocks) * 8192;  // MT_DIFF_NOALLOC_MAX_ELEMS
 static __device__ __align__(256) uint8_t g_diff_noalloc_scratch[256 + kNoAllocBlocks * sizeof(DiffPartial)];
 
-// Device address of the scratch array for the current device. Host code may
+// Device address of the scratch array in the current context. Host code may
 // not pass the array's name to a kernel (it is only a host-side stand-in), so
-// the address is looked up once per device, with that device current.
+// the address is looked up on every call, with the calling device current.
+// No cache: the lookup is cheap, shares no state between host threads and
+// stays right after a cudaDeviceReset or a primary-context reset gives the
+// array a new address.
 static int noalloc_scratch(void** out) {
-  static void* addr[64] = {nullptr};
-  int dev = 0;
-  MT_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) {
-    set_error("mt_diff_reduce_noalloc: device ordinal %d out of range", dev);
-    return MT_ERR_UNSUPPORTED;
-  }
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_diff_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_diff_noalloc_scratch)");
-    addr[dev] = p;
-  }
-  *out = addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_diff_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_diff_noalloc_scratch)");
+  *out = p;
   return MT_OK;
 }
 

@@ -70,7 +70,12 @@ static int run_tc_blocked(const QmmRequest& r, cudaStream_t stream) {
   if (mc < 128) mc = 128;
   const int64_t sets_n = dual ? 2 : 1;
   const int64_t row_bytes = sets_n * (r.K * r.bits / 8 + (r.K / r.group) * 2 * esz);
-  const int64_t N0 = r.set[0].N;
+  // Sets with N = 0 are skipped: a q/k/v call may fill only set 1 or 2, and
+  // the split then follows the first set that has rows (check_common has
+  // seen at least one).
+  int si = 0;
+  while (si < 2 && r.set[si].N == 0) ++si;
+  const int64_t N0 = r.set[si].N;
   int64_t nc = N0;
   if (split_n) {
     nc = budget / row_bytes / 128 * 128;
@@ -94,7 +99,7 @@ static int run_tc_blocked(const QmmRequest& r, cudaStream_t stream) {
         if (q.N == 0) continue;
         QmmSetReq& o = c.set[s];
         const int64_t ldy = q.ldy > 0 ? q.ldy : q.N;
-        if (s == 0) ldy0 = ldy;
+        if (s == si) ldy0 = ldy;
         o.ldy = ldy;
         const int64_t col = split_n ? n0 : 0;
         if (split_n) {

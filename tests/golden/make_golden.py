@@ -11,12 +11,13 @@ run — its tests need MLX on an Apple GPU) and writes the cases as JSON:
   grammar.json           tests/test_runtime.py:10-33 (launch grammar values,
                          rejections, runtime bounds)
 
-Usage: python tests/golden/make_golden.py [reference_root]
+Usage: python tests/golden/make_golden.py <reference_root>   (or MT_REFERENCE_ROOT=<reference_root>)
 """
 from __future__ import annotations
 
 import ast
 import json
+import os
 import math
 import sys
 from pathlib import Path
@@ -137,7 +138,12 @@ def grammar(ref: Path) -> dict:
                                {"expr": "in0.shape[5]", "shapes": [[4]], "match": "axis"}]}
 
 
-def main(ref_root: str = "/root/reference") -> None:
+def main(ref_root: str | None = None) -> None:
+    """Regenerate the fixtures from the reference checkout named by the first
+    argument or, failing that, the MT_REFERENCE_ROOT environment variable."""
+    ref_root = ref_root or os.environ.get("MT_REFERENCE_ROOT")
+    if not ref_root:
+        raise SystemExit("usage: make_golden.py <reference checkout>  (or set MT_REFERENCE_ROOT)")
     ref = Path(ref_root)
     (HERE / "numeric_contract.json").write_text(json.dumps(numeric_contract(ref), indent=1) + "\n")
     (HERE / "grammar.json").write_text(json.dumps(grammar(ref), indent=1) + "\n")

@@ -1,0 +1,31 @@
+"""The committed region bundles are exactly what the generator writes.
+
+`python -m metal_autotune_b200.bundles` writes every bundle under
+metal_autotune_b200/bundles/ (kernels/*.launch.json, swap_table.json,
+patch/wrappers.py, bundle.json); the wrapper module of each bundle is a copy
+of the one committed source. Regenerating into a temporary directory must
+give the committed bytes, file for file."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import pytest
+
+from metal_autotune_b200 import bundles
+
+
+def _files(d: Path) -> dict[str, bytes]:
+    return {str(p.relative_to(d)): p.read_bytes() for p in sorted(d.rglob("*"))
+            if p.is_file() and "__pycache__" not in p.parts}
+
+
+@pytest.mark.parametrize("name,layers", [("qwen3_4b", 36), ("qwen3_tiny", 2)])
+def test_committed_qwen3_bundle_is_generated(tmp_path, name, layers):
+    out = bundles.write_qwen3_bundle(tmp_path / name, layers)
+    assert _files(out) == _files(bundles.HERE / name)
+
+
+def test_bundle_wrappers_are_the_one_source():
+    src = bundles.WRAPPERS.read_bytes()
+    for name in ("qwen3_4b", "qwen3_tiny"):
+        assert (bundles.HERE / name / "patch" / "wrappers.py").read_bytes() == src

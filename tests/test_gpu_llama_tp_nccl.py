@@ -47,7 +47,17 @@ def test_tp2_over_nccl_matches_tp1(cuda, tmp_path):
     procs = [ctx.Process(target=_rank, args=(r, str(tmp_path / "pg"), q)) for r in range(2)]
     for p in procs:
         p.start()
-    for p in procs:
-        p.join(timeout=300)
+    try:
+        for p in procs:
+            p.join(timeout=300)
+    finally:
+        # a rank still alive (e.g. stuck in a collective) is ended, not left on its GPU
+        for p in procs:
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
     assert [p.exitcode for p in procs] == [0, 0]
     assert dict(q.get(timeout=5) for _ in range(2)) == {0: True, 1: True}

@@ -67,3 +67,29 @@ def test_blocked_equals_one_launch_within_tolerance(cuda, oracle, monkeypatch):
     monkeypatch.setenv("MT_QMM_L2_BLOCK_BYTES", BUDGET)
     blocked = lib.quantized_matmul(x, wq_t, s_t, b_t, bits=8)
     close_bf16(n(blocked), n(one), ulps=1)
+
+
+@pytest.mark.parametrize("empty", [(0,), (0, 2), (0, 1)])
+def test_blocked_multi_with_empty_leading_sets(cuda, oracle, small_blocks, empty):
+    """mt_quantized_matmul_multi with set 0 (and possibly another) left empty:
+    the blocked path splits by the first set that has rows."""
+    M, K, N = 300, 1024, 640
+    x = oracle.round_to(rng.standard_normal((M, K)).astype(np.float32), "bfloat16")
+    xt = t(x)
+    live = [i for i in range(3) if i not in empty]
+    sets = {i: quantized(oracle, N, K, 64, 8, seed=20 + i) for i in live}
+    ys = {i: torch.empty(M, N, dtype=torch.bfloat16, device="cuda") for i in live}
+    args = []
+    for i in range(3):
+        if i in sets:
+            w, s, b = sets[i][1]
+            args += [lib._ptr(w), lib._ptr(s), lib._ptr(b), lib._ptr(ys[i]), N]
+        else:
+            args += [None, None, None, None, 0]
+    ws = lib.Workspace.get(lib.qmm_workspace_bytes(M, N * len(live), K, 8, 0))
+    lib.call("mt_quantized_matmul_multi", lib._ptr(xt), *args, M, K, 64, 8, lib.MT_BF16, ws.ptr, ws.nbytes,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for i in live:
+        wq, s, b = sets[i][0]
+        close_bf16(n(ys[i]), oracle.quantized_matmul(x, wq, s, b, 64, 8), ulps=1)
