@@ -134,9 +134,10 @@ class LoadedKernel:
         self.spec = spec
         self._stages = None
         if spec.stages:
-            from .stages import wiring
-            indices, self._stage_outputs = wiring(spec)
-            self._stages = [(LoadedKernel(st.kernel), ins) for st, ins in zip(spec.stages, indices)]
+            from .stages import build_graph
+            self._graph = build_graph(spec)
+            self._stage_outputs = self._graph.outputs
+            self._stages = [(LoadedKernel(node.kernel), node.reads) for node in self._graph.nodes]
         elif spec.cuda is None:
             raise ValueError(f"kernel {spec.kernel_id}: a spec needs a cuda record or stages")
         self._fn = None
@@ -195,8 +196,7 @@ class LoadedKernel:
             out_dtypes = [_resolve_dtype(d, dtypes) for d in spec.output_dtypes]
             args = None
             if self._stages is not None:
-                from .stages import shapes as stage_shapes
-                _, outs = stage_shapes(spec, shapes, dtypes)
+                _, outs = self._graph.walk_shapes(shapes, dtypes)
                 if [(tuple(s), d) for s, d in outs] != list(zip(out_shapes, out_dtypes)):
                     raise ValueError("stage results do not match the region's output shapes/dtypes")
             else:

@@ -3,7 +3,6 @@ autotuner_runtime/sequence.py:16-188), timed with CUDA events."""
 from __future__ import annotations
 
 import statistics
-from dataclasses import asdict
 from typing import Callable
 
 from .measure import Session
@@ -65,7 +64,7 @@ def compare_sequences(session: Session, baseline: Callable, candidate: Callable,
     cmp = comparison_from_samples(base, cand)
     return {
         "protocol": "whole_sequences_balanced_ab_ba", "warmup_steps": warm, "pairs": pairs,
-        "observations": obs, "timing": asdict(cmp),
+        "observations": obs, "timing": cmp.as_record(),
         "baseline_sequence_ms": cmp.median_baseline_ms, "candidate_sequence_ms": statistics.median(cand),
         "speedup": 1 / cmp.median_ratio if cmp.median_ratio else float("nan"),
         "latency_reduction_pct": 100 * (1 - cmp.median_ratio),

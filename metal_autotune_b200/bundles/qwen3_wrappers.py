@@ -131,6 +131,7 @@ class W_qwen3_root(_Counting):
             if r is None:
                 r = [E.as_linear(xn)]
         logits = r[0]
+        object.__setattr__(self, "last_logits", logits)  # the last position's logits, for checks
         r = self._call("logits_pick", [logits])
         if r is None:
             lse = torch.logsumexp(logits.float(), dim=-1, keepdim=True)

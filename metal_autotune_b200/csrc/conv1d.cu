@@ -12,11 +12,10 @@
 // 4-stage ring of XOR-swizzled shared memory and multiplied with mma.sync
 // m16n8k16 (bf16/f16 in, fp32 accumulate; 8 warps of 64 x 32). The epilogue
 // rounds as the separate MLX ops would: conv, + bias, GELU, each to the
-// element type (GELU evaluated in fp32 on the rounded input, mt_math.h), and
+// element type (GELU evaluated in fp32 on the rounded input, device erff), and
 // stages the tile in shared memory for 16-byte coalesced stores.
 #include "mma_sync.cuh"
 #include "mt_common.cuh"
-#include "mt_math.h"
 
 namespace mt {
 
@@ -160,7 +159,7 @@ __global__ void __launch_bounds__(kCvThreads, 2) conv1d_kernel(const Conv1dParam
           const float b = (bias && co + e < p.Cout) ? Elem<DT>::to_f(bias[co + e]) : 0.f;
           float u = p.bias_fused ? round_to<DT>(acc[mi][nj][h * 2 + e] + b)
                                  : round_to<DT>(round_to<DT>(acc[mi][nj][h * 2 + e]) + b);
-          if (ACT == 1) u = round_to<DT>(mt_gelu_f32(u));
+          if (ACT == 1) u = round_to<DT>(gelu_erf_f32(u));
           v[e] = u;
         }
         *reinterpret_cast<typename Elem<DT>::T2*>(tile + rl * kPitch + cl) = Elem<DT>::pack2(v[0], v[1]);

@@ -1,13 +1,13 @@
 // fp32 dense linear (+bias, +GELU) for the GELU-MLP region (tiny MLP).
 //
-// Bit-reproducible: each output accumulates k = 0..K-1 in order with one
-// fused multiply-add per term, adds the bias once, then applies GELU with
-// the shared fixed-sequence erf (mt_math.h). Tiles of 32 x 32 outputs stage
+// Fixed order: each output accumulates k = 0..K-1 in order with one fused
+// multiply-add per term (bit-identical to a sequential CPU restatement), adds
+// the bias once, then applies GELU with the device library's erff. Tiles of
+// 32 x 32 outputs stage
 // x and w through shared memory; the accumulation order is unchanged by the
 // tiling. The tiny MLP is launch-bound (33.5 MFLOP), so this favours
 // exactness over tensor cores (TF32 would change every product).
 #include "mt_common.cuh"
-#include "mt_math.h"
 
 namespace mt {
 
@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(const float* __restrict
       if (m >= M) continue;
       float v = acc[i];
       if (bias) v = __fadd_rn(v, bias[n]);
-      if (act == 1) v = mt_gelu_f32(v);
+      if (act == 1) v = gelu_erf_f32(v);
       y[static_cast<int64_t>(m) * N + n] = v;
     }
   }

@@ -147,6 +147,13 @@ __device__ __forceinline__ void report_status(int code) {
 }
 
 // ------------------------------------------------------------- PDL primitives
+// mlx.nn.gelu, exact form: x * (1 + erf(x / sqrt(2))) / 2 in fp32, each
+// operation rounded as written, erf from the CUDA device math library.
+__device__ __forceinline__ float gelu_erf_f32(float x) {
+  const float u = __fadd_rn(1.0f, erff(__fdiv_rn(x, 1.41421356237309505f)));
+  return __fdiv_rn(__fmul_rn(x, u), 2.0f);
+}
+
 __device__ __forceinline__ void griddep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }

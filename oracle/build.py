@@ -15,7 +15,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 SRC = HERE / "mt_oracle.c"
 LIB = HERE / "liboracle.so"
-DEPS = [SRC, HERE.parent / "metal_autotune_b200" / "csrc" / "mt_math.h", Path(__file__)]
+DEPS = [SRC, Path(__file__)]
 
 
 def build_oracle(force: bool = False) -> Path:

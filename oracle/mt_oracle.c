@@ -21,7 +21,6 @@
 #include <stdlib.h>
 #include <string.h>
 
-#include "../metal_autotune_b200/csrc/mt_math.h"
 
 enum { DT_BF16 = 0, DT_F16 = 1, DT_F32 = 2 };
 
@@ -321,10 +320,20 @@ void orc_logits_pick(const float* x, int64_t n, int dt, int32_t* token, float* l
   *lse_out = lse;
 }
 
+/* mlx.nn.gelu (exact form): x * (1 + erf(x / sqrt(2))) / 2, each operation
+ * rounded to fp32 as written, erf from the C library (glibc erff). This is
+ * the oracle's own erf: the CUDA kernels call the device library's erff, so
+ * the two sides are independent implementations and agree only within their
+ * error bounds (glibc erff <= 1 ulp; CUDA erff <= 2 ulp). MLX's own CPU erf
+ * is not available here, so bit-exactness against MLX cannot be checked. */
+static float gelu_f32(float x) {
+  const float u = 1.0f + erff(x / 1.41421356237309505f);
+  return x * u / 2.0f;
+}
+
 /* Dense linear + bias (+ GELU) with a sequential-k fused multiply-add
  * accumulation (the reference's matmul restatement,
- * autotuner/scaffold/lower.py:1109-1142), bias added once, GELU per
- * mlx.nn.gelu with the fixed-sequence erf of mt_math.h. */
+ * autotuner/scaffold/lower.py:1109-1142), bias added once, then GELU. */
 void orc_linear(const float* x, const float* w, const float* bias, float* y, int64_t M, int64_t N, int64_t K,
                 int act) {
 #pragma omp parallel for collapse(2) schedule(static)
@@ -333,14 +342,13 @@ void orc_linear(const float* x, const float* w, const float* bias, float* y, int
       float acc = 0.0f;
       for (int64_t k = 0; k < K; ++k) acc = fmaf(x[m * K + k], w[n * K + k], acc);
       if (bias) acc = acc + bias[n];
-      if (act == 1) acc = mt_gelu_f32(acc);
+      if (act == 1) acc = gelu_f32(acc);
       y[m * N + n] = acc;
     }
 }
 
-float orc_erf(float x) { return mt_erf_f32(x); }
-float orc_exp(float x) { return mt_exp_f32(x); }
-float orc_gelu(float x) { return mt_gelu_f32(x); }
+float orc_erf(float x) { return erff(x); }
+float orc_gelu(float x) { return gelu_f32(x); }
 
 static float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
@@ -419,7 +427,7 @@ void orc_conv1d(const float* x, const float* w, const float* bias, float* y, int
         }
         float v = round_dt(acc, dt);
         if (bias) v = round_dt(v + bias[co], dt);
-        if (act == 1) v = round_dt(mt_gelu_f32(v), dt);
+        if (act == 1) v = round_dt(gelu_f32(v), dt);
         y[(n * Lout + t) * Cout + co] = v;
       }
 }
@@ -434,7 +442,7 @@ void orc_linear_lp(const float* x, const float* w, const float* bias, float* y, 
       float acc = 0.0f;
       for (int64_t k = 0; k < K; ++k) acc = fmaf(x[m * K + k], w[n * K + k], acc);
       float v = round_dt(bias ? acc + bias[n] : acc, dt);
-      if (act == 1) v = round_dt(mt_gelu_f32(v), dt);
+      if (act == 1) v = round_dt(gelu_f32(v), dt);
       y[m * N + n] = v;
     }
 }

@@ -41,7 +41,6 @@ def lib() -> C.CDLL:
             "orc_logits_pick": (None, [f32p, I64, I, C.POINTER(C.c_int32), C.POINTER(F), C.POINTER(F)]),
             "orc_linear": (None, [f32p, f32p, C.c_void_p, f32p, I64, I64, I64, I]),
             "orc_erf": (F, [F]),
-            "orc_exp": (F, [F]),
             "orc_gelu": (F, [F]),
             "orc_mamba_scan": (None, [f32p, f32p, C.c_void_p, f32p, f32p, f32p, C.c_void_p, f32p, f32p,
                                       C.c_void_p, I64, I64, I64, I]),
@@ -223,6 +222,14 @@ def quantized_embedding(tokens, wq, scales, biases, group=64, bits=4, dtype="bfl
     lib().orc_quantized_embedding(tok, np.ascontiguousarray(wq, np.uint32), _f32(scales), _f32(biases), out,
                                   tok.size, wq.shape[0], D, group, bits, DT[dtype])
     return out.reshape(*np.shape(tokens), D)
+
+
+def dequantize(wq, scales, biases, group=64, bits=4, dtype="bfloat16"):
+    """The dequantised weight matrix [N, K] in `dtype` values (MLX rounding,
+    round(round(scale * q) + bias)): every row gathered through the
+    embedding restatement."""
+    N = wq.shape[0]
+    return quantized_embedding(np.arange(N, dtype=np.int32), wq, scales, biases, group, bits, dtype)
 
 
 def logits_pick(logits, dtype="bfloat16"):

@@ -100,10 +100,11 @@ def test_sdpa_matches_float64(causal, off):
     assert np.abs(o - ref).max() <= 2 ** -7 * np.abs(ref).max() + 1e-6
 
 
-def test_fixed_sequence_erf_within_published_bound():
-    # A&S 7.1.26: |error| <= 1.5e-7 in exact arithmetic, plus a few fp32 ulps (2^-24) of evaluation
+def test_oracle_erf_is_the_c_library_erf():
+    # the oracle's GELU uses glibc erff: within one fp32 ulp of the correctly rounded value
     for x in np.linspace(-5, 5, 2001, dtype=np.float32):
-        assert abs(R.erf(float(x)) - math.erf(float(x))) < 1.5e-7 + 3 * 2 ** -24
+        e = math.erf(float(x))
+        assert abs(R.erf(float(x)) - e) <= np.spacing(np.float32(abs(e)))
 
 
 def test_swiglu_and_gelu_mlp():
@@ -150,3 +151,38 @@ def test_mamba_scan_and_conv_match_loops():
     for l in range(L):
         acc = sum(w[:, j] * (x[l - 3 + j] if l - 3 + j >= 0 else 0) for j in range(4))
         assert np.abs(yc[l] - acc).max() <= 2e-3 * max(1.0, np.abs(acc).max())
+
+
+# ------------------------------------------- second oracle path: the MLX-derived header arithmetic
+def test_oracle_dequant_equals_mlx_deq8_bit_for_bit():
+    """The oracle's dequantisation (round(round(s*q)+b) in bf16) against the
+    reference-held mlx_deq8 arithmetic (oracle/mlx_header_ref.py)."""
+    from oracle import mlx_header_ref as H
+    r = np.random.default_rng(41)
+    wq, s, b = R.quantize_affine(r.standard_normal((96, 1024)).astype(np.float32) * 0.02, 64, 4, "bfloat16")
+    got = R.dequantize(wq, s, b, 64, 4, "bfloat16")
+    want = H.deq8(wq, s, b, 64)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+QMV_HEADER_CASES = [(1, 256, 2560), (2, 128, 4096), (1, 64, 9728)]
+
+
+@pytest.mark.parametrize("M,N,K", QMV_HEADER_CASES)
+def test_oracle_qmv_against_mlx_qdot16(M, N, K):
+    """The oracle's qmv (factored form, fp32 sums in its own order) against the
+    qmv_qdot16 arithmetic. With the quad sums of x in fp32 the two are the
+    same factored form: within one bf16 ulp plus 2^-9 of the row scale. With
+    MLX's bf16 quad sums the outputs also differ by that rounding noise:
+    within 6 standard deviations of it (quad_sum_sigma) on top."""
+    from oracle import mlx_header_ref as H
+    r = np.random.default_rng(K + N)
+    x = R.round_to(r.standard_normal((M, K)).astype(np.float32), "bfloat16")
+    wq, s, b = R.quantize_affine(r.standard_normal((N, K)).astype(np.float32) * 0.02, 64, 4, "bfloat16")
+    got = R.qmv(x, wq, s, b, 64, 4, "bfloat16")
+    same_form = H.qmv_qdot16(x, wq, s, b, 64, bf16_quad_sums=False)
+    tol = 2 ** -7 * np.abs(same_form) + 2 ** -9 * np.abs(same_form).max()
+    assert (np.abs(got - same_form) <= tol).all(), np.abs(got - same_form).max()
+    mlx = H.qmv_qdot16(x, wq, s, b, 64)
+    tol = 2 ** -7 * np.abs(mlx) + 2 ** -9 * np.abs(mlx).max() + 6 * H.quad_sum_sigma(x, b, 64)
+    assert (np.abs(got - mlx) <= tol).all(), np.abs(got - mlx).max()

@@ -128,9 +128,10 @@ def test_stage_plan_valid_and_walks_shapes():
     assert KernelSpec.from_json(spec.to_json()) == spec
 
 
-@pytest.mark.parametrize("change", ["forward", "overwrite", "dead", "missing", "local_names"])
-def test_bad_stage_plans_rejected(change):
-    from metal_autotune_b200.autotuner_runtime.stages import wiring
+@pytest.mark.parametrize("change,code", [("forward", "unbound"), ("overwrite", "rebind"), ("dead", "dead"),
+                                         ("missing", "unproduced"), ("local_names", "local_inputs")])
+def test_bad_stage_plans_rejected(change, code):
+    from metal_autotune_b200.autotuner_runtime.stages import StageError, wiring
     s0 = KernelStage(("in0", "in1"), ("tmp0",), _local())
     s1 = KernelStage(("tmp0", "in1"), ("out0",), _local())
     if change == "forward":
@@ -143,8 +144,9 @@ def test_bad_stage_plans_rejected(change):
         s1 = KernelStage(("tmp0", "in1"), ("tmp1",), _local())
     if change == "local_names":
         s1 = KernelStage(("tmp0", "in1"), ("out0",), _rms_spec(kernel_id="x", input_names=("a", "b")))
-    with pytest.raises(ValueError):
+    with pytest.raises(StageError) as e:
         wiring(_stage_spec([s0, s1]))
+    assert e.value.code == code
 
 
 # ------------------------------------------------------------ swap / apply
