@@ -5,7 +5,9 @@ One step = one request as the reference's workload defines it
 131-156): from an empty KV cache, prefill 128 prompt tokens, pick the next
 token, run one decode step, pick again. Every region runs through the bundle's
 wrappers (try_call -> libmt.so), strict mode on (a fallback raises). The
-request is captured once in a CUDA graph and replayed.
+request is captured once in a CUDA graph and replayed. Timed regions go
+through the timing harness (autotuner_runtime.measure: CUDA events on the
+launching stream, device synchronised on both sides).
 
   value  prompt tokens/s (128 / request time) with tokens already on the
          device, CUDA events around K replays, max over ranks, x ranks
@@ -16,14 +18,19 @@ request is captured once in a CUDA graph and replayed.
   roofline  the dominant kernel (tcgen05 prefill qmm, all 144 launches of
          the request's prefill) timed on its own stream with CUDA events:
          algorithmic FLOPs / time vs the measured bf16 peak.
-  cpu_baseline  the oracle restatement (C, OpenMP, all host threads) on one
-         decoder layer of the same request, extrapolated to the full request.
+  cpu_baseline  the oracle restatement (C, OpenMP, all host threads) running
+         one whole request (36 layers, prefill 128 + decode 1, lm_head) on
+         this model's own weights, copied to the host.
+  llama_tp  the Llama-3-8B 8-bit prefill forward (batch 8 x 2048),
+         tensor-parallel over the same ranks (tp = N, NCCL all-reduce after
+         o_proj and down): ms per forward, whole-job tok/s, per-GPU TFLOP/s
+         and the share of the forward the all-reduces take alone.
 
 --impl reference times the CPU implementation of the path (the oracle port;
-the reference's own path is MLX on Apple GPUs, unavailable here) on the same
-metric. --mode kernels prints per-region kernel timings (profiling entry).
---config llama3_8b_tp times the Llama-3-8B 8-bit prefill forward (batch 8 x
-2048), tensor-parallel over the torchrun ranks with NCCL (run_llama_tp).
+the reference's own path is MLX on Apple GPUs, unavailable here): whole
+requests on the same weights, as many as fit a wall-clock cap. --mode
+kernels prints per-region kernel timings (profiling entry). --config
+llama3_8b_tp prints the Llama line alone.
 """
 from __future__ import annotations
 
@@ -53,21 +60,27 @@ def log(*a):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
+    """nvidia-smi samples every 50 ms while the measurement runs. The caller
+    marks the timed region (mark_start/mark_end); the summary gives the
+    median SM clock and the throttle reasons over the whole sampled window
+    (the timed region plus the untimed replays around it) and how many
+    samples fell inside the timed region itself."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_ms: int = 50):
         self.idx = device_index
+        self.period_ms = period_ms
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.timed = [None, None]
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -77,7 +90,13 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def mark_start(self):
+        self.timed[0] = time.time()
+
+    def mark_end(self):
+        self.timed[1] = time.time()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -88,22 +107,38 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        sms, mx, reasons = [], None, set()
+        sms, mx, reasons, inside = [], None, set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        t0, t1 = self.timed
+        for ts, ln in self.lines:
             p = [x.strip() for x in ln.split(",")]
-            if len(p) < 9:
+            if len(p) < 10:
                 continue
             try:
-                sms.append(float(p[1]))
-                mx = float(p[2])
+                sm = float(p[2])
+                mx = float(p[3])
             except ValueError:
                 continue
-            for name, v in zip(names, p[5:9]):
+            sms.append(sm)
+            if t0 is not None and t1 is not None and t0 - self.period_ms / 1e3 <= ts <= t1 + self.period_ms / 1e3:
+                inside += 1
+            for name, v in zip(names, p[6:10]):
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sms)}
+                "reasons": sorted(reasons), "samples": len(sms), "samples_in_timed_region": inside,
+                "period_ms": self.period_ms,
+                "window": "the timed region plus untimed replays of the same step around it"}
+
+
+def soak(fn, seconds: float):
+    """Untimed repetitions of fn for about `seconds` (clock samples around the timed region)."""
+    import torch
+    t_end = time.time() + seconds
+    while time.time() < t_end:
+        for _ in range(8):
+            fn()
+        torch.cuda.synchronize()
 
 
 # ------------------------------------------------------------------ peaks
@@ -225,18 +260,15 @@ class Request:
         self.host_out.copy_(self.res_dev, non_blocking=True)
 
 
-def time_region(fn, steps, world):
-    import torch
+def time_region(fn, steps, world, stream=None):
+    """Device milliseconds of `steps` calls of fn (autotuner_runtime.measure:
+    CUDA events on the launching stream, synchronised on both sides), between
+    barriers of all ranks."""
+    from metal_autotune_b200.autotuner_runtime import measure
     barrier(world)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        fn()
-    end.record()
-    torch.cuda.synchronize()
+    ms = measure.time_steps(fn, steps, stream)
     barrier(world)
-    return start.elapsed_time(end)
+    return ms
 
 
 def qmm_roofline(req, peaks, reps=20):
@@ -270,13 +302,8 @@ def qmm_roofline(req, peaks, reps=20):
             run_all()
         g.replay()
         s.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(s)
-        for _ in range(reps):
-            g.replay()
-        end.record(s)
-        s.synchronize()
-    ms = start.elapsed_time(end) / reps
+        from metal_autotune_b200.autotuner_runtime import measure
+        ms = measure.time_steps(g.replay, reps, stream=s) / reps
     launches = 4 * len(layers)
     flops = request_flops(cfg)
     achieved = flops / (ms / 1e3) / 1e12
@@ -288,98 +315,90 @@ def qmm_roofline(req, peaks, reps=20):
 
 
 # ------------------------------------------------------------------ CPU side
-def cpu_layer_sample(cfg, seed=0):
-    """Numpy copies of one random layer for the oracle (same generator as the model)."""
-    import numpy as np
-    import torch
-
-    from metal_autotune_b200 import workload
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    h, q, kv, ff = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.ffn
-    W = {}
-    for name, (nn_, kk) in dict(q=(q, h), k=(kv, h), v=(kv, h), o=(h, q), g=(ff, h), u=(ff, h), d=(h, ff)).items():
-        wq, s, b = workload.random_quantized(nn_, kk, group=cfg.group, bits=cfg.bits, generator=g, device="cpu")
-        W[name] = (wq.numpy().view(np.uint32), s.float().numpy(), b.float().numpy())
-    return W
+def qwen3_config_record(cfg, world):
+    """The `config` of the Qwen3 line, identical in both arms."""
+    return {"workload": "qwen3_4b_prefill_128+decode_1" if cfg.layers == 36 else "qwen3_tiny",
+            "model": f"Qwen3-{'4B' if cfg.layers == 36 else 'tiny'} 4-bit affine g64, random init (seed 0)",
+            "prompt_tokens": PROMPT, "decode_tokens": 1, "batch": 1,
+            "l2": "inputs larger than L2 (2.3 GB packed weights per request)",
+            "parallelism": f"replicas x{world}"}
 
 
-def cpu_request_seconds(cfg, threads):
-    """Oracle time of one decoder layer's prefill + decode (all regions),
-    extrapolated to the request (x layers) plus the lm_head rows."""
-    import numpy as np
+def host_weights(model):
+    """The oracle's host copy of a Qwen3 model's weights (bf16 values as fp32)."""
+    from oracle import qwen3_ref
+    return qwen3_ref.model_weights(model)
 
-    from oracle import ref as R
+
+def cpu_request(cfg, weights, tokens_np, threads):
+    """One whole request on the oracle (C, OpenMP `threads`): prefill, pick,
+    one decode step, pick, all 36 layers and the lm_head. Returns (seconds,
+    RequestResult)."""
     os.environ["OMP_NUM_THREADS"] = str(threads)
+    from oracle import qwen3_ref
+    from oracle import ref as R
     R.lib()
-    W = cpu_layer_sample(cfg)
-    rng = np.random.default_rng(0)
-    h = R.round_to(rng.standard_normal((PROMPT, cfg.hidden)).astype(np.float32), "bfloat16")
-    ones_h = np.ones(cfg.hidden, np.float32)
-    ones_d = np.ones(cfg.head_dim, np.float32)
-
-    def layer(x, kc, vc, off):
-        T = x.shape[0]
-        qm = lambda a, w: R.quantized_matmul(a, *w, cfg.group, cfg.bits)
-        xn = R.rms_norm(x, ones_h, cfg.eps)
-        q, k, v = qm(xn, W["q"]), qm(xn, W["k"]), qm(xn, W["v"])
-        qh, kc, vc = R.qk_norm_rope_cache(q, k, v, ones_d, ones_d, cfg.eps, kc, vc, cfg.heads, cfg.kv_heads,
-                                          off, cfg.rope_theta)
-        o = R.sdpa(qh[None], kc[None, :, :off + T], vc[None, :, :off + T], 1 / math.sqrt(cfg.head_dim), True, off)
-        o = o[0].transpose(1, 0, 2).reshape(T, -1)
-        h2 = R.add(qm(o, W["o"]), x)
-        xn2 = R.rms_norm(h2, ones_h, cfg.eps)
-        return R.add(qm(R.swiglu(qm(xn2, W["g"]), qm(xn2, W["u"])), W["d"]), h2)
-
-    kc = np.zeros((cfg.kv_heads, cfg.max_len, cfg.head_dim), np.float32)
-    vc = np.zeros_like(kc)
     t0 = time.perf_counter()
-    layer(h, kc, vc, 0)
-    layer(h[-1:], kc, vc, PROMPT)
-    t_layer = time.perf_counter() - t0
-    # lm_head: two rows against the tied embedding (vocab x hidden), timed on a slice and scaled
-    rows = 8192
-    wq, s, b = W["g"]  # any packed matrix of width `hidden` stands in for the embedding rows
-    reps = max(1, rows // wq.shape[0])
-    t1 = time.perf_counter()
-    for _ in range(reps):
-        R.qmv(h[-1:], wq, s, b, cfg.group, cfg.bits)
-    t_head = (time.perf_counter() - t1) / (reps * wq.shape[0]) * cfg.vocab * 2
-    return t_layer * cfg.layers + t_head, t_layer
+    res = qwen3_ref.request(cfg, weights, tokens_np)
+    return time.perf_counter() - t0, res
 
 
-def cpu_baseline(cfg, threads):
-    secs, t_layer = cpu_request_seconds(cfg, threads)
-    return {"value": round(PROMPT / secs, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": (f"oracle C restatement (OpenMP {threads} threads) of 1 of {cfg.layers} decoder layers of "
-                       f"the request (prefill 128 + decode 1, all regions) = {t_layer:.2f}s, x{cfg.layers} "
-                       "+ lm_head rows timed on a slice; MLX CPU unavailable on this box")}
+def cpu_baseline(cfg, model, tokens, threads, gpu_tokens=None):
+    """The oracle timed on one whole request of this model (its weights copied
+    to the host): about 20 s of CPU work on 16 cores."""
+    w = host_weights(model)
+    secs, res = cpu_request(cfg, w, tokens.cpu().numpy(), threads)
+    out = {"value": round(PROMPT / secs, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+           "sample": (f"one whole request (prefill {PROMPT} + decode 1, all {cfg.layers} layers and the lm_head) "
+                      f"of this model's weights on the oracle C restatement, OpenMP {threads} threads: "
+                      f"{secs:.2f} s; MLX CPU unavailable on this box")}
+    if gpu_tokens is not None:
+        out["picks_agree"] = [int(gpu_tokens[0]) == res.token0, int(gpu_tokens[1]) == res.token1]
+    return out
 
 
 def run_reference(args, cfg):
-    rank, world, _ = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    """The CPU implementation of the path (the oracle port; the reference's own
+    path is MLX on an Apple GPU, unavailable on this box), on the same seeded
+    weights and prompt as the GPU arm, whole requests on all host threads.
+    Rank 0 alone runs it; other ranks exit without work."""
+    rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    import torch
+
+    from metal_autotune_b200 import workload
+    from metal_autotune_b200.targets import qwen3
     threads = os.cpu_count() or 1
-    vals = []
+    # the same seeded weights as the GPU arm: generated where that arm generates them, then copied out
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    model = qwen3.build(cfg, seed=0, device=dev)
+    weights = host_weights(model)
+    del model
+    if dev == "cuda":
+        torch.cuda.empty_cache()
+    tokens = workload.seeded_tokens((PROMPT,), 0, cfg.vocab, seed=0, device="cpu").numpy()
+    secs, times = [], []
     t_start = time.time()
     for _ in range(max(1, args.steps)):
-        secs, t_layer = cpu_request_seconds(cfg, threads)
-        vals.append(PROMPT / secs)
-        if time.time() - t_start > REFERENCE_WALL_CAP_S:
+        dt, _ = cpu_request(cfg, weights, tokens, threads)
+        times.append(dt)
+        if time.time() - t_start + dt > REFERENCE_WALL_CAP_S:
             break
-    v = statistics.median(vals)
+    ms = statistics.median(times) * 1e3
+    v = PROMPT / (ms / 1e3)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(PROMPT / v * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": "qwen3_4b_prefill_128+decode_1", "model": "Qwen3-4B 4-bit g64 (random init)",
-                       "prompt_tokens": PROMPT, "decode_tokens": 1, "batch": 1, "parallelism": "host cores"},
+            "steps": len(times), "steps_requested": args.steps, "warmup": 0, "warmup_requested": args.warmup,
+            "ms_per_step": round(ms, 3), "ms_per_step_all": [round(t * 1e3, 1) for t in times],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": qwen3_config_record(cfg, args.gpus),
             "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                             "sample": f"each step: 1 of {cfg.layers} decoder layers (prefill 128 + decode 1) "
-                                       f"timed, extrapolated x{cfg.layers}; median of {len(vals)} steps (of "
-                                       f"{args.steps} requested; wall cap {REFERENCE_WALL_CAP_S}s); the "
-                                       "reference's own path is MLX on an Apple GPU (unavailable on this box), "
-                                       "so the oracle port is timed"},
+                             "sample": f"each step one whole request (prefill {PROMPT} + decode 1, all "
+                                       f"{cfg.layers} layers and the lm_head) on the oracle C restatement, "
+                                       f"OpenMP {threads} threads; {len(times)} of {args.steps} requested steps "
+                                       f"measured (wall cap {REFERENCE_WALL_CAP_S} s); no warm-up (no caches "
+                                       "or compilation to warm); the reference's own path is MLX on an Apple "
+                                       "GPU (unavailable on this box), so the oracle port is timed"},
             "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -552,25 +571,23 @@ def run_kernels(args, cfg):
 LLAMA_B, LLAMA_L = 8, 2048
 
 
-def run_llama_tp(args):
-    """Llama-3-8B 8-bit, batch 8 x prefill 2048, tensor-parallel over the
-    ranks (one shard per GPU, NCCL all-reduce after o_proj and down).
+def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local):
+    """Llama-3-8B 8-bit prefill forward (batch B x L), tensor-parallel over the
+    `world` ranks (one shard per GPU, NCCL all-reduce after o_proj and down).
+    Every rank takes the same collective steps; times are max over ranks.
 
-      value  prompt tokens/s of the whole job (8 x 2048 / forward time),
-             CUDA events around K forwards, max over ranks
-      e2e    the same with pinned host tokens copied in and rank 0's
-             last-position logits read back every forward
-      roofline  the whole forward per GPU: its algorithmic FLOPs / tp over
-             the forward time, against the sustained bf16 peak; plus the
-             gate/up qmm+SwiGLU (the largest kernel) timed alone."""
+      ms / tok_s    the forward (CUDA events around `steps` forwards)
+      e2e           the same with pinned host tokens copied in and the gathered
+                    last-position logits read back every forward
+      per_gpu_tflops  algorithmic FLOPs / tp / forward time, vs the sustained peak
+      allreduce     the forward's 2 x layers all-reduces of [B*L, hidden] bf16
+                    timed alone (same sizes, same communicator): their share
+                    of the forward
+      gate_up_swiglu  the largest kernel alone (layer 0's shard)"""
     import torch
 
-    from metal_autotune_b200 import build, lib, workload
+    from metal_autotune_b200 import lib, workload
     from metal_autotune_b200.targets import llama_tp
-    build.build_library()
-    rank, world, local = dist_setup()
-    cfg = llama_tp.LLAMA3_8B if args.config == "llama3_8b_tp" else llama_tp.TINY
-    B, L = (LLAMA_B, LLAMA_L) if cfg.layers == 32 else (2, 128)
     comm = llama_tp.ProcessGroupComm() if world > 1 else llama_tp.LocalComm()
     t0 = time.time()
     model = llama_tp.LlamaTP(cfg, world, [rank], comm, seed=0, device="cuda")
@@ -590,23 +607,36 @@ def run_llama_tp(args):
         out["logits"] = model(tokens)
         host_logits.copy_(out["logits"], non_blocking=True)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     calls0 = lib.CALLS[0]
     with ClockSampler(local) as clk:
-        ms_total = time_region(step, args.steps, world)
-        ms_e2e_total = time_region(e2e_step, args.steps, world)
+        clk.mark_start()
+        ms_total = time_region(step, steps, world)
+        clk.mark_end()
+        ms_e2e_total = time_region(e2e_step, steps, world)
     launches = lib.CALLS[0] - calls0
-    ms = max_over_ranks(ms_total / args.steps, world)
-    ms_e2e = max_over_ranks(ms_e2e_total / args.steps, world)
+    ms = max_over_ranks(ms_total / steps, world)
+    ms_e2e = max_over_ranks(ms_e2e_total / steps, world)
     status = lib.device_status(clear=True)
     if status != 0:
         raise RuntimeError(f"device status {status:#x}: a kernel's bounded wait expired")
     if not bool(torch.isfinite(out["logits"].float()).all()):
         raise RuntimeError("non-finite logits")
 
+    # the forward's all-reduces alone: 2 per layer of the [B*L, hidden] bf16 partial
+    ar_ms = 0.0
+    if world > 1:
+        buf = torch.randn(B * L, cfg.hidden, device="cuda").to(torch.bfloat16)
+        n_ar = 2 * cfg.layers
+        for _ in range(2):
+            comm.all_reduce([buf])
+        ar_ms = max_over_ranks(time_region(lambda: [comm.all_reduce([buf]) for _ in range(n_ar)], 1, world), world)
+        del buf
+
     # the largest kernel alone: gate/up qmm + SwiGLU of layer 0 on this shard
+    from metal_autotune_b200.autotuner_runtime import measure
     peaks = measured_peaks()
     sl = model.shards[0].layers[0]
     xn = torch.randn(B * L, cfg.hidden, device="cuda", dtype=torch.bfloat16)
@@ -614,46 +644,60 @@ def run_llama_tp(args):
     run = lambda: lib.quantized_matmul_swiglu(xn, *sl.gate, *sl.up, group_size=cfg.group, bits=cfg.bits, out=act)
     for _ in range(3):
         run()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    torch.cuda.synchronize()
-    ev[0].record()
-    for _ in range(10):
-        run()
-    ev[1].record()
-    torch.cuda.synchronize()
-    k_ms = ev[0].elapsed_time(ev[1]) / 10
+    k_ms = measure.time_steps(run, 10) / 10
     k_flops = 2 * B * L * 2 * sl.gate[0].shape[0] * cfg.hidden
     fwd_flops = llama_tp.forward_flops(cfg, B, L)
     sustained = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
     achieved = fwd_flops / world / (ms / 1e3) / 1e12
-    roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": sustained, "unit": "TFLOP/s",
-            "frac": round(achieved / sustained, 4), "traffic": None, "peak_source": f"{peaks['source']} sustained",
-            "what": "whole forward per GPU (algorithmic FLOPs / tp / forward time)",
-            "forward_tflop": round(fwd_flops / 1e12, 3),
-            "gate_up_swiglu": {"ms": round(k_ms, 4), "tflops": round(k_flops / (k_ms / 1e3) / 1e12, 2),
-                               "frac_of_burst": round(k_flops / (k_ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
-                               "M": B * L, "N": 2 * sl.gate[0].shape[0], "K": cfg.hidden}}
-    if rank != 0:
-        barrier(world)
-        return 0
-    line = {
-        "metric": "Llama-3-8B-8bit prefill tok/s (batch 8 x 2048), tensor-parallel",
-        "value": round(B * L / (ms / 1e3), 2), "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "llama3_8b_prefill_8x2048" if cfg.layers == 32 else "llama_tiny",
-                   "model": "Llama-3-8B 8-bit affine g64, random init" if cfg.layers == 32 else "tiny Llama",
-                   "batch": B, "prompt_tokens": L, "parallelism": f"tp{world}",
-                   "collective": "NCCL all-reduce (bf16) after o_proj and down, all-gather of lm_head rows",
-                   "l2": "inputs larger than L2 (8.5 GB of packed weights per forward / tp)"},
-        "e2e": {"value": round(B * L / (ms_e2e / 1e3), 2), "unit": "tok/s",
-                "h2d_bytes_per_step": B * L * 4, "d2h_bytes_per_step": B * cfg.vocab * 2},
-        "roofline": roof, "clocks": clk.summary(), "gpu_launches": launches,
-        "gpu_launches_note": "libmt entry-point calls in the timed region; a blocked prefill qmm call issues "
-                             "one launch per L2-sized block, so kernel launches are at least this many",
-    }
+    rec = {"tp": world, "nccl_ranks": world if world > 1 else 0, "ms_per_forward": round(ms, 4),
+           "steps": steps, "warmup": warmup, "tok_s": round(B * L / (ms / 1e3), 2),
+           "e2e_tok_s": round(B * L / (ms_e2e / 1e3), 2),
+           "e2e_bytes": {"h2d_per_step": B * L * 4, "d2h_per_step": B * cfg.vocab * 2},
+           "forward_tflop": round(fwd_flops / 1e12, 3), "per_gpu_tflops": round(achieved, 2),
+           "frac_of_sustained": round(achieved / sustained, 4),
+           "peak": {"value": sustained, "unit": "TFLOP/s", "source": f"{peaks['source']} sustained bf16"},
+           "allreduce": {"calls_per_forward": 2 * cfg.layers if world > 1 else 0,
+                         "bytes_each": B * L * cfg.hidden * 2, "ms_alone": round(ar_ms, 4),
+                         "share_of_forward": round(ar_ms / ms, 4),
+                         "what": "NCCL bf16 all-reduce of the row-parallel partial after o_proj and down"},
+           "gate_up_swiglu": {"ms": round(k_ms, 4), "tflops": round(k_flops / (k_ms / 1e3) / 1e12, 2),
+                              "frac_of_burst": round(k_flops / (k_ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
+                              "M": B * L, "N": 2 * sl.gate[0].shape[0], "K": cfg.hidden},
+           "clocks": clk.summary(), "gpu_launches": launches,
+           "config": {"workload": "llama3_8b_prefill_8x2048" if cfg.layers == 32 else "llama_tiny",
+                      "model": "Llama-3-8B 8-bit affine g64, random init (seed 0)" if cfg.layers == 32
+                      else "tiny Llama", "batch": B, "prompt_tokens": L, "parallelism": f"tp{world}",
+                      "scaling": "strong"}}
+    del model, out
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_llama_tp(args):
+    """The Llama-3-8B tensor-parallel forward as its own JSON line."""
+    from metal_autotune_b200 import build
+    from metal_autotune_b200.targets import llama_tp
+    build.build_library()
+    rank, world, local = dist_setup()
+    cfg = llama_tp.LLAMA3_8B if args.config == "llama3_8b_tp" else llama_tp.TINY
+    B, L = (LLAMA_B, LLAMA_L) if cfg.layers == 32 else (2, 128)
+    rec = llama_tp_record(cfg, B, L, args.steps, args.warmup, rank, world, local)
+    if rank == 0:
+        line = {"metric": "Llama-3-8B-8bit prefill tok/s (batch 8 x 2048), tensor-parallel",
+                "value": rec["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": rec["ms_per_forward"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": rec["config"],
+                "e2e": {"value": rec["e2e_tok_s"], "unit": "tok/s",
+                        "h2d_bytes_per_step": rec["e2e_bytes"]["h2d_per_step"],
+                        "d2h_bytes_per_step": rec["e2e_bytes"]["d2h_per_step"]},
+                "roofline": {"bound": "tensor", "achieved": rec["per_gpu_tflops"], "peak": rec["peak"]["value"],
+                             "unit": "TFLOP/s", "frac": rec["frac_of_sustained"], "traffic": None,
+                             "what": "whole forward per GPU (algorithmic FLOPs / tp / forward time)"},
+                "clocks": rec["clocks"], "gpu_launches": rec["gpu_launches"], "llama_tp": rec}
     barrier(world)
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -671,6 +715,9 @@ def main():
     ap.add_argument("--mode", default="request", choices=["request", "kernels"])
     ap.add_argument("--only", default="", help="kernels mode: comma-separated kernel names")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-llama-tp", action="store_true",
+                    help="skip the Llama-3-8B tensor-parallel record of the default line")
+    ap.add_argument("--llama-steps", type=int, default=5, help="timed forwards of the Llama record")
     ap.add_argument("--launch-list", action="store_true",
                     help="replay the request W + K times, the K inside an NVTX range 'request', and exit "
                          "(for ncu --nvtx --nvtx-include request/)")
@@ -717,13 +764,18 @@ def main():
         log(f"launch list: {args.steps} request(s) of {req.launches_per_step} launches")
         return 0
     with ClockSampler(local) as clk:
+        soak(req.replay, 0.5)
+        clk.mark_start()
         ms_total = time_region(req.replay, args.steps, world)
+        clk.mark_end()
         ms_e2e_total = time_region(req.e2e_step, args.steps, world)
+        soak(req.replay, 0.5)
     ms = max_over_ranks(ms_total / args.steps, world)
     ms_e2e = max_over_ranks(ms_e2e_total / args.steps, world)
     status = lib.device_status(clear=True)
     if status != 0:
         raise RuntimeError(f"device status {status:#x}: a kernel's bounded wait expired")
+    gpu_picks = [int(x) for x in req.host_out[:2].tolist()]
     peaks = measured_peaks()
     roof = qmm_roofline(req, peaks)
     wbytes, ebytes = packed_weight_bytes(cfg)
@@ -733,31 +785,32 @@ def main():
     if prof.exists():
         roof["traffic"] = json.loads(prof.read_text()).get("bytes_per_launch")
         roof["traffic_note"] = json.loads(prof.read_text()).get("note")
-    if rank != 0:
-        barrier(world)
-        return 0
     line = {
         "metric": METRIC, "value": round(PROMPT * world / (ms / 1e3), 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "qwen3_4b_prefill_128+decode_1" if cfg.layers == 36 else "qwen3_tiny",
-                   "model": f"Qwen3-{'4B' if cfg.layers == 36 else 'tiny'} 4-bit affine g64, random init",
-                   "prompt_tokens": PROMPT, "decode_tokens": 1, "batch": 1,
-                   "l2": "inputs larger than L2 (2.3 GB packed weights per request)",
-                   "parallelism": f"replicas x{world}", "graph": "one CUDA graph per request"},
+        "config": qwen3_config_record(cfg, world),
+        "graph": "one CUDA graph per request",
         "e2e": {"value": round(PROMPT * world / (ms_e2e / 1e3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": 12},
         "roofline": roof, "clocks": clk.summary(),
         "gpu_launches": int(req.launches_per_step * args.steps * 2),
         "launches_per_step": req.launches_per_step,
     }
-    if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline(cfg, os.cpu_count() or 1)
+    if not args.no_cpu_baseline and world == 1 and rank == 0:
+        line["cpu_baseline"] = cpu_baseline(cfg, req.model, req.tokens, os.cpu_count() or 1, gpu_picks)
+    if not args.no_llama_tp and cfg.layers == 36:
+        # every rank builds its shard and takes the same collective steps
+        from metal_autotune_b200.targets import llama_tp
+        del req
+        torch.cuda.empty_cache()
+        line["llama_tp"] = llama_tp_record(llama_tp.LLAMA3_8B, LLAMA_B, LLAMA_L, args.llama_steps, 3, rank, world,
+                                           local)
     barrier(world)
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
-        del req
         dist.destroy_process_group()
     return 0
 

@@ -2,8 +2,9 @@
 session.py:22-249, clocks.py:26-287 — re-hosted from host wall clocks on
 Apple GPUs to device events on B200).
 
- - time_once: synchronise, record a start event, run, record an end event on
-   the same stream, synchronise; device milliseconds.
+ - time_once / time_steps: synchronise, record a start event, run (once or
+   `steps` times back to back), record an end event on the same stream,
+   synchronise; device milliseconds. bench.py times its steps with these.
  - Session.warm_until_stable: throw the first call away, then sample until
    the reading stops improving by more than max(1% of best, 100 us) for 10
    samples, at most 60 (session.py:52-70, sequence.py:152-188).
@@ -31,16 +32,27 @@ def _sync() -> None:
     torch.cuda.synchronize()
 
 
-def time_once(fn: Callable[[], object]) -> float:
-    """Device milliseconds of one call, events on the current stream."""
+def time_steps(fn: Callable[[], object], steps: int = 1, stream: torch.cuda.Stream | None = None) -> float:
+    """Device milliseconds of `steps` back-to-back calls of fn, between two
+    CUDA events recorded on `stream` (default: the current stream, which is
+    where fn launches its work), with the device synchronised on both sides."""
+    if steps < 1:
+        raise ValueError("steps must be >= 1")
+    s = stream if stream is not None else torch.cuda.current_stream()
     _sync()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    start.record()
-    fn()
-    end.record()
+    start.record(s)
+    for _ in range(steps):
+        fn()
+    end.record(s)
     _sync()
     return start.elapsed_time(end)
+
+
+def time_once(fn: Callable[[], object]) -> float:
+    """Device milliseconds of one call, events on the current stream."""
+    return time_steps(fn, 1)
 
 
 class L2Flush:
@@ -74,18 +86,22 @@ class Session:
     WARM_PATIENCE = 10
 
     def __init__(self, duty_idle_factor: float = 0.0, flush: L2Flush | None = None,
-                 sleep: Callable[[float], None] = time.sleep, log: Callable[..., None] | None = None):
+                 sleep: Callable[[float], None] = time.sleep, log: Callable[..., None] | None = None,
+                 clock: Callable[[Callable[[], object]], float] = time_once):
+        """clock(fn) -> milliseconds of one call of fn; CUDA events by default
+        (a test passes a scripted clock to drive the protocol without a GPU)."""
         self.duty_idle_factor = duty_idle_factor
         self.flush = flush
         self._sleep = sleep
         self._debt_ms = 0.0
         self._log = log
+        self._clock = clock
 
     def timed(self, fn: Callable[[], object]) -> float:
         """Milliseconds per call of fn (a chained loop reports per step)."""
         if self.flush is not None:
             self.flush.flush()
-        ms = time_once(fn)
+        ms = self._clock(fn)
         self._debt_ms += ms
         return ms / getattr(fn, "steps", 1)
 

@@ -80,8 +80,10 @@ __device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cas
 // bf16, 4-bit: (128+q)*s - 128*s in one fused op is exactly s*q before its
 // single rounding, so round(s*q) costs one HFMA2; -128*s is exact for every
 // finite bf16 scale below 2^120. fp16: (1024+q) - 1024 is exact, then one
-// rounded multiply. bf16, 8-bit: q and s*q are exact in fp32, then rounded
-// once to bf16.
+// rounded multiply (__hmul2_rn: a plain __hmul2 followed by the bias add may
+// be contracted into one fused multiply-add, which skips the rounding of s*q
+// and moves the result by up to a few ulps). bf16, 8-bit: q and s*q are
+// exact in fp32, then rounded once to bf16.
 template <int DT, int BITS>
 __device__ __forceinline__ void dequant_chunk(const uint4 wv, float s, float b, uint32_t* out);
 
@@ -116,7 +118,7 @@ __device__ __forceinline__ void dequant_chunk<MT_F16, 4>(const uint4 wv, float s
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const __half2 q = __hsub2(bits_h2(nibble_pair_f16(lo, hi, p)), k1024);
-      out[wi * 4 + p] = h2_bits(__hadd2(__hmul2(q, s2), b2));
+      out[wi * 4 + p] = h2_bits(__hadd2(__hmul2_rn(q, s2), b2));
     }
   }
 }
@@ -151,7 +153,7 @@ __device__ __forceinline__ void dequant_chunk<MT_F16, 8>(const uint4 wv, float s
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const __half2 q = __hsub2(bits_h2(byte_pair_f16(words[wi], p)), k1024);
-      out[wi * 2 + p] = h2_bits(__hadd2(__hmul2(q, s2), b2));
+      out[wi * 2 + p] = h2_bits(__hadd2(__hmul2_rn(q, s2), b2));
     }
   }
 }

@@ -41,7 +41,7 @@ class Qwen3Config:
 
 
 QWEN3_4B = Qwen3Config()
-TINY = Qwen3Config(hidden=512, layers=2, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1000, max_len=48)
+TINY = Qwen3Config(hidden=512, layers=2, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1000)
 
 
 class QLinear(nn.Module):

@@ -192,6 +192,11 @@ def qk_norm_rope_cache(q, k, v, qw, kw, eps, k_cache, v_cache, Hq, Hkv, offset, 
     q, k, v = _f32(q), _f32(k), _f32(v)
     T = q.shape[0]
     D = q.shape[1] // Hq
+    if offset < 0 or offset + T > k_cache.shape[-2] or v_cache.shape != k_cache.shape:
+        raise ValueError(f"cache rows {offset}..{offset + T} outside a cache of {k_cache.shape[-2]}")
+    for c in (k_cache, v_cache):
+        if c.dtype != np.float32 or not c.flags.c_contiguous:
+            raise ValueError("caches must be C-contiguous float32 (updated in place)")
     q_out = np.zeros((Hq, T, D), np.float32)
     lib().orc_qk_norm_rope_cache(q, k, v, _f32(qw), _f32(kw), eps, q_out, k_cache, v_cache, T, Hq, Hkv, D,
                                  k_cache.shape[-2], offset, base, DT[dtype])

@@ -227,12 +227,13 @@ def test_swiglu(cuda, oracle):
     close_bf16(n(y), oracle.swiglu(g, u), ulps=1, abs_frac=0)
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
 @pytest.mark.parametrize("bits", [4, 8])
-def test_quantized_embedding_bit_exact(cuda, oracle, bits):
-    (wq, s, b), (wq_t, s_t, b_t) = quantized(oracle, 1000, 256, 64, bits)
+def test_quantized_embedding_bit_exact(cuda, oracle, bits, dtype):
+    (wq, s, b), (wq_t, s_t, b_t) = quantized(oracle, 1000, 256, 64, bits, dtype)
     tok = np.array([0, 999, 17, 17, 500], np.int32)
     out = lib.quantized_embedding(torch.from_numpy(tok).cuda(), wq_t, s_t, b_t, bits=bits)
-    assert np.array_equal(n(out), oracle.quantized_embedding(tok, wq, s, b, 64, bits))
+    assert np.array_equal(n(out), oracle.quantized_embedding(tok, wq, s, b, 64, bits, dtype))
 
 
 def test_quantized_embedding_bad_id_reports(cuda, oracle):
