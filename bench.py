@@ -330,7 +330,7 @@ def host_weights(model):
     return qwen3_ref.model_weights(model)
 
 
-def cpu_request(cfg, weights, tokens_np, threads):
+def cpu_request(cfg, weights, tokens_np, threads, force_token0=None):
     """One whole request on the oracle (C, OpenMP `threads`): prefill, pick,
     one decode step, pick, all 36 layers and the lm_head. Returns (seconds,
     RequestResult)."""
@@ -339,21 +339,33 @@ def cpu_request(cfg, weights, tokens_np, threads):
     from oracle import ref as R
     R.lib()
     t0 = time.perf_counter()
-    res = qwen3_ref.request(cfg, weights, tokens_np)
+    res = qwen3_ref.request(cfg, weights, tokens_np, force_token0=force_token0)
     return time.perf_counter() - t0, res
 
 
-def cpu_baseline(cfg, model, tokens, threads, gpu_tokens=None):
+def cpu_baseline(cfg, model, tokens, threads, gpu=None):
     """The oracle timed on one whole request of this model (its weights copied
-    to the host): about 20 s of CPU work on 16 cores."""
+    to the host): about 20 s of CPU work on 16 cores. With gpu = (first pick,
+    second pick, decode logits) of the GPU request, the oracle decodes the
+    GPU's first pick and the two decode logits rows are compared."""
+    import numpy as np
     w = host_weights(model)
-    secs, res = cpu_request(cfg, w, tokens.cpu().numpy(), threads)
+    secs, res = cpu_request(cfg, w, tokens.cpu().numpy(), threads,
+                            force_token0=None if gpu is None else int(gpu[0]))
     out = {"value": round(PROMPT / secs, 3), "unit": "tok/s", "cores": threads, "kind": "port",
            "sample": (f"one whole request (prefill {PROMPT} + decode 1, all {cfg.layers} layers and the lm_head) "
                       f"of this model's weights on the oracle C restatement, OpenMP {threads} threads: "
                       f"{secs:.2f} s; MLX CPU unavailable on this box")}
-    if gpu_tokens is not None:
-        out["picks_agree"] = [int(gpu_tokens[0]) == res.token0, int(gpu_tokens[1]) == res.token1]
+    if gpu is not None:
+        t0, t1, lg = gpu
+        ref = res.decode_logits.astype(np.float64)
+        got = np.asarray(lg, np.float64).reshape(-1)
+        diff = np.abs(got - ref)
+        out["check"] = {"first_pick_equal": int(t0) == res.token0,
+                        "decode_logits_rel_l2": float(np.linalg.norm(got - ref) / np.linalg.norm(ref)),
+                        "decode_logits_max_abs_over_max": float(diff.max() / np.abs(ref).max()),
+                        "second_pick_gap_to_oracle_max": float(ref.max() - ref[int(t1)]),
+                        "second_pick_within_2x_max_abs": bool(ref.max() - ref[int(t1)] <= 2 * diff.max())}
     return out
 
 
@@ -776,6 +788,7 @@ def main():
     if status != 0:
         raise RuntimeError(f"device status {status:#x}: a kernel's bounded wait expired")
     gpu_picks = [int(x) for x in req.host_out[:2].tolist()]
+    gpu_decode_logits = req.model.last_logits.float().cpu().numpy()
     peaks = measured_peaks()
     roof = qmm_roofline(req, peaks)
     wbytes, ebytes = packed_weight_bytes(cfg)
@@ -798,7 +811,8 @@ def main():
         "launches_per_step": req.launches_per_step,
     }
     if not args.no_cpu_baseline and world == 1 and rank == 0:
-        line["cpu_baseline"] = cpu_baseline(cfg, req.model, req.tokens, os.cpu_count() or 1, gpu_picks)
+        line["cpu_baseline"] = cpu_baseline(cfg, req.model, req.tokens, os.cpu_count() or 1,
+                                            (gpu_picks[0], gpu_picks[1], gpu_decode_logits))
     if not args.no_llama_tp and cfg.layers == 36:
         # every rank builds its shard and takes the same collective steps
         from metal_autotune_b200.targets import llama_tp

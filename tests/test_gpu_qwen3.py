@@ -108,7 +108,7 @@ def check_request(oracle, cfg, weights, tokens_np, gpu, tol_frac):
     # logprob of the GPU's pick under the oracle's logits (lse in fp32, the difference rounded to bf16)
     r = ref.decode_logits.astype(np.float64)
     lse = np.log(np.exp(r - r.max()).sum()) + r.max()
-    lp_ref = float(oracle.round_to(np.float32(r[t1] - lse), "bfloat16"))
+    lp_ref = float(oracle.round_to(np.array([r[t1] - lse], np.float32), "bfloat16")[0])
     assert abs(lp1 - lp_ref) <= 2 * a1 + 2 ** -7 * abs(lp_ref), (lp1, lp_ref)
     return ref
 
