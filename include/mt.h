@@ -403,11 +403,24 @@ int mt_diff_reduce_noalloc(const void* a, const void* b, int64_t n, int dtype,
  * bias may be NULL. dtype MT_F32; MT_BF16 / MT_F16 run the tensor-core
  * implicit GEMM of mt_conv1d (the Whisper MLP sizes: K a multiple of 32),
  * fp32 sums with the bias added before the one rounding (mx.addmm) and GELU
- * rounded after it (not bit-reproducible: the sums run in tiles).
+ * rounded after it (not bit-reproducible: the sums run in tiles). The 16-bit
+ * path runs on the tcgen05 GEMM (tensor memory accumulators, TMA-staged
+ * operands) when K is a multiple of 8.
  */
 int mt_linear(const void* x, const void* w, const void* bias, void* y,
               int64_t M, int64_t N, int64_t K, int act, int dtype,
               mt_stream_t stream);
+
+/*
+ * The residual branch of a pre-norm block (mlx-whisper ResidualAttentionBlock:
+ * x + attn.out(...), x + mlp2(...); models/whisper_large_v3_turbo_encoder.py:
+ * 8-12): y = round(round(x[M,K] · w[N,K]^T + bias[N]) + residual[M,N]) in
+ * bf16 / f16 with fp32 sums (bias may be NULL), on the tcgen05 GEMM. K must
+ * be a multiple of 8 (MT_ERR_UNSUPPORTED otherwise); y may alias residual.
+ */
+int mt_linear_residual(const void* x, const void* w, const void* bias,
+                       const void* residual, void* y, int64_t M, int64_t N,
+                       int64_t K, int dtype, mt_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* a-8: LayerNorm                                                            */
@@ -419,7 +432,10 @@ int mt_linear(const void* x, const void* w, const void* bias, void* y,
  * Lout = (L + 2*padding - K) / stride + 1, zero padding on both sides. The
  * conv sums in fp32; conv, + bias (NULL: none) and GELU (act = 1; 0: none)
  * are each rounded to dtype as the separate MLX ops would. Cin must be a
- * multiple of 32 (MT_ERR_UNSUPPORTED otherwise); bf16 or f16.
+ * multiple of 32 (MT_ERR_UNSUPPORTED otherwise); bf16 or f16. Runs on the
+ * tcgen05 implicit GEMM when Cin is a multiple of 64, the stride 1 or 2 with
+ * L a multiple of it, and K <= 4 (both mlx-whisper stem convs); otherwise on
+ * an mma.sync implicit GEMM.
  */
 int mt_conv1d(const void* x, const void* w, const void* bias, void* y, int64_t N,
               int64_t L, int64_t Cin, int64_t Cout, int K, int stride,

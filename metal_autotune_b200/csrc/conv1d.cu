@@ -190,6 +190,9 @@ using namespace mt;
 namespace mt {
 int conv1d_run(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
                int64_t Cout, int K, int stride, int padding, int act, int dtype, int bias_fused, cudaStream_t stream);
+int gemm_tc_run(const void* x, const void* w, const void* bias, const void* residual, void* y, int64_t B,
+                int64_t L, int64_t Cin, int64_t Cout, int taps, int stride, int padding, int act, int dtype,
+                int bias_fused, int64_t ldy, cudaStream_t stream);
 }
 
 extern "C" int mt_conv1d(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
@@ -222,6 +225,13 @@ int mt::conv1d_run(const void* x, const void* w, const void* bias, void* y, int6
   MT_CHECK_ARG(aligned(x, 16) && aligned(w, 16) && aligned(y, 4), "mt_conv1d: x and w must be 16-byte aligned");
   const int64_t Lout = (L + 2 * padding - K) / stride + 1;
   if (N == 0) return MT_OK;
+  // the tcgen05 kernel takes every shape of the targets (Cin a multiple of
+  // 64, stride 1 or 2 with L a multiple of it, up to 4 taps); the mma.sync
+  // kernel below serves the rest
+  const int tc = gemm_tc_run(x, w, bias, nullptr, y, N, L, Cin, Cout, K, stride, padding, act, dtype, bias_fused,
+                             Cout, stream);
+  if (tc != MT_ERR_UNSUPPORTED) return tc;
+  clear_error();
   Conv1dParams p = {x, w, bias, y, N * Lout, (int)L, (int)Lout, (int)Cin, (int)Cout, K, stride, padding, bias_fused};
   MT_CHECK_ARG(p.M / kCvBM < 65535, "mt_conv1d: %lld output rows exceed the grid", (long long)p.M);
   const dim3 grid(static_cast<unsigned>((Cout + kCvBN - 1) / kCvBN), static_cast<unsigned>((p.M + kCvBM - 1) / kCvBM));

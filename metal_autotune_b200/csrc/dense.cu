@@ -57,6 +57,9 @@ using namespace mt;
 namespace mt {
 int conv1d_run(const void* x, const void* w, const void* bias, void* y, int64_t N, int64_t L, int64_t Cin,
                int64_t Cout, int K, int stride, int padding, int act, int dtype, int bias_fused, cudaStream_t stream);
+int gemm_tc_run(const void* x, const void* w, const void* bias, const void* residual, void* y, int64_t B,
+                int64_t L, int64_t Cin, int64_t Cout, int taps, int stride, int padding, int act, int dtype,
+                int bias_fused, int64_t ldy, cudaStream_t stream);
 }
 
 extern "C" int mt_linear(const void* x, const void* w, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
@@ -80,4 +83,23 @@ extern "C" int mt_linear(const void* x, const void* w, const void* bias, void* y
   const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((M + 31) / 32));
   return launch(linear_f32_kernel, grid, dim3(256), 0, (cudaStream_t)stream, (const float*)x, (const float*)w,
                 (const float*)bias, (float*)y, (int)M, (int)N, (int)K, act);
+}
+
+// nn.Linear (+ bias) then + residual, in 16 bits: y = round(round(x w^T + b) + r)
+// (mlx's `x + linear(...)` of a residual block), on the tcgen05 GEMM.
+extern "C" int mt_linear_residual(const void* x, const void* w, const void* bias, const void* residual, void* y,
+                                  int64_t M, int64_t N, int64_t K, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && w && y && residual, "mt_linear_residual: null pointer");
+  MT_CHECK_ARG(M >= 0 && N > 0 && K > 0 && M < (int64_t(1) << 31) && N < (1 << 24) && K < (1 << 24),
+               "mt_linear_residual: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (dtype != MT_BF16 && dtype != MT_F16) {
+    set_error("mt_linear_residual: dtype %d is not built (bf16 or f16)", dtype);
+    return MT_ERR_UNSUPPORTED;
+  }
+  if (M == 0) return MT_OK;
+  const int rc = gemm_tc_run(x, w, bias, residual, y, 1, M, K, N, 1, 1, 0, 0, dtype, 1, N, (cudaStream_t)stream);
+  if (rc == MT_ERR_UNSUPPORTED)
+    set_error("mt_linear_residual: K=%lld must be a multiple of 8 and x, w 16-byte aligned", (long long)K);
+  return rc;
 }

@@ -1,0 +1,394 @@
+// Dense 16-bit GEMM and implicit-GEMM conv1d on the 5th-generation tensor
+// cores (tcgen05 + TMA + tensor memory), for the GELU-MLP linears and the
+// conv stem (mx.addmm / nn.Linear, mx.conv1d + bias + GELU).
+//
+//   y[(b, t), n] = epilogue( sum over taps j, channels c of
+//                            x[b, t*stride + j - pad, c] * w[n, j, c] )
+//
+// A linear is the one-tap case (b = 0, t = row, stride 1, pad 0). x is
+// channels-last [B, L, Cin], w is [Cout, taps, Cin] (mlx layouts), y is
+// [B, Lout, Cout] with row pitch ldy.
+//
+// Tiles: 128 output rows (t) x BN output columns (n), BN = 128 or 256, one
+// persistent CTA per SM walking the tiles in groups of 8 row tiles per
+// column sweep (the row tiles of a group share the weight tiles in L2). The
+// reduction runs in K-blocks of 64 channels of one tap, each one TMA copy
+// of the x tile and one of the weight tile into a 4-stage shared-memory ring
+// (128-byte swizzle). The x copy addresses the input through a 3-D tensor
+// map (channels*v, L/v, B) with v = stride: output row t of tap j reads view
+// row t + floor((j - pad)/v) at channel offset ((j - pad) mod v)*Cin, so a
+// stride-2 conv needs no gather and the zero padding at both ends is the
+// copy's out-of-range fill (a negative row coordinate reads zeros).
+//
+// Roles (192 threads): warp 0 issues the TMA copies; warp 1 owns the tensor
+// memory (two BN-column fp32 accumulators) and one elected lane issues
+// tcgen05.mma.kind::f16 (M = 128, N = BN, K = 16; both operands from shared
+// memory); warps 2-5 are the epilogue: each reads its 32 accumulator rows
+// from tensor memory (tcgen05.ld), rounds as the MLX ops would, and stores,
+// while the MMAs of the next tile run into the other accumulator.
+//
+// Epilogue rounding (element type T = bf16 or f16):
+//   conv   (bias_fused = 0): round(acc), + bias -> round, GELU -> round
+//   linear (bias_fused = 1): round(acc + bias) (mx.addmm: one rounding),
+//                            GELU -> round
+//   residual (optional):     + residual -> round
+//
+// Every mbarrier wait is bounded (2 s); on expiry the CTA records a site code
+// in the device status word, stops issuing, drains its in-flight copies and
+// MMAs (bounded) and frees its tensor memory.
+#include "mt_common.cuh"
+#include "mt_tma.h"
+
+namespace mt {
+
+constexpr int kGtBM = 128;
+constexpr int kGtBK = 64;
+constexpr int kGtStages = 4;
+constexpr int kGtThreads = 192;
+constexpr int kGtGroup = 8;  // row tiles per column sweep
+constexpr int kGtMaxTaps = 4;
+
+struct GemmTcParams {
+  CUtensorMap tma_x;  // (Cin*v, L/v, B), box (64, 128, 1)
+  CUtensorMap tma_w;  // (taps*Cin, Cout), box (64, BN)
+  const void* bias;
+  const void* residual;
+  void* y;
+  long long ldy;       // y / residual row pitch in elements
+  int B, Lout, Cin, Cout, taps, kb_per_tap;
+  int dr[kGtMaxTaps];  // view-row offset of each tap
+  int dc[kGtMaxTaps];  // channel offset of each tap
+  int mt_per_b, num_mt, num_nt, tiles;
+  int bias_fused, vec;
+};
+
+template <int BN>
+struct GtSmem {
+  static constexpr int kA = kGtBM * kGtBK * 2;  // 16 KB
+  static constexpr int kB = BN * kGtBK * 2;     // 16 / 32 KB
+  static constexpr int kStage = kA + kB;
+  static constexpr int kBars = 1024;            // barriers and flags after the ring
+  static constexpr int kTotal = kGtStages * kStage + kBars + 1024;  // + alignment slack
+};
+
+struct GtTile {
+  int b, t0, n0;
+};
+
+__device__ __forceinline__ GtTile gt_tile(const GemmTcParams& p, int id) {
+  const int span = kGtGroup * p.num_nt;
+  const int group = id / span;
+  const int first = group * kGtGroup;
+  const int gsz = min(kGtGroup, p.num_mt - first);
+  const int in = id - group * span;
+  const int m = first + in % gsz;
+  GtTile t;
+  t.n0 = in / gsz;  // column tile index
+  t.b = m / p.mt_per_b;
+  t.t0 = (m - t.b * p.mt_per_b) * kGtBM;
+  return t;
+}
+
+template <int DT, int BN, int ACT>
+__global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmTcParams p) {
+  using T = typename Elem<DT>::T;
+  using S = GtSmem<BN>;
+  extern __shared__ uint8_t gt_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gt_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGtStages * S::kStage);
+  uint64_t* full = bars;                       // [stages]
+  uint64_t* empty = bars + kGtStages;          // [stages]
+  uint64_t* acc_full = bars + 2 * kGtStages;   // [2]
+  uint64_t* acc_empty = acc_full + 2;          // [2]
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tma_x);
+    prefetch_tmap(&p.tma_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch();
+
+  const int kblocks = p.taps * p.kb_per_tap;
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    int s = 0, ph = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (int id = blockIdx.x; id < p.tiles && ok; id += gridDim.x) {
+      const GtTile tl = gt_tile(p, id);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait_warp(&empty[s], ph ^ 1, abort_flag, 0x601)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
+          const int j = kb / p.kb_per_tap;
+          const int c = (kb - j * p.kb_per_tap) * kGtBK;
+          uint8_t* a = ring + s * S::kStage;
+          mbar_arrive_expect_tx(&full[s], S::kStage);
+          tma_load_3d(a, &p.tma_x, &full[s], c + p.dc[j], tl.t0 + p.dr[j], tl.b);
+          tma_load_2d(a + S::kA, &p.tma_w, &full[s], j * p.Cin + c, tl.n0 * BN);
+        }
+        __syncwarp();
+        ++issued;
+        if (++s == kGtStages) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+    if (!ok) {  // let the copies already issued land before the CTA exits
+      const long long first = issued > kGtStages ? issued - kGtStages : 0;
+      for (long long i = first; i < issued; ++i)
+        mbar_wait_drain(&full[i % kGtStages], static_cast<uint32_t>((i / kGtStages) & 1), 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = idesc_f16(kGtBM, BN, DT == MT_BF16);
+    const uint64_t ring_desc = smem_desc_k_sw128(smem_addr(ring));
+    const uint32_t stage_step = S::kStage >> 4, b_off = S::kA >> 4;
+    int s = 0, ph = 0, buf = 0;
+    int use[2] = {0, 0};
+    bool ok = true, issued = false;
+    for (int id = blockIdx.x; id < p.tiles && ok; id += gridDim.x) {
+      if (!mbar_wait_warp(&acc_empty[buf], (use[buf] & 1) ^ 1, abort_flag, 0x602)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait_warp(&full[s], ph, abort_flag, 0x603)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = ring_desc + s * stage_step;
+        const uint64_t bd = ad + b_off;
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < kGtBK / 16; ++kk)
+            tc_mma_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&empty[s]);
+        }
+        __syncwarp();
+        issued = true;
+        if (++s == kGtStages) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (elect_one()) tc_commit(&acc_full[buf]);
+      __syncwarp();
+      ++use[buf];
+      buf ^= 1;
+    }
+    if (__any_sync(0xffffffffu, *abort_flag != 0) && issued) {
+      if (elect_one()) {
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0, 200000000ull);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // tensor-memory lanes [32*quad, 32*quad + 32)
+    const int row = quad * 32 + lane;
+    const T* bias = static_cast<const T*>(p.bias);
+    const T* res = static_cast<const T*>(p.residual);
+    T* y = static_cast<T*>(p.y);
+    int buf = 0;
+    int use[2] = {0, 0};
+    for (int id = blockIdx.x; id < p.tiles; id += gridDim.x) {
+      const GtTile tl = gt_tile(p, id);
+      if (!mbar_wait_warp(&acc_full[buf], use[buf] & 1, abort_flag, 0x604)) break;
+      tc_fence_after();
+      const int t = tl.t0 + row;
+      const bool live = t < p.Lout;
+      const long long yrow = (static_cast<long long>(tl.b) * p.Lout + t) * p.ldy;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+        tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + ch * 32, r);
+        tmem_wait_ld();
+        const int n0 = tl.n0 * BN + ch * 32;
+        if (!live || n0 >= p.Cout) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        // bias, in 16-byte pieces when the chunk is whole
+        float bv[32];
+        if (bias) {
+          if (p.vec && n0 + 32 <= p.Cout) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 u = *reinterpret_cast<const uint4*>(bias + n0 + 8 * q);
+              const typename Elem<DT>::T2* h = reinterpret_cast<const typename Elem<DT>::T2*>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = Elem<DT>::unpack2(h[e]);
+                bv[8 * q + 2 * e] = f.x;
+                bv[8 * q + 2 * e + 1] = f.y;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) bv[i] = n0 + i < p.Cout ? Elem<DT>::to_f(bias[n0 + i]) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float u;
+          if (p.bias_fused)
+            u = round_to<DT>(bias ? v[i] + bv[i] : v[i]);
+          else
+            u = bias ? round_to<DT>(round_to<DT>(v[i]) + bv[i]) : round_to<DT>(v[i]);
+          if (ACT == 1) u = round_to<DT>(gelu_erf_f32(u));
+          v[i] = u;
+        }
+        if (res) {
+          if (p.vec && n0 + 32 <= p.Cout) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 u = *reinterpret_cast<const uint4*>(res + yrow + n0 + 8 * q);
+              const typename Elem<DT>::T2* h = reinterpret_cast<const typename Elem<DT>::T2*>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = Elem<DT>::unpack2(h[e]);
+                v[8 * q + 2 * e] = round_to<DT>(v[8 * q + 2 * e] + f.x);
+                v[8 * q + 2 * e + 1] = round_to<DT>(v[8 * q + 2 * e + 1] + f.y);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n0 + i < p.Cout) v[i] = round_to<DT>(v[i] + Elem<DT>::to_f(res[yrow + n0 + i]));
+          }
+        }
+        if (p.vec && n0 + 32 <= p.Cout) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 u;
+            typename Elem<DT>::T2* h = reinterpret_cast<typename Elem<DT>::T2*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = Elem<DT>::pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+            *reinterpret_cast<uint4*>(y + yrow + n0 + 8 * q) = u;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (n0 + i < p.Cout) y[yrow + n0 + i] = Elem<DT>::from_f(v[i]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      ++use[buf];
+      buf ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 2 * BN);
+}
+
+// Tensor-core eligibility and launch. Returns MT_ERR_UNSUPPORTED when the
+// shape is outside what this kernel takes (the caller then uses the
+// mma.sync implicit GEMM).
+int gemm_tc_run(const void* x, const void* w, const void* bias, const void* residual, void* y, int64_t B,
+                int64_t L, int64_t Cin, int64_t Cout, int taps, int stride, int padding, int act, int dtype,
+                int bias_fused, int64_t ldy, cudaStream_t stream) {
+  if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED;
+  if (taps < 1 || taps > kGtMaxTaps || (stride != 1 && stride != 2)) return MT_ERR_UNSUPPORTED;
+  if (taps > 1 ? Cin % kGtBK != 0 : Cin % 8 != 0) return MT_ERR_UNSUPPORTED;
+  if (L % stride != 0 || !aligned(x, 16) || !aligned(w, 16)) return MT_ERR_UNSUPPORTED;
+  const int64_t Lout = (L + 2 * padding - taps) / stride + 1;
+  if (Lout < 1 || B < 1) return MT_ERR_UNSUPPORTED;
+  if (B * Lout >= (int64_t(1) << 31) || Cout >= (1 << 24) || taps * Cin >= (1 << 24)) return MT_ERR_UNSUPPORTED;
+
+  GemmTcParams p;
+  memset(&p, 0, sizeof(p));
+  const int BN = Cout <= 128 ? 128 : 256;
+  const CUtensorMapDataType dt = dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(Cin * stride), static_cast<uint64_t>(L / stride),
+                              static_cast<uint64_t>(B)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(Cin * stride * 2), static_cast<uint64_t>(L * Cin * 2)};
+    const uint32_t box[3] = {kGtBK, kGtBM, 1};
+    const int rc = make_tmap(&p.tma_x, x, dt, 2, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != MT_OK) return rc;
+  }
+  {
+    const int rc = make_tmap_2d(&p.tma_w, w, dt, 2, static_cast<uint64_t>(taps * Cin), static_cast<uint64_t>(Cout),
+                                static_cast<uint64_t>(taps * Cin * 2), kGtBK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != MT_OK) return rc;
+  }
+  for (int j = 0; j < taps; ++j) {
+    const int o = j - padding;
+    const int q = o >= 0 ? o / stride : -((-o + stride - 1) / stride);  // floor division
+    p.dr[j] = q;
+    p.dc[j] = (o - q * stride) * static_cast<int>(Cin);
+  }
+  p.bias = bias;
+  p.residual = residual;
+  p.y = y;
+  p.ldy = ldy;
+  p.B = static_cast<int>(B);
+  p.Lout = static_cast<int>(Lout);
+  p.Cin = static_cast<int>(Cin);
+  p.Cout = static_cast<int>(Cout);
+  p.taps = taps;
+  p.kb_per_tap = static_cast<int>((Cin + kGtBK - 1) / kGtBK);
+  p.mt_per_b = static_cast<int>((Lout + kGtBM - 1) / kGtBM);
+  p.num_mt = p.mt_per_b * p.B;
+  p.num_nt = static_cast<int>((Cout + BN - 1) / BN);
+  const int64_t tiles = static_cast<int64_t>(p.num_mt) * p.num_nt;
+  if (tiles >= (int64_t(1) << 31)) return MT_ERR_UNSUPPORTED;
+  p.tiles = static_cast<int>(tiles);
+  p.bias_fused = bias_fused;
+  p.vec = (ldy % 8 == 0) && aligned(y, 16) && (!bias || aligned(bias, 16)) && (!residual || aligned(residual, 16));
+  int sms = 148;
+  if (int e = device_sm_count(&sms)) return e;
+  const unsigned grid = static_cast<unsigned>(p.tiles < sms ? p.tiles : sms);
+  auto run = [&](auto kern, size_t smem) -> int {
+    if (int e = ensure_smem(kern, smem)) return e;
+    return launch(kern, dim3(grid), dim3(kGtThreads), smem, stream, p);
+  };
+  const bool bf = dtype == MT_BF16;
+  if (BN == 128) {
+    const size_t sm = GtSmem<128>::kTotal;
+    if (bf) return act ? run(gemm_tc_kernel<MT_BF16, 128, 1>, sm) : run(gemm_tc_kernel<MT_BF16, 128, 0>, sm);
+    return act ? run(gemm_tc_kernel<MT_F16, 128, 1>, sm) : run(gemm_tc_kernel<MT_F16, 128, 0>, sm);
+  }
+  const size_t sm = GtSmem<256>::kTotal;
+  if (bf) return act ? run(gemm_tc_kernel<MT_BF16, 256, 1>, sm) : run(gemm_tc_kernel<MT_BF16, 256, 0>, sm);
+  return act ? run(gemm_tc_kernel<MT_F16, 256, 1>, sm) : run(gemm_tc_kernel<MT_F16, 256, 0>, sm);
+}
+
+}  // namespace mt

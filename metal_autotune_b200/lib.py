@@ -91,6 +91,7 @@ SIGNATURES = {
     "mt_diff_reduce": (C.c_int, [P, P, I64, I32, F32, F32, F32, P, P, SZ, P]),
     "mt_diff_reduce_noalloc": (C.c_int, [P, P, I64, I32, F32, F32, F32, P, P]),
     "mt_linear": (C.c_int, [P, P, P, P, I64, I64, I64, I32, I32, P]),
+    "mt_linear_residual": (C.c_int, [P, P, P, P, P, I64, I64, I64, I32, P]),
     "mt_layer_norm": (C.c_int, [P, P, P, F32, P, I64, I64, I32, P]),
     "mt_mamba_scan": (C.c_int, [P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I32, P]),
     "mt_causal_conv1d": (C.c_int, [P, P, P, P, P, I64, I64, I32, I32, I32, P]),
@@ -472,6 +473,20 @@ def linear(x, w, bias=None, *, act=0, out=None):
     N = w.shape[0]
     y = out if out is not None else torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
     call("mt_linear", _ptr(x), _ptr(w), _ptr(bias), _ptr(y), M, N, K, int(act), dtype_code(x.dtype), _stream())
+    return y
+
+
+def linear_residual(x, w, bias, residual, *, out=None):
+    """round(round(x @ w.T + bias) + residual) in x's 16-bit dtype (tcgen05 GEMM)."""
+    K = x.shape[-1]
+    M = x.numel() // K
+    N = w.shape[0]
+    _dense(x, "x")
+    _dense(w, "w")
+    _dense(residual, "residual")
+    y = out if out is not None else torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
+    call("mt_linear_residual", _ptr(x), _ptr(w), _ptr(bias) if bias is not None else None, _ptr(residual), _ptr(y),
+         M, N, K, dtype_code(x.dtype), _stream())
     return y
 
 

@@ -410,6 +410,10 @@ CONV_CASES = [
     (1, 50, 64, 129, 3, 1, 1, 0, True, "bfloat16"),        # odd Cout: scalar tail stores
     (1, 3000, 128, 1280, 3, 1, 1, 1, True, "float16"),     # mlx-whisper conv1 at full length
     (1, 600, 1280, 1280, 3, 2, 1, 1, True, "float16"),     # conv2 channels, shortened
+    (2, 3000, 1280, 1280, 3, 2, 1, 1, True, "float16"),    # mlx-whisper conv2 at full length, two clips
+    (3, 200, 128, 256, 3, 1, 1, 1, True, "bfloat16"),      # several clips, row tiles ending mid-clip
+    (1, 301, 128, 128, 3, 2, 1, 1, True, "float16"),       # stride 2 over an odd length (mma.sync path)
+    (2, 64, 64, 64, 4, 1, 2, 0, False, "bfloat16"),        # 4 taps, padding 2
 ]
 
 
@@ -439,6 +443,10 @@ def test_conv1d(cuda, oracle, N, L, Cin, Cout, K, stride, pad, act, bias, dtype)
     (37, 130, 64, 0, False, "bfloat16"),
     (1500, 5120, 1280, 1, True, "float16"),   # mlx-whisper fc1 for one 1500-frame clip
     (1500, 1280, 5120, 0, True, "float16"),   # fc2
+    (200, 256, 200, 0, True, "bfloat16"),     # K not a multiple of 64: zero-filled tail block
+    (512, 96, 2048, 0, False, "float16"),     # Mamba-370m x_proj (N = dt_rank + 2 d_state)
+    (512, 4096, 1024, 0, False, "float16"),   # Mamba-370m in_proj
+    (512, 2048, 64, 0, True, "float16"),      # Mamba-370m dt_proj
 ])
 def test_linear_16bit(cuda, oracle, M, N, K, act, bias, dtype):
     tdt = BF if dtype == "bfloat16" else torch.float16
@@ -449,6 +457,26 @@ def test_linear_16bit(cuda, oracle, M, N, K, act, bias, dtype):
     y = lib.linear(t(x, tdt), t(w, tdt), t(b, tdt) if bias else None, act=act)
     torch.cuda.synchronize()
     ref = oracle.linear_lp(x, w, b, act, dtype)
+    ulp = 2.0 ** (-7 if dtype == "bfloat16" else -10)
+    got, refd = n(y).astype(np.float64), ref.astype(np.float64)
+    tol = 3 * ulp * np.abs(refd) + 2 * ulp * np.abs(refd).max()
+    bad = np.abs(got - refd) > tol
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance; worst {np.abs(got - refd).max():.4g}"
+
+
+@pytest.mark.parametrize("M,N,K,bias,dtype", [(300, 1280, 1280, True, "float16"), (129, 200, 512, False, "bfloat16"),
+                                             (1500, 1280, 5120, True, "float16")])
+def test_linear_residual(cuda, oracle, M, N, K, bias, dtype):
+    """x + linear(h): round(round(h w^T + b) + x), the residual branch of the
+    mlx-whisper blocks, against the oracle's linear then add."""
+    tdt = BF if dtype == "bfloat16" else torch.float16
+    r = np.random.default_rng(M * 3 + N + K)
+    h = oracle.round_to(r.standard_normal((M, K)).astype(np.float32), dtype)
+    w = oracle.round_to(r.standard_normal((N, K)).astype(np.float32) / np.sqrt(K), dtype)
+    b = oracle.round_to(r.standard_normal(N).astype(np.float32) * 0.1, dtype) if bias else None
+    x = oracle.round_to(r.standard_normal((M, N)).astype(np.float32), dtype)
+    y = lib.linear_residual(t(h, tdt), t(w, tdt), t(b, tdt) if bias else None, t(x, tdt))
+    ref = oracle.add(oracle.linear_lp(h, w, b, 0, dtype), x, dtype)
     ulp = 2.0 ** (-7 if dtype == "bfloat16" else -10)
     got, refd = n(y).astype(np.float64), ref.astype(np.float64)
     tol = 3 * ulp * np.abs(refd) + 2 * ulp * np.abs(refd).max()
