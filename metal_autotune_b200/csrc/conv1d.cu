@@ -218,20 +218,20 @@ int mt::conv1d_run(const void* x, const void* w, const void* bias, void* y, int6
     set_error("mt_conv1d: dtype %d is not built (bf16 or f16)", dtype);
     return MT_ERR_UNSUPPORTED;
   }
-  if (Cin % kCvBK != 0) {
-    set_error("mt_conv1d: Cin=%lld must be a multiple of %d", (long long)Cin, kCvBK);
-    return MT_ERR_UNSUPPORTED;
-  }
   MT_CHECK_ARG(aligned(x, 16) && aligned(w, 16) && aligned(y, 4), "mt_conv1d: x and w must be 16-byte aligned");
   const int64_t Lout = (L + 2 * padding - K) / stride + 1;
   if (N == 0) return MT_OK;
   // the tcgen05 kernel takes every shape of the targets (Cin a multiple of
-  // 64, stride 1 or 2 with L a multiple of it, up to 4 taps); the mma.sync
-  // kernel below serves the rest
+  // 64, or of 8 for one tap; stride 1 or 2 with L a multiple of it; up to 4
+  // taps); the mma.sync kernel below serves the rest
   const int tc = gemm_tc_run(x, w, bias, nullptr, y, N, L, Cin, Cout, K, stride, padding, act, dtype, bias_fused,
                              Cout, stream);
   if (tc != MT_ERR_UNSUPPORTED) return tc;
   clear_error();
+  if (Cin % kCvBK != 0) {
+    set_error("mt_conv1d: Cin=%lld must be a multiple of %d", (long long)Cin, kCvBK);
+    return MT_ERR_UNSUPPORTED;
+  }
   Conv1dParams p = {x, w, bias, y, N * Lout, (int)L, (int)Lout, (int)Cin, (int)Cout, K, stride, padding, bias_fused};
   MT_CHECK_ARG(p.M / kCvBM < 65535, "mt_conv1d: %lld output rows exceed the grid", (long long)p.M);
   const dim3 grid(static_cast<unsigned>((Cout + kCvBN - 1) / kCvBN), static_cast<unsigned>((p.M + kCvBM - 1) / kCvBM));

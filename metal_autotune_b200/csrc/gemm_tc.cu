@@ -20,12 +20,13 @@
 // stride-2 conv needs no gather and the zero padding at both ends is the
 // copy's out-of-range fill (a negative row coordinate reads zeros).
 //
-// Roles (192 threads): warp 0 issues the TMA copies; warp 1 owns the tensor
+// Roles (320 threads): warp 0 issues the TMA copies; warp 1 owns the tensor
 // memory (two BN-column fp32 accumulators) and one elected lane issues
 // tcgen05.mma.kind::f16 (M = 128, N = BN, K = 16; both operands from shared
-// memory); warps 2-5 are the epilogue: each reads its 32 accumulator rows
-// from tensor memory (tcgen05.ld), rounds as the MLX ops would, and stores,
-// while the MMAs of the next tile run into the other accumulator.
+// memory); warps 2-9 are the epilogue: each reads 32 accumulator rows of
+// every other 32-column chunk from tensor memory (tcgen05.ld), rounds as the
+// MLX ops would, and stores, while the MMAs of the next tile run into the
+// other accumulator. GELU here uses the branch-free erf of gelu_as_f32.
 //
 // Epilogue rounding (element type T = bf16 or f16):
 //   conv   (bias_fused = 0): round(acc), + bias -> round, GELU -> round
@@ -44,7 +45,8 @@ namespace mt {
 constexpr int kGtBM = 128;
 constexpr int kGtBK = 64;
 constexpr int kGtStages = 4;
-constexpr int kGtThreads = 192;
+constexpr int kGtThreads = 320;
+constexpr int kGtEpiWarps = 8;  // two per tensor-memory lane quadrant
 constexpr int kGtGroup = 8;  // row tiles per column sweep
 constexpr int kGtMaxTaps = 4;
 
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);  // one arrive per epilogue warp
+      mbar_init(&acc_empty[a], kGtEpiWarps);  // one arrive per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -216,7 +218,11 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;  // tensor-memory lanes [32*quad, 32*quad + 32)
+    // warps 2-9: warp w reads tensor-memory lanes [32*(w%4), +32) (the lane
+    // quadrant its warp index allows) and every other 32-column chunk, the
+    // pair of warps of a quadrant splitting the columns between them
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
     const T* bias = static_cast<const T*>(p.bias);
     const T* res = static_cast<const T*>(p.residual);
@@ -231,7 +237,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
       const bool live = t < p.Lout;
       const long long yrow = (static_cast<long long>(tl.b) * p.Lout + t) * p.ldy;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
+      for (int ch = half; ch < BN / 32; ch += 2) {
         uint32_t r[32];
         __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
         tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + ch * 32, r);
@@ -268,7 +274,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
             u = round_to<DT>(bias ? v[i] + bv[i] : v[i]);
           else
             u = bias ? round_to<DT>(round_to<DT>(v[i]) + bv[i]) : round_to<DT>(v[i]);
-          if (ACT == 1) u = round_to<DT>(gelu_erf_f32(u));
+          if (ACT == 1) u = round_to<DT>(gelu_as_f32(u));
           v[i] = u;
         }
         if (res) {

@@ -154,6 +154,27 @@ __device__ __forceinline__ float gelu_erf_f32(float x) {
   return __fdiv_rn(__fmul_rn(x, u), 2.0f);
 }
 
+// GELU for results rounded to a 16-bit type: the same exact (erf) form, with
+// erf from Abramowitz & Stegun, Handbook of Mathematical Functions, formula
+// 7.1.26 (Hastings' rational approximation, |error| <= 1.5e-7) and the
+// hardware base-2 exponential. Branch-free, so a warp evaluates many values
+// back to back; its error (a few 1e-7 absolute) is far below the 2^-8 / 2^-11
+// relative step of bf16 / f16 that the caller rounds to.
+__device__ __forceinline__ float gelu_as_f32(float x) {
+  const float z = x * 0.70710678118654752f;
+  const float az = fabsf(z);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, az, 1.0f));
+  float q = fmaf(1.061405429f, t, -1.453152027f);
+  q = fmaf(q, t, 1.421413741f);
+  q = fmaf(q, t, -0.284496736f);
+  q = fmaf(q, t, 0.254829592f);
+  q *= t;
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-az * az * 1.44269504088896341f));
+  const float erf_z = copysignf(1.0f - q * e, z);
+  return 0.5f * x * (1.0f + erf_z);
+}
+
 __device__ __forceinline__ void griddep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
