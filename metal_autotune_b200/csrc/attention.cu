@@ -539,6 +539,13 @@ extern "C" int mt_qk_norm_rope_sdpa_decode(const void* q, const void* k, const v
   return one ? run(decode_attn_kernel<MT_F16, 1>) : run(decode_attn_kernel<MT_F16, 3>);
 }
 
+namespace mt {
+int attn_tc_run(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv, int64_t Lq,
+                int64_t Lk, int64_t D, float scale, int causal, int64_t q_offset, int64_t qs_b, int64_t qs_h,
+                int64_t qs_l, int64_t ks_b, int64_t ks_h, int64_t ks_l, int64_t vs_b, int64_t vs_h, int64_t vs_l,
+                int64_t os_b, int64_t os_h, int64_t os_l, int dtype, cudaStream_t stream);
+}
+
 extern "C" int mt_sdpa(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv,
                        int64_t Lq, int64_t Lk, int64_t D, float scale, int causal, int64_t q_offset, int64_t qs_b,
                        int64_t qs_h, int64_t qs_l, int64_t ks_b, int64_t ks_h, int64_t ks_l, int64_t vs_b,
@@ -556,6 +563,12 @@ extern "C" int mt_sdpa(const void* q, const void* k, const void* v, void* o, int
                    qs_b % 8 == 0 && ks_b % 8 == 0 && vs_b % 8 == 0 && os_l % 2 == 0,
                "mt_sdpa: q/k/v rows must be 16-byte aligned");
   if (B == 0 || Lq == 0) return MT_OK;
+  // tensor-core flash attention (tcgen05, TMA) for every layout TMA can
+  // address; the mma.sync kernel below serves the rest
+  const int tc = attn_tc_run(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, scale, causal, q_offset, qs_b, qs_h, qs_l, ks_b, ks_h,
+                             ks_l, vs_b, vs_h, vs_l, os_b, os_h, os_l, dtype, (cudaStream_t)stream);
+  if (tc != MT_ERR_UNSUPPORTED) return tc;
+  clear_error();
   SdpaParams p = {q, k, v, o, qs_b, qs_h, qs_l, ks_b, ks_h, ks_l, vs_b, vs_h, vs_l, os_b, os_h, os_l,
                   (int)Hq, (int)Hkv, (int)Lq, (int)Lk, q_offset, scale * 1.4426950408889634f, causal};
   const dim3 grid(static_cast<unsigned>((Lq + 63) / 64), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
