@@ -563,9 +563,13 @@ extern "C" int mt_sdpa(const void* q, const void* k, const void* v, void* o, int
                    qs_b % 8 == 0 && ks_b % 8 == 0 && vs_b % 8 == 0 && os_l % 2 == 0,
                "mt_sdpa: q/k/v rows must be 16-byte aligned");
   if (B == 0 || Lq == 0) return MT_OK;
-  // tensor-core flash attention (tcgen05, TMA) for every layout TMA can
-  // address; the mma.sync kernel below serves the rest
-  const int tc = attn_tc_run(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, scale, causal, q_offset, qs_b, qs_h, qs_l, ks_b, ks_h,
+  // tensor-core flash attention (tcgen05, TMA) for sequences of several key
+  // blocks in any layout TMA can address (measured on B200: Llama-3-8B
+  // prefill [8, 32/8, 2048, 128] causal 1040 -> 512 us, mlx-whisper encoder
+  // [8, 20, 1500, 64] 406 -> 254 us); short ones (the Qwen3 prefill, 128 x 128
+  // per head: 5.4 us here against 7.0 us there, the tensor-memory set-up of a
+  // one-block CTA not amortised) and other layouts stay on the mma.sync kernel
+  const int tc = (Lq < 64 || Lk < 384) ? MT_ERR_UNSUPPORTED : attn_tc_run(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, scale, causal, q_offset, qs_b, qs_h, qs_l, ks_b, ks_h,
                              ks_l, vs_b, vs_h, vs_l, os_b, os_h, os_l, dtype, (cudaStream_t)stream);
   if (tc != MT_ERR_UNSUPPORTED) return tc;
   clear_error();
