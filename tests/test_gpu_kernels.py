@@ -203,11 +203,12 @@ def test_qk_norm_rope_cache(cuda, oracle, T, offset):
     (1, 20, 20, 1500, 1500, 64, False),
     # Llama-3-8B prefill heads over 1024 of its 2048 positions (GQA 32/8)
     (1, 32, 8, 1024, 1024, 128, True),
-    # tcgen05 path: ragged query and key blocks, a chunk of queries after a cached prefix
-    # (q_offset = Lk - Lq > 0 with the diagonal inside a key block), two clips
+    # tcgen05 path (from 64 queries and 384 keys): ragged query and key blocks, a chunk of
+    # queries after a cached prefix (q_offset = Lk - Lq > 0, the diagonal inside a key block),
+    # two clips
     (1, 8, 2, 300, 700, 128, True),
-    (2, 4, 4, 129, 257, 64, True),
-    (2, 6, 3, 256, 256, 128, False),
+    (2, 4, 4, 129, 513, 64, True),
+    (2, 6, 3, 400, 400, 128, False),
 ])
 def test_sdpa(cuda, oracle, B, Hq, Hkv, Lq, Lk, D, causal):
     q = oracle.round_to(rng.standard_normal((B, Hq, Lq, D)).astype(np.float32), "bfloat16")
