@@ -716,14 +716,213 @@ def run_llama_tp(args):
     return 0
 
 
+# ------------------------------------------------------------------ other targets
+WHISPER_BATCH, MAMBA_TOKENS = 8, 512
+
+
+class ModelStep:
+    """A bundle-applied target, its seeded device input and pinned host
+    copies, one forward captured in a CUDA graph."""
+
+    def __init__(self, kind: str, tiny: bool = False):
+        import torch
+
+        from metal_autotune_b200 import lib, workload
+        from metal_autotune_b200.autotuner_runtime.apply import apply
+        os.environ["MT_STRICT_REGIONS"] = "1"
+        self.torch, self.kind = torch, kind
+        bdir = ROOT / "metal_autotune_b200" / "bundles"
+        if kind == "whisper":
+            from metal_autotune_b200.targets import whisper
+            self.cfg = whisper.TINY if tiny else whisper.WHISPER_TURBO
+            model = whisper.build(self.cfg, seed=0)
+            g = torch.Generator(device="cuda").manual_seed(0)
+            self.x = torch.randn(WHISPER_BATCH, self.cfg.frames, self.cfg.n_mels, generator=g,
+                                 device="cuda").to(torch.float16)
+            self.model = apply(model, bdir / ("whisper_tiny" if tiny else "whisper_turbo"))
+            self.flops = whisper.encoder_flops(self.cfg, WHISPER_BATCH)
+            self.units = WHISPER_BATCH * self.cfg.frames
+        elif kind == "mamba":
+            from metal_autotune_b200.targets import mamba
+            self.cfg = mamba.TINY if tiny else mamba.MAMBA_370M
+            model = mamba.build(self.cfg, seed=0)
+            self.x = workload.seeded_tokens((MAMBA_TOKENS,), 0, self.cfg.vocab, seed=0)
+            self.model = apply(model, bdir / ("mamba_tiny" if tiny else "mamba_370m"))
+            self.flops = mamba.prefill_flops(self.cfg, MAMBA_TOKENS)
+            self.units = MAMBA_TOKENS
+        else:
+            from metal_autotune_b200.targets import tiny_mlp
+            self.cfg = tiny_mlp.TINY_MLP
+            model, self.x = tiny_mlp.build(self.cfg)
+            self.model = apply(model, bdir / "tiny_mlp")
+            self.flops = tiny_mlp.flops(self.cfg)
+            self.units = 1
+        self.raw = model
+        self.host_x = self.x.cpu().pin_memory()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.model(self.x)
+            self.model(self.x)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        before = lib.CALLS[0]
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            out = self.model(self.x)
+        self.launches_per_step = lib.CALLS[0] - before
+        self.out = out[0] if isinstance(out, tuple) else out  # the pick for Mamba, the activations otherwise
+        self.host_out = torch.empty_like(self.out, device="cpu").pin_memory()
+
+    def replay(self):
+        self.graph.replay()
+
+    def e2e_step(self):
+        self.x.copy_(self.host_x, non_blocking=True)
+        self.graph.replay()
+        self.host_out.copy_(self.out, non_blocking=True)
+
+
+def model_cpu_baseline(step, threads):
+    """The oracle on a bounded sample of the same workload, on all host threads."""
+    import numpy as np
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    from oracle import ref as R
+    R.lib()
+    if step.kind == "whisper":
+        from oracle import whisper_ref
+        cfg = step.cfg
+        W = whisper_ref.encoder_weights(step.raw, n_blocks=1)
+        mel = step.x[:1].float().cpu().numpy()
+        t0 = time.perf_counter()
+        x = whisper_ref.stem(cfg, W, mel)
+        t_stem = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        whisper_ref.block(cfg, W.blocks[0], x)
+        t_block = time.perf_counter() - t0
+        secs = WHISPER_BATCH * (t_stem + cfg.n_layer * t_block)
+        sample = (f"the stem ({t_stem:.2f} s) and one block ({t_block:.2f} s) of one clip on the oracle C "
+                  f"restatement, OpenMP {threads} threads, scaled to {WHISPER_BATCH} clips x {cfg.n_layer} blocks")
+        return {"value": round(step.units / secs, 3), "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": sample}
+    if step.kind == "mamba":
+        from oracle import mamba_ref
+        W = mamba_ref.model_weights(step.raw)
+        t0 = time.perf_counter()
+        mamba_ref.prefill(step.cfg, W, step.x.cpu().numpy())
+        secs = time.perf_counter() - t0
+        return {"value": round(MAMBA_TOKENS / secs, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                "sample": f"the whole prefill ({step.cfg.n_layer} layers, {MAMBA_TOKENS} tokens, lm_head) on the "
+                          f"oracle C restatement, OpenMP {threads} threads: {secs:.2f} s"}
+    m = step.raw
+    xs = step.x.cpu().numpy()
+    w1, b1 = m.l1.weight.cpu().numpy(), m.l1.bias.cpu().numpy()
+    w2, b2 = m.l2.weight.cpu().numpy(), m.l2.bias.cpu().numpy()
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 2.0:
+        R.gelu_mlp(xs, w1, b1, w2, b2)
+        n += 1
+    us = (time.perf_counter() - t0) / n * 1e6
+    return {"value": round(us, 2), "unit": "us", "cores": threads, "kind": "port",
+            "sample": f"{n} forwards of the oracle C restatement (OpenMP {threads} threads) in 2 s"}
+
+
+MODEL_LINES = {
+    "whisper_turbo": ("whisper", "Whisper-large-v3-turbo encoder mel frames/s (batch 8 x 3000 frames)", "frames/s",
+                      True),
+    "whisper_tiny": ("whisper", "Whisper encoder (tiny) mel frames/s", "frames/s", True),
+    "mamba_370m": ("mamba", "Mamba-370m prefill tok/s (512 tokens)", "tok/s", True),
+    "mamba_tiny": ("mamba", "Mamba (tiny) prefill tok/s", "tok/s", True),
+    "tiny_mlp": ("mlp", "tiny GELU-MLP forward latency (x [32,256] fp32, 256->1024->256)", "us", False),
+}
+
+
+def run_model_line(args):
+    """One bench line for the Whisper encoder, Mamba-370m or the tiny MLP:
+    value = the target's units per second (or the forward's latency for the
+    tiny MLP), CUDA events around K graph replays; e2e the same with the
+    input copied from pinned host memory and the output read back; roofline
+    the whole forward's algorithmic FLOPs against the measured bf16/fp16
+    tensor peak."""
+    import torch
+
+    from metal_autotune_b200 import build, lib
+    kind, metric, unit, higher = MODEL_LINES[args.config]
+    build.build_library()
+    rank, world, local = dist_setup()
+    tiny = args.config.endswith("_tiny")
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        step = ModelStep(kind, tiny)
+        cb = model_cpu_baseline(step, os.cpu_count() or 1)
+        v = cb["value"]
+        ms = (1e3 / (v / step.units)) if higher else v / 1e3
+        print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": args.gpus,
+                          "steps": 1, "warmup": 0, "ms_per_step": round(ms, 4), "higher_is_better": higher,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f32" if kind == "mlp" else "f16",
+                          "data": "synthetic", "config": {"workload": args.config}, "cpu_baseline": cb,
+                          "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return 0
+    step = ModelStep(kind, tiny)
+    for _ in range(args.warmup):
+        step.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        soak(step.replay, 0.3)
+        clk.mark_start()
+        ms_total = time_region(step.replay, args.steps, world)
+        clk.mark_end()
+        ms_e2e_total = time_region(step.e2e_step, args.steps, world)
+        soak(step.replay, 0.3)
+    ms = max_over_ranks(ms_total / args.steps, world)
+    ms_e2e = max_over_ranks(ms_e2e_total / args.steps, world)
+    status = lib.device_status(clear=True)
+    if status != 0:
+        raise RuntimeError(f"device status {status:#x}: a kernel's bounded wait expired")
+    peaks = measured_peaks()
+    achieved = step.flops / (ms / 1e3) / 1e12
+    val = (lambda t: round(step.units * world / (t / 1e3), 2)) if higher else (lambda t: round(t * 1e3, 3))
+    line = {"metric": metric, "value": val(ms), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": higher, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32" if kind == "mlp" else "f16", "data": "synthetic",
+            "config": {"workload": args.config, "parallelism": f"replicas x{world}",
+                       "graph": "one CUDA graph per forward",
+                       "l2": "inputs larger than L2" if kind != "mlp" else "fits L2 (launch-bound, 1.3 MB)"},
+            "e2e": {"value": val(ms_e2e), "unit": unit, "h2d_bytes_per_step": step.host_x.numel()
+                    * step.host_x.element_size(), "d2h_bytes_per_step": step.host_out.numel()
+                    * step.host_out.element_size()},
+            "roofline": {"bound": "tensor" if kind != "mlp" else "launch", "achieved": round(achieved, 3),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16_tflops"], 5), "traffic": None,
+                         "what": "whole forward: algorithmic FLOPs / forward time vs the measured bf16 burst peak",
+                         "forward_gflop": round(step.flops / 1e9, 3)},
+            "clocks": clk.summary(), "gpu_launches": int(step.launches_per_step * args.steps * 2),
+            "launches_per_step": step.launches_per_step}
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = model_cpu_baseline(step, os.cpu_count() or 1)
+    barrier(world)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=None, help="default 300 (Qwen3 request), 5 (Llama forward)")
+    ap.add_argument("--steps", type=int, default=None,
+                    help="default 300 (Qwen3 request), 5 (Llama forward), 20 (the other targets)")
     ap.add_argument("--warmup", type=int, default=None, help="default 10 (Qwen3 request), 3 (Llama forward)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3_4b", choices=["qwen3_4b", "qwen3_tiny", "llama3_8b_tp", "llama_tiny_tp"],
-                    help="llama*_tp: Llama-3-8B 8-bit prefill 8 x 2048, tensor-parallel over the ranks")
+    ap.add_argument("--config", default="qwen3_4b",
+                    choices=["qwen3_4b", "qwen3_tiny", "llama3_8b_tp", "llama_tiny_tp", *MODEL_LINES],
+                    help="llama*_tp: Llama-3-8B 8-bit prefill 8 x 2048, tensor-parallel over the ranks; "
+                         "whisper_turbo / mamba_370m / tiny_mlp: the other targets' own lines")
     ap.add_argument("--mode", default="request", choices=["request", "kernels"])
     ap.add_argument("--only", default="", help="kernels mode: comma-separated kernel names")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -736,12 +935,14 @@ def main():
     args = ap.parse_args()
     llama = args.config.startswith("llama")
     if args.steps is None:
-        args.steps = 5 if llama else 300
+        args.steps = 5 if llama else 20 if args.config in MODEL_LINES else 300
     if args.warmup is None:
         args.warmup = 3 if llama else 10
     if args.warmup < 3 and args.mode == "request":
         args.warmup = 3
 
+    if args.config in MODEL_LINES:
+        return run_model_line(args)
     if args.config.startswith("llama"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the Llama TP line has no CPU arm; the default "

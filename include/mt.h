@@ -292,6 +292,20 @@ int mt_qk_norm_rope_sdpa_decode(const void* q, const void* k, const void* v,
 int mt_swiglu(const void* gate, const void* up, void* y, int64_t n, int dtype,
               mt_stream_t stream);
 
+/* y[i] = round(x[i] + r[i mod period]) in dtype (bf16 / f16 / f32): the `+`
+ * of a residual branch, or the mlx-whisper encoder's `x + positional_embedding`
+ * (models/whisper_large_v3_turbo_encoder.py:8-12) with the [n_ctx, n_state]
+ * table repeated over the batch (period = n_ctx * n_state). n must be a
+ * multiple of period; y may alias x. */
+int mt_add(const void* x, const void* r, void* y, int64_t n, int64_t period,
+           int dtype, mt_stream_t stream);
+
+/* nn.Embedding: out[t, :] = table[tokens[t], :] for a dense [vocab, D] table
+ * (mlx-lm mamba's embedding, models/mamba_370m.py:4-8). An id outside
+ * [0, vocab) writes zeros and is reported through the device status. */
+int mt_embedding(const int32_t* tokens, const void* table, void* out, int64_t T,
+                 int64_t vocab, int64_t D, int dtype, mt_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* a-6: causal GQA scaled-dot-product attention                              */
 /* ------------------------------------------------------------------------ */

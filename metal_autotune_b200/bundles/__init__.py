@@ -174,6 +174,192 @@ LAYER_KERNELS = ["rms_norm", "qkv_qmm", "qk_norm_rope_cache", "sdpa_causal_gqa",
 ROOT_KERNELS = ["quantized_embedding", "rms_norm", "lm_head", "logits_pick", "rms_norm_lm_head"]
 
 
+def whisper_specs(eps: float = 1e-5) -> list[KernelSpec]:
+    """Shape-generic specs of the mlx-whisper encoder regions (fp16 or bf16,
+    activations [batch, positions, features])."""
+    rows = "in0.shape[0] * in0.shape[1]"
+    S = []
+    for kid, stride in (("conv1_gelu", 1), ("conv2_gelu", 2)):
+        S.append(KernelSpec(
+            kernel_id=kid, name="mt_conv1d", input_names=("in0", "in1", "in2"), output_names=("out0",),
+            cuda={"symbol": "mt_conv1d", "args": [
+                {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in0.shape[1]"},
+                {"expr": "in0.shape[2]"}, {"expr": "in1.shape[0]"}, {"expr": "in1.shape[1]"}, {"int": stride},
+                {"int": 1}, {"int": 1}, {"dtype": "in0"}, {"stream": True}]},
+            output_shapes=(("in0.shape[0]", f"(in0.shape[1] + 2 - in1.shape[1]) // {stride} + 1", "in1.shape[0]"),),
+            output_dtypes=("in0",), fallback_predicate="in0.shape[2] % 32 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="pos_add", name="mt_add", input_names=("in0", "in1"), output_names=("out0",),
+        cuda={"symbol": "mt_add", "args": [
+            {"in": 0}, {"in": 1}, {"out": 0}, {"expr": "in0.shape[0] * in0.shape[1] * in0.shape[2]"},
+            {"expr": "in1.shape[0] * in1.shape[1]"}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]", "in0.shape[2]"),), output_dtypes=("in0",),
+        fallback_predicate="in1.shape[0] != in0.shape[1] or in1.shape[1] != in0.shape[2]"))
+    S.append(KernelSpec(
+        kernel_id="layer_norm", name="mt_layer_norm", input_names=("in0", "in1", "in2"), output_names=("out0",),
+        cuda={"symbol": "mt_layer_norm", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"float": eps}, {"out": 0}, {"expr": rows}, {"expr": "in0.shape[2]"},
+            {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]", "in0.shape[2]"),), output_dtypes=("in0",),
+        reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="qkv_linear", name="mt_linear", input_names=("in0", "in1", "in2"), output_names=("out0",),
+        cuda={"symbol": "mt_linear", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"expr": rows}, {"expr": "in1.shape[0]"},
+            {"expr": "in0.shape[2]"}, {"int": 0}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]", "in1.shape[0]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[2] % 8 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="self_attention", name="mt_sdpa", input_names=("in0", "in1", "in2"), output_names=("out0",),
+        cuda={"symbol": "mt_sdpa", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in0.shape[2]"},
+            {"expr": "in1.shape[2]"}, {"expr": "in0.shape[1]"}, {"expr": "in1.shape[1]"}, {"expr": "in0.shape[3]"},
+            {"float": 0.125}, {"int": 0}, {"int": 0},
+            {"stride": [0, 0]}, {"stride": [0, 2]}, {"stride": [0, 1]},
+            {"stride": [1, 0]}, {"stride": [1, 2]}, {"stride": [1, 1]},
+            {"stride": [2, 0]}, {"stride": [2, 2]}, {"stride": [2, 1]},
+            {"expr": "in0.shape[1] * in0.shape[2] * in0.shape[3]"}, {"expr": "in0.shape[3]"},
+            {"expr": "in0.shape[2] * in0.shape[3]"}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]", "in0.shape[2] * in0.shape[3]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[3] != 64", ensure_row_contiguous=False, reassociates=True))
+    for kid in ("out_proj_residual", "fc2_residual"):
+        S.append(KernelSpec(
+            kernel_id=kid, name="mt_linear_residual", input_names=("in0", "in1", "in2", "in3"),
+            output_names=("out0",),
+            cuda={"symbol": "mt_linear_residual", "args": [
+                {"in": 0}, {"in": 1}, {"in": 2}, {"in": 3}, {"out": 0}, {"expr": rows}, {"expr": "in1.shape[0]"},
+                {"expr": "in0.shape[2]"}, {"dtype": "in0"}, {"stream": True}]},
+            output_shapes=(("in0.shape[0]", "in0.shape[1]", "in1.shape[0]"),), output_dtypes=("in0",),
+            fallback_predicate="in0.shape[2] % 8 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="fc1_gelu", name="mt_linear", input_names=("in0", "in1", "in2"), output_names=("out0",),
+        cuda={"symbol": "mt_linear", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"expr": rows}, {"expr": "in1.shape[0]"},
+            {"expr": "in0.shape[2]"}, {"int": 1}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]", "in1.shape[0]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[2] % 8 != 0", reassociates=True))
+    return S
+
+
+def mamba_specs(eps: float = 1e-5) -> list[KernelSpec]:
+    """Shape-generic specs of the mlx-lm mamba regions (activations [tokens, features])."""
+    S = []
+    S.append(KernelSpec(
+        kernel_id="rms_norm", name="mt_rms_norm", input_names=("in0", "in1"), output_names=("out0",),
+        cuda={"symbol": "mt_rms_norm", "args": [
+            {"in": 0}, {"in": 1}, {"float": eps}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in0.shape[1]"},
+            {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]"),), output_dtypes=("in0",), reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="linear", name="mt_linear", input_names=("in0", "in1"), output_names=("out0",),
+        cuda={"symbol": "mt_linear", "args": [
+            {"in": 0}, {"in": 1}, {"null": True}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in1.shape[0]"},
+            {"expr": "in0.shape[1]"}, {"int": 0}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[1] % 8 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="linear_bias", name="mt_linear", input_names=("in0", "in1", "in2"), output_names=("out0",),
+        cuda={"symbol": "mt_linear", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in1.shape[0]"},
+            {"expr": "in0.shape[1]"}, {"int": 0}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[1] % 8 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="causal_conv1d_silu", name="mt_causal_conv1d", input_names=("in0", "in1", "in2"),
+        output_names=("out0",),
+        cuda={"symbol": "mt_causal_conv1d", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"null": True}, {"out": 0}, {"expr": "in0.shape[0]"},
+            {"expr": "in0.shape[1]"}, {"expr": "in1.shape[1]"}, {"int": 1}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]"),), output_dtypes=("in0",)))
+    S.append(KernelSpec(
+        kernel_id="selective_scan", name="mt_mamba_scan", input_names=tuple(f"in{i}" for i in range(7)),
+        output_names=("out0",),
+        cuda={"symbol": "mt_mamba_scan", "args": [
+            {"in": 0}, {"in": 1}, {"null": True}, {"in": 2}, {"in": 3}, {"in": 4}, {"in": 5}, {"in": 6}, {"out": 0},
+            {"null": True}, {"expr": "in0.shape[0]"}, {"expr": "in0.shape[1]"}, {"expr": "in2.shape[1]"},
+            {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]"),), output_dtypes=("in0",), reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="out_proj_residual", name="mt_linear_residual", input_names=("in0", "in1", "in2"),
+        output_names=("out0",),
+        cuda={"symbol": "mt_linear_residual", "args": [
+            {"in": 0}, {"in": 1}, {"null": True}, {"in": 2}, {"out": 0}, {"expr": "in0.shape[0]"},
+            {"expr": "in1.shape[0]"}, {"expr": "in0.shape[1]"}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",),
+        fallback_predicate="in0.shape[1] % 8 != 0", reassociates=True))
+    S.append(KernelSpec(
+        kernel_id="embedding", name="mt_embedding", input_names=("in0", "in1"), output_names=("out0",),
+        cuda={"symbol": "mt_embedding", "args": [
+            {"in": 0}, {"in": 1}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in1.shape[0]"},
+            {"expr": "in1.shape[1]"}, {"dtype": "in1"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in1.shape[1]"),), output_dtypes=("in1",)))
+    S.append(KernelSpec(
+        kernel_id="logits_pick", name="mt_logits_pick", input_names=("in0",),
+        output_names=("out0", "out1", "out2"),
+        cuda={"symbol": "mt_logits_pick", "args": [
+            {"in": 0}, {"expr": "in0.shape[0] * in0.shape[1]"}, {"dtype": "in0"}, {"out": 0}, {"out": 1},
+            {"out": 2}, {"stream": True}]},
+        output_shapes=(("1",), ("1",), ("1",)), output_dtypes=("int32", "float32", "float32"),
+        fallback_predicate="in0.shape[0] != 1"))
+    return S
+
+
+MAMBA_LAYER_KERNELS = ["rms_norm", "linear", "linear_bias", "causal_conv1d_silu", "selective_scan",
+                       "out_proj_residual"]
+MAMBA_ROOT_KERNELS = ["embedding", "rms_norm", "linear", "logits_pick"]
+
+
+def write_mamba_bundle(directory: str | Path, n_layers: int) -> Path:
+    table = [{"scope_path": f"layers.{i}", "wrapper_class": "W_mamba_layer", "kernel_ids": MAMBA_LAYER_KERNELS}
+             for i in range(n_layers)]
+    table.append({"scope_path": "", "wrapper_class": "W_mamba_model", "kernel_ids": MAMBA_ROOT_KERNELS})
+    return _write_bundle(Path(directory), mamba_specs(), table, HERE / "mamba_wrappers.py",
+                         {"target": "mamba", "layers": n_layers})
+
+
+def tiny_mlp_specs() -> list[KernelSpec]:
+    """The two fp32 linears of the tiny GELU-MLP (mt_linear, act 1 / 0)."""
+    S = []
+    for kid, act in (("linear_gelu_f32", 1), ("linear_f32", 0)):
+        S.append(KernelSpec(
+            kernel_id=kid, name="mt_linear", input_names=("in0", "in1", "in2"), output_names=("out0",),
+            cuda={"symbol": "mt_linear", "args": [
+                {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"expr": "in0.shape[0]"}, {"expr": "in1.shape[0]"},
+                {"expr": "in0.shape[1]"}, {"int": act}, {"dtype": "in0"}, {"stream": True}]},
+            output_shapes=(("in0.shape[0]", "in1.shape[0]"),), output_dtypes=("in0",)))
+    return S
+
+
+def write_tiny_mlp_bundle(directory: str | Path) -> Path:
+    table = [{"scope_path": "", "wrapper_class": "W_tiny_mlp", "kernel_ids": ["linear_gelu_f32", "linear_f32"]}]
+    return _write_bundle(Path(directory), tiny_mlp_specs(), table, HERE / "tiny_mlp_wrappers.py",
+                         {"target": "tiny_mlp", "layers": 2})
+
+
+WHISPER_BLOCK_KERNELS = ["layer_norm", "qkv_linear", "self_attention", "out_proj_residual", "fc1_gelu",
+                         "fc2_residual"]
+WHISPER_ROOT_KERNELS = ["conv1_gelu", "conv2_gelu", "pos_add", "layer_norm"]
+
+
+def _write_bundle(d: Path, specs, table, wrappers: Path, meta: dict) -> Path:
+    (d / "kernels").mkdir(parents=True, exist_ok=True)
+    (d / "patch").mkdir(exist_ok=True)
+    for spec in specs:
+        write_spec(d / "kernels", spec)
+    (d / "swap_table.json").write_text(json.dumps(table, indent=1) + "\n")
+    shutil.copyfile(wrappers, d / "patch" / "wrappers.py")
+    (d / "bundle.json").write_text(json.dumps(meta, indent=1) + "\n")
+    return d
+
+
+def write_whisper_bundle(directory: str | Path, n_layers: int) -> Path:
+    table = [{"scope_path": f"blocks.{i}", "wrapper_class": "W_whisper_block", "kernel_ids": WHISPER_BLOCK_KERNELS}
+             for i in range(n_layers)]
+    table.append({"scope_path": "", "wrapper_class": "W_whisper_encoder", "kernel_ids": WHISPER_ROOT_KERNELS})
+    return _write_bundle(Path(directory), whisper_specs(), table, HERE / "whisper_wrappers.py",
+                         {"target": "whisper_encoder", "layers": n_layers})
+
+
 def write_qwen3_bundle(directory: str | Path, n_layers: int) -> Path:
     d = Path(directory)
     (d / "kernels").mkdir(parents=True, exist_ok=True)
@@ -189,9 +375,20 @@ def write_qwen3_bundle(directory: str | Path, n_layers: int) -> Path:
     return d
 
 
+BUNDLES = {
+    "qwen3_4b": lambda d: write_qwen3_bundle(d, 36),
+    "qwen3_tiny": lambda d: write_qwen3_bundle(d, 2),
+    "whisper_turbo": lambda d: write_whisper_bundle(d, 32),
+    "whisper_tiny": lambda d: write_whisper_bundle(d, 2),
+    "mamba_370m": lambda d: write_mamba_bundle(d, 48),
+    "mamba_tiny": lambda d: write_mamba_bundle(d, 2),
+    "tiny_mlp": write_tiny_mlp_bundle,
+}
+
+
 def main() -> None:
-    write_qwen3_bundle(HERE / "qwen3_4b", 36)
-    write_qwen3_bundle(HERE / "qwen3_tiny", 2)
+    for name, write in BUNDLES.items():
+        write(HERE / name)
 
 
 if __name__ == "__main__":

@@ -1,5 +1,6 @@
-// Elementwise and gather regions: SwiGLU, the quantized embedding gather and
-// the greedy pick from the last row of logits.
+// Elementwise and gather regions: SwiGLU, the residual / positional add, the
+// dense and the quantized embedding gathers and the greedy pick from the
+// last row of logits.
 #include <cooperative_groups.h>
 
 #include "mt_common.cuh"
@@ -40,6 +41,66 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const void* __restrict__ gp
   }
   for (int64_t i = tid; i < n; i += stride)
     y[i] = Elem<DT>::from_f(swiglu_rounded<DT>(Elem<DT>::to_f(g[i]), Elem<DT>::to_f(u[i])));
+}
+
+// y[i] = round(x[i] + r[i mod period]): a residual or positional add with the
+// second operand repeated every `period` elements (period = n: plain add).
+template <int DT>
+__global__ void __launch_bounds__(256) add_kernel(const void* __restrict__ xp, const void* __restrict__ rp,
+                                                  void* __restrict__ yp, int64_t n, int64_t period) {
+  using T = typename Elem<DT>::T;
+  griddep_wait();
+  griddep_launch();
+  const T* x = static_cast<const T*>(xp);
+  const T* r = static_cast<const T*>(rp);
+  T* y = static_cast<T*>(yp);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(r) | reinterpret_cast<uintptr_t>(y)) &
+                    15) == 0 && period % V == 0;
+  if (vec) {
+    const int64_t nv = n / V;
+    for (int64_t v = tid; v < nv; v += stride) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(x + v * V);
+      const uint4 rv = *reinterpret_cast<const uint4*>(r + (v * V) % period);
+      uint4 yv;
+      const T* xe = reinterpret_cast<const T*>(&xv);
+      const T* re = reinterpret_cast<const T*>(&rv);
+      T* ye = reinterpret_cast<T*>(&yv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) ye[e] = Elem<DT>::from_f(Elem<DT>::to_f(xe[e]) + Elem<DT>::to_f(re[e]));
+      *reinterpret_cast<uint4*>(y + v * V) = yv;
+    }
+    for (int64_t i = nv * V + tid; i < n; i += stride)
+      y[i] = Elem<DT>::from_f(Elem<DT>::to_f(x[i]) + Elem<DT>::to_f(r[i % period]));
+    return;
+  }
+  for (int64_t i = tid; i < n; i += stride)
+    y[i] = Elem<DT>::from_f(Elem<DT>::to_f(x[i]) + Elem<DT>::to_f(r[i % period]));
+}
+
+// out[t, :] = table[tok[t], :] (a dense embedding gather, 16-byte copies);
+// an id outside [0, vocab) writes zeros and records the device status.
+__global__ void __launch_bounds__(128) embed_kernel(const int32_t* __restrict__ tokens, const uint8_t* __restrict__ table,
+                                                    uint8_t* __restrict__ out, int64_t vocab, int64_t row_bytes) {
+  griddep_wait();
+  griddep_launch();
+  const int t = blockIdx.x;
+  const int tok = tokens[t];
+  uint8_t* dst = out + static_cast<int64_t>(t) * row_bytes;
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) report_status(0x501);
+    for (int64_t i = threadIdx.x; i < row_bytes; i += blockDim.x) dst[i] = 0;
+    return;
+  }
+  const uint8_t* src = table + static_cast<int64_t>(tok) * row_bytes;
+  if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    for (int64_t i = threadIdx.x; i < row_bytes / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  } else {
+    for (int64_t i = threadIdx.x; i < row_bytes; i += blockDim.x) dst[i] = src[i];
+  }
 }
 
 // out[t, k] = round(round(s*q) + b) for token tok[t]; one CTA per token.
@@ -223,6 +284,42 @@ int mt_swiglu(const void* gate, const void* up, void* y, int64_t n, int dtype, m
     case MT_F32: return launch(swiglu_kernel<MT_F32>, grid, dim3(256), 0, (cudaStream_t)stream, gate, up, y, n);
     default: set_error("mt_swiglu: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
   }
+}
+
+int mt_add(const void* x, const void* r, void* y, int64_t n, int64_t period, int dtype, mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(x && r && y, "mt_add: null pointer");
+  MT_CHECK_ARG(n >= 0 && period > 0 && (n == 0 || n % period == 0), "mt_add: n=%lld must be a multiple of period=%lld",
+               (long long)n, (long long)period);
+  if (n == 0) return MT_OK;
+  int sms = 148;
+  int rc = device_sm_count(&sms);
+  if (rc) return rc;
+  const int64_t want = (n + 255) / 256;
+  const dim3 grid(static_cast<unsigned>(want < sms * 16 ? want : sms * 16));
+  switch (dtype) {
+    case MT_BF16: return launch(add_kernel<MT_BF16>, grid, dim3(256), 0, (cudaStream_t)stream, x, r, y, n, period);
+    case MT_F16: return launch(add_kernel<MT_F16>, grid, dim3(256), 0, (cudaStream_t)stream, x, r, y, n, period);
+    case MT_F32: return launch(add_kernel<MT_F32>, grid, dim3(256), 0, (cudaStream_t)stream, x, r, y, n, period);
+    default: set_error("mt_add: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
+  }
+}
+
+int mt_embedding(const int32_t* tokens, const void* table, void* out, int64_t T, int64_t vocab, int64_t D, int dtype,
+                 mt_stream_t stream) {
+  clear_error();
+  MT_CHECK_ARG(tokens && table && out, "mt_embedding: null pointer");
+  MT_CHECK_ARG(T >= 0 && T < (1 << 30) && vocab > 0 && D > 0, "mt_embedding: bad shape");
+  int esz = 0;
+  switch (dtype) {
+    case MT_BF16:
+    case MT_F16: esz = 2; break;
+    case MT_F32: esz = 4; break;
+    default: set_error("mt_embedding: unsupported dtype %d", dtype); return MT_ERR_UNSUPPORTED;
+  }
+  if (T == 0) return MT_OK;
+  return launch(embed_kernel, dim3(static_cast<unsigned>(T)), dim3(128), 0, (cudaStream_t)stream, tokens,
+                static_cast<const uint8_t*>(table), static_cast<uint8_t*>(out), vocab, D * esz);
 }
 
 int mt_quantized_embedding(const int32_t* tokens, const uint32_t* w, const void* scales, const void* biases,

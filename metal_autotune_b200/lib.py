@@ -90,6 +90,8 @@ SIGNATURES = {
     "mt_diff_workspace_bytes": (C.c_size_t, [I64]),
     "mt_diff_reduce": (C.c_int, [P, P, I64, I32, F32, F32, F32, P, P, SZ, P]),
     "mt_diff_reduce_noalloc": (C.c_int, [P, P, I64, I32, F32, F32, F32, P, P]),
+    "mt_add": (C.c_int, [P, P, P, I64, I64, I32, P]),
+    "mt_embedding": (C.c_int, [P, P, P, I64, I64, I64, I32, P]),
     "mt_linear": (C.c_int, [P, P, P, P, I64, I64, I64, I32, I32, P]),
     "mt_linear_residual": (C.c_int, [P, P, P, P, P, I64, I64, I64, I32, P]),
     "mt_layer_norm": (C.c_int, [P, P, P, F32, P, I64, I64, I32, P]),
@@ -419,6 +421,26 @@ def sdpa(q, k, v, *, scale, causal, q_offset=0, out=None, out_layout="bhld"):
          int(q_offset), q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0),
          v.stride(1), v.stride(2), os_b, os_h, os_l, dtype_code(q.dtype), _stream())
     return out
+
+
+def add(x, r, *, out=None):
+    """round(x + r) with r repeated over x's leading elements (r.numel() divides x.numel())."""
+    _dense(x, "x")
+    _dense(r, "r")
+    y = out if out is not None else torch.empty_like(x)
+    call("mt_add", _ptr(x), _ptr(r), _ptr(y), x.numel(), r.numel(), dtype_code(x.dtype), _stream())
+    return y
+
+
+def embedding(tokens, table, *, out=None):
+    """table[tokens] for a dense [vocab, D] table."""
+    _dense(table, "table")
+    T = tokens.numel()
+    D = table.shape[1]
+    y = out if out is not None else torch.empty(*tokens.shape, D, dtype=table.dtype, device=table.device)
+    call("mt_embedding", _ptr(tokens), _ptr(table), _ptr(y), T, table.shape[0], D, dtype_code(table.dtype),
+         _stream())
+    return y
 
 
 def quantized_embedding(tokens, w, scales, biases, *, group_size=64, bits=4, dtype=None, out=None):

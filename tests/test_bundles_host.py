@@ -29,3 +29,10 @@ def test_bundle_wrappers_are_the_one_source():
     src = bundles.WRAPPERS.read_bytes()
     for name in ("qwen3_4b", "qwen3_tiny"):
         assert (bundles.HERE / name / "patch" / "wrappers.py").read_bytes() == src
+
+
+@pytest.mark.parametrize("name", sorted(bundles.BUNDLES))
+def test_every_committed_bundle_is_generated(tmp_path, name):
+    out = tmp_path / name
+    bundles.BUNDLES[name](out)
+    assert _files(out) == _files(bundles.HERE / name)
