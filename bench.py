@@ -583,7 +583,7 @@ def run_kernels(args, cfg):
 LLAMA_B, LLAMA_L = 8, 2048
 
 
-def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local):
+def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local, overlap=True):
     """Llama-3-8B 8-bit prefill forward (batch B x L), tensor-parallel over the
     `world` ranks (one shard per GPU, NCCL all-reduce after o_proj and down).
     Every rank takes the same collective steps; times are max over ranks.
@@ -602,7 +602,7 @@ def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local):
     from metal_autotune_b200.targets import llama_tp
     comm = llama_tp.ProcessGroupComm() if world > 1 else llama_tp.LocalComm()
     t0 = time.time()
-    model = llama_tp.LlamaTP(cfg, world, [rank], comm, seed=0, device="cuda")
+    model = llama_tp.LlamaTP(cfg, world, [rank], comm, seed=0, device="cuda", overlap=overlap)
     torch.cuda.synchronize()
     log(f"rank {rank}: built Llama shard {rank}/{world} ({cfg.layers} layers) in {time.time() - t0:.1f}s, "
         f"{torch.cuda.memory_allocated() / 2**30:.1f} GiB")
@@ -662,6 +662,7 @@ def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local):
     sustained = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
     achieved = fwd_flops / world / (ms / 1e3) / 1e12
     rec = {"tp": world, "nccl_ranks": world if world > 1 else 0, "ms_per_forward": round(ms, 4),
+           "allreduce_overlap": bool(overlap and world > 1),
            "steps": steps, "warmup": warmup, "tok_s": round(B * L / (ms / 1e3), 2),
            "e2e_tok_s": round(B * L / (ms_e2e / 1e3), 2),
            "e2e_bytes": {"h2d_per_step": B * L * 4, "d2h_per_step": B * cfg.vocab * 2},
@@ -693,7 +694,7 @@ def run_llama_tp(args):
     rank, world, local = dist_setup()
     cfg = llama_tp.LLAMA3_8B if args.config == "llama3_8b_tp" else llama_tp.TINY
     B, L = (LLAMA_B, LLAMA_L) if cfg.layers == 32 else (2, 128)
-    rec = llama_tp_record(cfg, B, L, args.steps, args.warmup, rank, world, local)
+    rec = llama_tp_record(cfg, B, L, args.steps, args.warmup, rank, world, local, overlap=not args.no_overlap)
     if rank == 0:
         line = {"metric": "Llama-3-8B-8bit prefill tok/s (batch 8 x 2048), tensor-parallel",
                 "value": rec["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -929,6 +930,8 @@ def main():
     ap.add_argument("--no-llama-tp", action="store_true",
                     help="skip the Llama-3-8B tensor-parallel record of the default line")
     ap.add_argument("--llama-steps", type=int, default=5, help="timed forwards of the Llama record")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="Llama TP: all-reduces between the blocks instead of overlapped with the other micro-batch")
     ap.add_argument("--launch-list", action="store_true",
                     help="replay the request W + K times, the K inside an NVTX range 'request', and exit "
                          "(for ncu --nvtx --nvtx-include request/)")
@@ -1020,7 +1023,7 @@ def main():
         del req
         torch.cuda.empty_cache()
         line["llama_tp"] = llama_tp_record(llama_tp.LLAMA3_8B, LLAMA_B, LLAMA_L, args.llama_steps, 3, rank, world,
-                                           local)
+                                           local, overlap=not args.no_overlap)
     barrier(world)
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -27,7 +27,10 @@ outputs at any tp agree up to the order of the partial sums.
 
 Shards run either one per process (`ProcessGroupComm`, NCCL on the GPU box)
 or all in one process (`LocalComm`, the sum taken in shard order), which
-lets one GPU check tp > 1 against tp = 1.
+lets one GPU check tp > 1 against tp = 1. With one shard per process the
+forward runs as two software-pipelined micro-batches, each micro-batch's
+all-reduce overlapping the other's next block of compute
+(`_forward_overlapped`; `overlap=False` gives the serial forward).
 """
 from __future__ import annotations
 
@@ -112,6 +115,11 @@ class ProcessGroupComm:
         self.dist.all_reduce(p)
         return p
 
+    def all_reduce_async(self, p):
+        """Start an in-place sum of p over the ranks; returns the handle whose
+        wait() makes the current stream wait for the sum (the host does not block)."""
+        return self.dist.all_reduce(p, async_op=True)
+
     def all_gather(self, parts):
         (p,) = parts
         outs = [torch.empty_like(p) for _ in range(self.world)]
@@ -144,8 +152,9 @@ class LlamaTP:
     is split by vocab rows."""
 
     def __init__(self, cfg: LlamaConfig, tp: int, ranks, comm, seed: int = 0, device="cuda",
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, overlap: bool = True):
         self.cfg, self.tp, self.ranks, self.comm = cfg, tp, list(ranks), comm
+        self.overlap = overlap
         self.dtype, self.device = dtype, device
         if cfg.heads % tp or cfg.kv_heads % tp:
             raise ValueError(f"{cfg.heads}/{cfg.kv_heads} heads do not split over tp={tp}")
@@ -199,6 +208,8 @@ class LlamaTP:
         """tokens int32 [B, L] -> logits [B, vocab] of each sequence's last position."""
         cfg = self.cfg
         B, L = tokens.shape
+        if self.overlap and hasattr(self.comm, "all_reduce_async") and len(self.shards) == 1 and B >= 2 and B % 2 == 0:
+            return self._forward_overlapped(tokens)
         h = lib.quantized_embedding(tokens.reshape(-1), *self.embed, group_size=cfg.group, bits=cfg.bits,
                                     dtype=self.dtype)
         xn = lib.rms_norm(h, self.attn_norm[0], cfg.eps)
@@ -211,6 +222,49 @@ class LlamaTP:
         last = xn.view(B, L, cfg.hidden)[:, -1].contiguous()
         parts = [lib.quantized_matmul(last, *s.lm_head, group_size=cfg.group, bits=cfg.bits) for s in self.shards]
         return self.comm.all_gather(parts)
+
+    def _forward_overlapped(self, tokens: torch.Tensor) -> torch.Tensor:
+        """The same forward in two micro-batches (the first and the second half
+        of the sequences; attention never mixes sequences), software-pipelined
+        on one compute stream: each micro-batch's all-reduce is started
+        asynchronously (NCCL, its own stream) and waited for only after the
+        other micro-batch's next attention or MLP block has been issued, so
+        every all-reduce runs beside a block of compute. The sums are the same
+        per micro-batch; only the partition of the projections' launches
+        changes (reordered fp32 partial sums, within the tolerance of the
+        unsplit forward)."""
+        cfg = self.cfg
+        B, L = tokens.shape
+        sh = self.shards[0]
+        comm = self.comm
+        h = lib.quantized_embedding(tokens.reshape(-1), *self.embed, group_size=cfg.group, bits=cfg.bits,
+                                    dtype=self.dtype)
+        xn = lib.rms_norm(h, self.attn_norm[0], cfg.eps)
+        half = (B // 2) * L
+        hs, xns = [h[:half], h[half:]], [xn[:half], xn[half:]]
+        pend: list = [None, None]
+        for li in range(cfg.layers):
+            sl = sh.layers[li]
+            for m in (0, 1):
+                if pend[m] is not None:
+                    work, d = pend[m]
+                    work.wait()
+                    hs[m], xns[m] = lib.add_rms_norm(d, hs[m], self.attn_norm[li], cfg.eps)
+                o = self._attn(sl, xns[m], B // 2, L)
+                pend[m] = (comm.all_reduce_async(o), o)
+            for m in (0, 1):
+                work, o = pend[m]
+                work.wait()
+                hs[m], xns[m] = lib.add_rms_norm(o, hs[m], self.mlp_norm[li], cfg.eps)
+                d = self._mlp(sl, xns[m])
+                pend[m] = (comm.all_reduce_async(d), d)
+        for m in (0, 1):
+            work, d = pend[m]
+            work.wait()
+            hs[m], xns[m] = lib.add_rms_norm(d, hs[m], self.final_norm, cfg.eps)
+        last = torch.cat([x.view(B // 2, L, cfg.hidden)[:, -1] for x in xns]).contiguous()
+        part = lib.quantized_matmul(last, *sh.lm_head, group_size=cfg.group, bits=cfg.bits)
+        return comm.all_gather([part])
 
     __call__ = forward
 

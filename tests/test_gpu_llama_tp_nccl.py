@@ -26,13 +26,16 @@ def _rank(rank, init_file, q):
         cfg = llama_tp.LlamaConfig(hidden=512, layers=2, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024)
         tok = workload.seeded_tokens((2, 192), 0, cfg.vocab, seed=3, device=f"cuda:{rank}")
         m = llama_tp.LlamaTP(cfg, 2, [rank], llama_tp.ProcessGroupComm(), seed=5, device=f"cuda:{rank}")
-        got = m(tok)
+        got = m(tok)                      # two micro-batches, all-reduces overlapped with compute
+        m.overlap = False
+        serial = m(tok)                   # one batch, all-reduces between the blocks
         torch.cuda.synchronize()
         ok = lib.device_status(clear=True) == 0 and tuple(got.shape) == (2, cfg.vocab)
         if rank == 0:
             ref = llama_tp.LlamaTP(cfg, 1, [0], llama_tp.LocalComm(), seed=5, device="cuda:0")(tok)
-            rel = ((got.float() - ref.float()).norm() / ref.float().norm()).item()
-            ok = ok and rel < 1e-2
+            for out in (got, serial):
+                rel = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
+                ok = ok and rel < 1e-2
         dist.barrier()
         q.put((rank, bool(ok)))
     finally:
