@@ -313,8 +313,13 @@ def write_mamba_bundle(directory: str | Path, n_layers: int) -> Path:
     table = [{"scope_path": f"layers.{i}", "wrapper_class": "W_mamba_layer", "kernel_ids": MAMBA_LAYER_KERNELS}
              for i in range(n_layers)]
     table.append({"scope_path": "", "wrapper_class": "W_mamba_model", "kernel_ids": MAMBA_ROOT_KERNELS})
-    return _write_bundle(Path(directory), mamba_specs(), table, HERE / "mamba_wrappers.py",
-                         {"target": "mamba", "layers": n_layers})
+    full = n_layers == 48
+    meta = {"target": "mamba", "layers": n_layers, **artifact_meta(
+        "metal_autotune_b200.targets.mamba:build", "MAMBA_370M" if full else "TINY", 0, "mamba_prefill",
+        {"prompt": {"seeded": {"kind": "randint", "shape": [512 if full else 64], "dtype": "int32", "seed": 0,
+                               "high": 50280 if full else 1000}}},
+        {"rtol": 2e-2, "atol": 2e-2}, steps=2 if full else 5)}
+    return _write_bundle(Path(directory), mamba_specs(), table, HERE / "mamba_wrappers.py", meta)
 
 
 def tiny_mlp_specs() -> list[KernelSpec]:
@@ -332,13 +337,31 @@ def tiny_mlp_specs() -> list[KernelSpec]:
 
 def write_tiny_mlp_bundle(directory: str | Path) -> Path:
     table = [{"scope_path": "", "wrapper_class": "W_tiny_mlp", "kernel_ids": ["linear_gelu_f32", "linear_f32"]}]
-    return _write_bundle(Path(directory), tiny_mlp_specs(), table, HERE / "tiny_mlp_wrappers.py",
-                         {"target": "tiny_mlp", "layers": 2})
+    d = Path(directory)
+    (d / "workloads").mkdir(parents=True, exist_ok=True)
+    from safetensors.torch import save_file
+
+    from ..targets import tiny_mlp
+    _, x = tiny_mlp.build(tiny_mlp.TINY_MLP, device="cpu")  # the BASELINE input (seed 0, after the weights)
+    save_file({"i0": x.contiguous()}, str(d / "workloads" / "x.safetensors"))
+    meta = {"target": "tiny_mlp", "layers": 2, **artifact_meta(
+        "metal_autotune_b200.targets.tiny_mlp:build", "TINY_MLP", None, "tiny_mlp",
+        {"x": {"file": "workloads/x.safetensors"}}, {"rtol": 1e-4, "atol": 1e-4}, steps=20)}
+    return _write_bundle(d, tiny_mlp_specs(), table, HERE / "tiny_mlp_wrappers.py", meta)
 
 
 WHISPER_BLOCK_KERNELS = ["layer_norm", "qkv_linear", "self_attention", "out_proj_residual", "fc1_gelu",
                          "fc2_residual"]
 WHISPER_ROOT_KERNELS = ["conv1_gelu", "conv2_gelu", "pos_add", "layer_norm"]
+
+
+def artifact_meta(builder: str, config: str | None, seed: int | None, entry: str, workloads: dict,
+                  tolerances: dict | None, steps: int = 5) -> dict:
+    """The bundle.json fields bundles/artifact.py reads to rebuild, check and
+    time the target in a fresh process."""
+    return {"builder": builder, "config": config, "seed": seed, "entry": entry, "workloads": workloads,
+            "correctness_rule": "baseline_tolerance", "tolerances": tolerances,
+            "final_benchmark": {"pairs": 4, "warmup_steps": 3, "steps": steps}}
 
 
 def _write_bundle(d: Path, specs, table, wrappers: Path, meta: dict) -> Path:
@@ -356,8 +379,13 @@ def write_whisper_bundle(directory: str | Path, n_layers: int) -> Path:
     table = [{"scope_path": f"blocks.{i}", "wrapper_class": "W_whisper_block", "kernel_ids": WHISPER_BLOCK_KERNELS}
              for i in range(n_layers)]
     table.append({"scope_path": "", "wrapper_class": "W_whisper_encoder", "kernel_ids": WHISPER_ROOT_KERNELS})
-    return _write_bundle(Path(directory), whisper_specs(), table, HERE / "whisper_wrappers.py",
-                         {"target": "whisper_encoder", "layers": n_layers})
+    full = n_layers == 32
+    meta = {"target": "whisper_encoder", "layers": n_layers, **artifact_meta(
+        "metal_autotune_b200.targets.whisper:build", "WHISPER_TURBO" if full else "TINY", 0, "whisper_encoder",
+        {"mel": {"seeded": {"kind": "randn", "shape": [1, 3000, 128] if full else [2, 400, 128], "dtype": "float16",
+                            "seed": 0}}},
+        {"rtol": 2e-2, "atol": 4e-2}, steps=2 if full else 5)}
+    return _write_bundle(Path(directory), whisper_specs(), table, HERE / "whisper_wrappers.py", meta)
 
 
 def write_qwen3_bundle(directory: str | Path, n_layers: int) -> Path:
@@ -371,7 +399,12 @@ def write_qwen3_bundle(directory: str | Path, n_layers: int) -> Path:
     table.append({"scope_path": "", "wrapper_class": "W_qwen3_root", "kernel_ids": ROOT_KERNELS})
     (d / "swap_table.json").write_text(json.dumps(table, indent=1) + "\n")
     shutil.copyfile(WRAPPERS, d / "patch" / "wrappers.py")
-    (d / "bundle.json").write_text(json.dumps({"target": "qwen3", "layers": n_layers}, indent=1) + "\n")
+    meta = {"target": "qwen3", "layers": n_layers, **artifact_meta(
+        "metal_autotune_b200.targets.qwen3:build", "QWEN3_4B" if n_layers == 36 else "TINY", 0, "qwen3_prefill",
+        {"prompt": {"seeded": {"kind": "randint", "shape": [128 if n_layers == 36 else 32], "dtype": "int32",
+                               "seed": 0, "high": 151936 if n_layers == 36 else 1000}}},
+        {"rtol": 5e-2, "atol": 5e-2})}
+    (d / "bundle.json").write_text(json.dumps(meta, indent=1) + "\n")
     return d
 
 

@@ -215,6 +215,7 @@ class Qwen3Model(nn.Module):
             c.offset += T
         last = self.norm(h[-1:])
         logits = self.embed_tokens.as_linear(last)
+        self.last_logits = logits  # the last position's logits, for checks
         lse = torch.logsumexp(logits.float(), dim=-1, keepdim=True)
         lp = (logits.float() - lse.to(logits.dtype).float()).to(logits.dtype)
         tok = torch.argmax(lp, dim=-1).to(torch.int32)

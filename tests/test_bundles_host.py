@@ -10,6 +10,7 @@ from __future__ import annotations
 from pathlib import Path
 
 import pytest
+import torch
 
 from metal_autotune_b200 import bundles
 
@@ -36,3 +37,33 @@ def test_every_committed_bundle_is_generated(tmp_path, name):
     out = tmp_path / name
     bundles.BUNDLES[name](out)
     assert _files(out) == _files(bundles.HERE / name)
+
+
+# ------------------------------------------------------------ fresh-process artifact tools (host side)
+def test_artifact_workloads_and_builders_resolve_on_cpu():
+    from metal_autotune_b200.bundles import artifact
+    for name in sorted(bundles.BUNDLES):
+        d = bundles.HERE / name
+        meta = artifact.read_meta(d)
+        assert meta["entry"] in artifact.ENTRIES
+        assert meta["correctness_rule"] in ("baseline_tolerance", "exact")
+        for label, w in meta["workloads"].items():
+            (x,) = artifact.workload_inputs(d, w, device="cpu")
+            if "seeded" in w:
+                assert list(x.shape) == w["seeded"]["shape"]
+                again = artifact.workload_inputs(d, w, device="cpu")[0]
+                assert torch.equal(x, again)  # seeded workloads are reproducible
+
+
+def test_artifact_tiny_targets_build_on_cpu():
+    from metal_autotune_b200.bundles import artifact
+    for name in ("qwen3_tiny", "whisper_tiny", "mamba_tiny", "tiny_mlp"):
+        model = artifact.build_target(artifact.read_meta(bundles.HERE / name), device="cpu")
+        assert isinstance(model, torch.nn.Module)
+
+
+def test_tiny_mlp_workload_file_is_the_baseline_input():
+    from metal_autotune_b200.bundles import artifact
+    from metal_autotune_b200.targets import tiny_mlp
+    (x,) = artifact.workload_inputs(bundles.HERE / "tiny_mlp", {"file": "workloads/x.safetensors"}, device="cpu")
+    assert torch.equal(x, tiny_mlp.build(device="cpu")[1])
