@@ -725,7 +725,7 @@ class ModelStep:
     """A bundle-applied target, its seeded device input and pinned host
     copies, one forward captured in a CUDA graph."""
 
-    def __init__(self, kind: str, tiny: bool = False):
+    def __init__(self, kind: str, tiny: bool = False, backend: str = "replay"):
         import torch
 
         from metal_autotune_b200 import lib, workload
@@ -733,6 +733,9 @@ class ModelStep:
         os.environ["MT_STRICT_REGIONS"] = "1"
         self.torch, self.kind = torch, kind
         bdir = ROOT / "metal_autotune_b200" / "bundles"
+        sfx = "_graph" if backend == "graph" else ""
+        if backend == "graph" and kind == "mamba":
+            raise SystemExit("the graph backend has no Mamba bundle (the replay bundle serves it)")
         if kind == "whisper":
             from metal_autotune_b200.targets import whisper
             self.cfg = whisper.TINY if tiny else whisper.WHISPER_TURBO
@@ -740,7 +743,7 @@ class ModelStep:
             g = torch.Generator(device="cuda").manual_seed(0)
             self.x = torch.randn(WHISPER_BATCH, self.cfg.frames, self.cfg.n_mels, generator=g,
                                  device="cuda").to(torch.float16)
-            self.model = apply(model, bdir / ("whisper_tiny" if tiny else "whisper_turbo"))
+            self.model = apply(model, bdir / (("whisper_tiny" if tiny else "whisper_turbo") + sfx))
             self.flops = whisper.encoder_flops(self.cfg, WHISPER_BATCH)
             self.units = WHISPER_BATCH * self.cfg.frames
         elif kind == "mamba":
@@ -755,7 +758,7 @@ class ModelStep:
             from metal_autotune_b200.targets import tiny_mlp
             self.cfg = tiny_mlp.TINY_MLP
             model, self.x = tiny_mlp.build(self.cfg)
-            self.model = apply(model, bdir / "tiny_mlp")
+            self.model = apply(model, bdir / ("tiny_mlp" + sfx))
             self.flops = tiny_mlp.flops(self.cfg)
             self.units = 1
         self.raw = model
@@ -867,7 +870,7 @@ def run_model_line(args):
                           "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
               flush=True)
         return 0
-    step = ModelStep(kind, tiny)
+    step = ModelStep(kind, tiny, args.backend)
     for _ in range(args.warmup):
         step.replay()
     torch.cuda.synchronize()
@@ -890,7 +893,7 @@ def run_model_line(args):
             "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": higher, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32" if kind == "mlp" else "f16", "data": "synthetic",
             "config": {"workload": args.config, "parallelism": f"replicas x{world}",
-                       "graph": "one CUDA graph per forward",
+                       "graph": "one CUDA graph per forward", "backend": args.backend,
                        "l2": "inputs larger than L2" if kind != "mlp" else "fits L2 (launch-bound, 1.3 MB)"},
             "e2e": {"value": val(ms_e2e), "unit": unit, "h2d_bytes_per_step": step.host_x.numel()
                     * step.host_x.element_size(), "d2h_bytes_per_step": step.host_out.numel()
@@ -925,6 +928,9 @@ def main():
                     help="llama*_tp: Llama-3-8B 8-bit prefill 8 x 2048, tensor-parallel over the ranks; "
                          "whisper_turbo / mamba_370m / tiny_mlp: the other targets' own lines")
     ap.add_argument("--mode", default="request", choices=["request", "kernels"])
+    ap.add_argument("--backend", default="replay", choices=["replay", "graph"],
+                    help="whisper / tiny_mlp lines: the replay bundle (hand-written wrappers) or the graph bundle "
+                         "(traced graph with the regions substituted)")
     ap.add_argument("--only", default="", help="kernels mode: comma-separated kernel names")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-llama-tp", action="store_true",

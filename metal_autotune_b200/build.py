@@ -1,4 +1,5 @@
-"""Build libmt.so (the sm_100a region kernels) in-tree with nvcc.
+"""Build libmt.so (the sm_100a region kernels) in-tree with nvcc, and
+libmt_graph.so (the host-side graph substitution engine) with g++.
 
 Each translation unit compiles with relocatable device code (the device
 status word is shared across them) and the objects are device-linked into
@@ -77,5 +78,30 @@ def build_library(force: bool = False, verbose: bool = False, jobs: int | None =
     return LIB
 
 
+GRAPH_SRC = CSRC / "graph_native.cpp"
+GRAPH_LIB = LIBDIR / "libmt_graph.so"
+
+
+def build_graph_library(force: bool = False) -> Path:
+    """Compile csrc/graph_native.cpp (plain C++17, no CUDA) into
+    lib/libmt_graph.so; returns its path."""
+    deps = [GRAPH_SRC, INCLUDE / "mt_graph.h", Path(__file__)]
+    if not force and not _stale(GRAPH_LIB, deps):
+        return GRAPH_LIB
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("no C++ compiler; libmt_graph.so cannot be built")
+    LIBDIR.mkdir(exist_ok=True)
+    tmp = GRAPH_LIB.with_suffix(".so.tmp")
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-Wall", "-Wextra", f"-I{INCLUDE}", str(GRAPH_SRC),
+           "-o", str(tmp)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed on {GRAPH_SRC.name}:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, GRAPH_LIB)
+    return GRAPH_LIB
+
+
 if __name__ == "__main__":
     print(build_library(force="--force" in sys.argv, verbose=True))
+    print(build_graph_library(force="--force" in sys.argv))

@@ -408,6 +408,130 @@ def write_qwen3_bundle(directory: str | Path, n_layers: int) -> Path:
     return d
 
 
+# ------------------------------------------------------------------ graph-backend bundles
+GRAPH_WRAPPERS = HERE / "graph_wrappers.py"
+_TINY_MLP_MOD = "metal_autotune_b200.targets.tiny_mlp"
+_WHISPER_MOD = "metal_autotune_b200.targets.whisper"
+
+
+def tiny_mlp_graph_variants(batches=(32,)) -> dict:
+    """The tiny MLP's graph rules per batch: the first linear + GELU, then
+    the second linear (each one occurrence)."""
+    from ..targets import tiny_mlp
+    cfg = tiny_mlp.TINY_MLP
+    D, H, f32 = cfg.d_in, cfg.d_hidden, "float32"
+    out = []
+    for B in batches:
+        out.append({"args": [[[B, D], f32]], "rules": [
+            {"kernel_id": "linear_gelu_f32", "sequence": f"{_TINY_MLP_MOD}:linear_gelu",
+             "input_specs": [[[B, D], f32], [[H, D], f32], [[H], f32]], "count": 1},
+            {"kernel_id": "linear_f32", "sequence": f"{_TINY_MLP_MOD}:linear",
+             "input_specs": [[[B, H], f32], [[D, H], f32], [[D], f32]], "count": 1}]})
+    return {"G_tiny_mlp": out}
+
+
+def whisper_graph_specs(n_head: int, head_dim: int = 64) -> list[KernelSpec]:
+    """Specs the graph rules add to the Whisper regions: self-attention on the
+    [B, L, n_state] projections (heads split by strides), and the q/v and k
+    projections as separate linears."""
+    S = [s for s in whisper_specs() if s.kernel_id in
+         ("conv1_gelu", "conv2_gelu", "pos_add", "fc1_gelu", "fc2_residual", "out_proj_residual", "layer_norm")]
+    row = "in0.shape[1] * in0.shape[2]"
+    S.append(KernelSpec(
+        kernel_id="attention", name="mt_sdpa", input_names=("in0", "in1", "in2"), output_names=("out0",),
+        cuda={"symbol": "mt_sdpa", "args": [
+            {"in": 0}, {"in": 1}, {"in": 2}, {"out": 0}, {"expr": "in0.shape[0]"}, {"int": n_head}, {"int": n_head},
+            {"expr": "in0.shape[1]"}, {"expr": "in1.shape[1]"}, {"int": head_dim},
+            {"float": 1.0 / math.sqrt(head_dim)}, {"int": 0}, {"int": 0},
+            {"expr": row}, {"int": head_dim}, {"expr": "in0.shape[2]"},
+            {"expr": "in1.shape[1] * in1.shape[2]"}, {"int": head_dim}, {"expr": "in1.shape[2]"},
+            {"expr": "in2.shape[1] * in2.shape[2]"}, {"int": head_dim}, {"expr": "in2.shape[2]"},
+            {"expr": row}, {"int": head_dim}, {"expr": "in0.shape[2]"}, {"dtype": "in0"}, {"stream": True}]},
+        output_shapes=(("in0.shape[0]", "in0.shape[1]", "in0.shape[2]"),), output_dtypes=("in0",),
+        fallback_predicate=f"in0.shape[2] != {n_head * head_dim}", reassociates=True))
+    rows = "in0.shape[0] * in0.shape[1]"
+    for kid, bias in (("linear_bias", {"in": 2}), ("linear_nobias", {"null": True})):
+        n_in = 3 if kid == "linear_bias" else 2
+        S.append(KernelSpec(
+            kernel_id=kid, name="mt_linear", input_names=tuple(f"in{i}" for i in range(n_in)), output_names=("out0",),
+            cuda={"symbol": "mt_linear", "args": [
+                {"in": 0}, {"in": 1}, bias, {"out": 0}, {"expr": rows}, {"expr": "in1.shape[0]"},
+                {"expr": "in0.shape[2]"}, {"int": 0}, {"dtype": "in0"}, {"stream": True}]},
+            output_shapes=(("in0.shape[0]", "in0.shape[1]", "in1.shape[0]"),), output_dtypes=("in0",),
+            fallback_predicate="in0.shape[2] % 8 != 0", reassociates=True))
+    return S
+
+
+def whisper_graph_variants(cfg, batches) -> dict:
+    """The encoder's graph rules per batch, larger regions first (a rule
+    rewrites before the next one looks for its pattern)."""
+    S, L, T, M, n, f16 = cfg.n_state, cfg.n_ctx, cfg.frames, cfg.n_mels, cfg.n_layer, "float16"
+    out = []
+    for B in batches:
+        act = [[B, L, S], f16]
+        vec = lambda k: [[k], f16]
+        out.append({"args": [[[B, T, M], f16]], "rules": [
+            {"kernel_id": "conv1_gelu", "sequence": f"{_WHISPER_MOD}:conv_gelu", "bind": {"stride": 1},
+             "input_specs": [[[B, T, M], f16], [[S, 3, M], f16], vec(S)], "count": 1},
+            {"kernel_id": "conv2_gelu", "sequence": f"{_WHISPER_MOD}:conv_gelu", "bind": {"stride": 2},
+             "input_specs": [[[B, T, S], f16], [[S, 3, S], f16], vec(S)], "count": 1},
+            {"kernel_id": "pos_add", "sequence": f"{_WHISPER_MOD}:residual_add",
+             "input_specs": [act, [[L, S], f16]], "count": 1,
+             "anchors": [None, ["weight", "positional_embedding"]]},
+            {"kernel_id": "fc1_gelu", "sequence": f"{_WHISPER_MOD}:linear_gelu",
+             "input_specs": [act, [[4 * S, S], f16], vec(4 * S)], "count": n},
+            {"kernel_id": "fc2_residual", "sequence": f"{_WHISPER_MOD}:linear_residual",
+             "input_specs": [[[B, L, 4 * S], f16], [[S, 4 * S], f16], vec(S), act], "count": n},
+            {"kernel_id": "out_proj_residual", "sequence": f"{_WHISPER_MOD}:linear_residual",
+             "input_specs": [act, [[S, S], f16], vec(S), act], "count": n},
+            {"kernel_id": "attention", "sequence": f"{_WHISPER_MOD}:attend", "bind": {"n_head": cfg.n_head},
+             "input_specs": [act, act, act], "count": n},
+            {"kernel_id": "linear_bias", "sequence": f"{_WHISPER_MOD}:linear",
+             "input_specs": [act, [[S, S], f16], vec(S)], "count": 2 * n},
+            {"kernel_id": "linear_nobias", "sequence": f"{_WHISPER_MOD}:linear",
+             "input_specs": [act, [[S, S], f16]], "count": n},
+            {"kernel_id": "layer_norm", "sequence": f"{_WHISPER_MOD}:layer_norm", "bind": {"eps": cfg.eps},
+             "input_specs": [act, vec(S), vec(S)], "count": 2 * n + 1}]})
+    return {"G_whisper_encoder": out}
+
+
+def _write_graph_bundle(d: Path, specs, wrapper_class: str, kernel_ids, variants: dict, meta: dict) -> Path:
+    table = [{"scope_path": "", "wrapper_class": wrapper_class, "kernel_ids": list(kernel_ids)}]
+    _write_bundle(d, specs, table, GRAPH_WRAPPERS, {**meta, "backend": "graph"})
+    (d / "patch" / "graph_variants.json").write_text(json.dumps(variants, indent=1) + "\n")
+    return d
+
+
+def write_tiny_mlp_graph_bundle(directory: str | Path) -> Path:
+    d = Path(directory)
+    (d / "workloads").mkdir(parents=True, exist_ok=True)
+    from safetensors.torch import save_file
+
+    from ..targets import tiny_mlp
+    _, x = tiny_mlp.build(tiny_mlp.TINY_MLP, device="cpu")  # the BASELINE input (seed 0, after the weights)
+    save_file({"i0": x.contiguous()}, str(d / "workloads" / "x.safetensors"))
+    meta = {"target": "tiny_mlp", "layers": 2, **artifact_meta(
+        "metal_autotune_b200.targets.tiny_mlp:build", "TINY_MLP", None, "tiny_mlp",
+        {"x": {"file": "workloads/x.safetensors"}}, {"rtol": 1e-4, "atol": 1e-4}, steps=20)}
+    return _write_graph_bundle(d, tiny_mlp_specs(), "G_tiny_mlp", ["linear_gelu_f32", "linear_f32"],
+                               tiny_mlp_graph_variants(), meta)
+
+
+def write_whisper_graph_bundle(directory: str | Path, n_layers: int) -> Path:
+    from ..targets import whisper
+    cfg = whisper.WHISPER_TURBO if n_layers == 32 else whisper.TINY
+    full = n_layers == 32
+    batches = (1, 8) if full else (2,)
+    meta = {"target": "whisper_encoder", "layers": n_layers, **artifact_meta(
+        "metal_autotune_b200.targets.whisper:build", "WHISPER_TURBO" if full else "TINY", 0, "whisper_encoder",
+        {"mel": {"seeded": {"kind": "randn", "shape": [1, 3000, 128] if full else [2, 400, 128], "dtype": "float16",
+                            "seed": 0}}},
+        {"rtol": 2e-2, "atol": 4e-2}, steps=2 if full else 5)}
+    specs = whisper_graph_specs(cfg.n_head, cfg.head_dim)
+    return _write_graph_bundle(Path(directory), specs, "G_whisper_encoder", [s.kernel_id for s in specs],
+                               whisper_graph_variants(cfg, batches), meta)
+
+
 BUNDLES = {
     "qwen3_4b": lambda d: write_qwen3_bundle(d, 36),
     "qwen3_tiny": lambda d: write_qwen3_bundle(d, 2),
@@ -416,6 +540,9 @@ BUNDLES = {
     "mamba_370m": lambda d: write_mamba_bundle(d, 48),
     "mamba_tiny": lambda d: write_mamba_bundle(d, 2),
     "tiny_mlp": write_tiny_mlp_bundle,
+    "tiny_mlp_graph": write_tiny_mlp_graph_bundle,
+    "whisper_turbo_graph": lambda d: write_whisper_graph_bundle(d, 32),
+    "whisper_tiny_graph": lambda d: write_whisper_graph_bundle(d, 2),
 }
 
 

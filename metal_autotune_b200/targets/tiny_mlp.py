@@ -28,6 +28,21 @@ class TinyMLPConfig:
 TINY_MLP = TinyMLPConfig()
 
 
+def linear(x, w, b):
+    """One Linear's original op: x w^T + b."""
+    return x @ w.t() + b
+
+
+def gelu(h):
+    """GELU in its exact erf form."""
+    return h * (1 + torch.erf(h / math.sqrt(2))) / 2
+
+
+def linear_gelu(x, w, b):
+    """The first region's original ops: the first Linear, then GELU."""
+    return gelu(linear(x, w, b))
+
+
 class Linear(nn.Module):
     def __init__(self, w, b):
         super().__init__()
@@ -35,7 +50,7 @@ class Linear(nn.Module):
         self.register_buffer("bias", b)
 
     def forward(self, x):
-        return x @ self.weight.t() + self.bias
+        return linear(x, self.weight, self.bias)
 
 
 class TinyMLP(nn.Module):
@@ -44,9 +59,7 @@ class TinyMLP(nn.Module):
         self.l1, self.l2 = l1, l2
 
     def forward(self, x):
-        h = self.l1(x)
-        h = h * (1 + torch.erf(h / math.sqrt(2))) / 2
-        return self.l2(h)
+        return self.l2(gelu(self.l1(x)))
 
 
 def kaiming_uniform(n_out: int, n_in: int, g: torch.Generator) -> torch.Tensor:

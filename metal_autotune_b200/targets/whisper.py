@@ -62,6 +62,57 @@ def _r(x: torch.Tensor) -> torch.Tensor:
     return x.to(torch.float16)
 
 
+# ---- each op's original sequence, shared by the modules below and by the
+# graph bundles' region patterns (bundles/graph_wrappers.py)
+def linear(x, w, b=None):
+    """mlx.nn.Linear: y = round(x w^T + b) (one rounding, fp32 sums)."""
+    y = x.float() @ w.float().t()
+    if b is not None:
+        y = y + b.float()
+    return _r(y)
+
+
+def conv1d(x, w, b, stride: int, padding: int):
+    """mlx.nn.Conv1d on channels-last x [B, L, Cin], weight [Cout, K, Cin]:
+    conv rounded, then + bias rounded."""
+    y = F.conv1d(x.float().transpose(1, 2), w.float().permute(0, 2, 1), stride=stride,
+                 padding=padding).transpose(1, 2)
+    return _r(_r(y).float() + b.float())
+
+
+def layer_norm(x, w, b, eps: float):
+    return _r(F.layer_norm(x.float(), (x.shape[-1],), w.float(), b.float(), eps))
+
+
+def residual_add(x, y):
+    """x + y of two fp16 tensors, rounded once."""
+    return _r(x.float() + y.float())
+
+
+def attend(q, k, v, n_head: int):
+    """q, k, v [B, L, n_state] -> softmax(q k^T / sqrt(d)) v, heads concatenated."""
+    B, L, S = q.shape
+    d = S // n_head
+    sh = lambda t: t.float().view(B, L, n_head, d).transpose(1, 2)
+    o = F.scaled_dot_product_attention(sh(q), sh(k), sh(v), scale=1.0 / math.sqrt(d))
+    return _r(o.transpose(1, 2).reshape(B, L, S))
+
+
+def conv_gelu(x, w, b, stride: int):
+    """Region: a conv of the stem, then GELU."""
+    return gelu(conv1d(x, w, b, stride, 1))
+
+
+def linear_gelu(x, w, b):
+    """Region: fc1, then GELU."""
+    return gelu(linear(x, w, b))
+
+
+def linear_residual(x, w, b, res):
+    """Region: a projection (out or fc2) added to the residual stream."""
+    return residual_add(res, linear(x, w, b))
+
+
 class Linear(nn.Module):
     """mlx.nn.Linear: y = round(x w^T + b) (one rounding, fp32 sums)."""
 
@@ -71,10 +122,7 @@ class Linear(nn.Module):
         self.register_buffer("bias", b if b is not None else None)
 
     def forward(self, x):
-        y = x.float() @ self.weight.float().t()
-        if self.bias is not None:
-            y = y + self.bias.float()
-        return _r(y)
+        return linear(x, self.weight, self.bias)
 
 
 class Conv1d(nn.Module):
@@ -88,9 +136,7 @@ class Conv1d(nn.Module):
         self.stride, self.padding = stride, padding
 
     def forward(self, x):
-        y = F.conv1d(x.float().transpose(1, 2), self.weight.float().permute(0, 2, 1), stride=self.stride,
-                     padding=self.padding).transpose(1, 2)
-        return _r(_r(y).float() + self.bias.float())
+        return conv1d(x, self.weight, self.bias, self.stride, self.padding)
 
 
 class LayerNorm(nn.Module):
@@ -101,7 +147,7 @@ class LayerNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x):
-        return _r(F.layer_norm(x.float(), (x.shape[-1],), self.weight.float(), self.bias.float(), self.eps))
+        return layer_norm(x, self.weight, self.bias, self.eps)
 
 
 def gelu(x: torch.Tensor) -> torch.Tensor:
@@ -118,11 +164,7 @@ class MultiHeadAttention(nn.Module):
 
     def attend(self, q, k, v):
         """q, k, v [B, L, n_state] -> softmax(q k^T / sqrt(d)) v, heads concatenated."""
-        cfg = self.cfg
-        B, L, S = q.shape
-        sh = lambda t: t.float().view(B, L, cfg.n_head, cfg.head_dim).transpose(1, 2)
-        o = F.scaled_dot_product_attention(sh(q), sh(k), sh(v), scale=1.0 / math.sqrt(cfg.head_dim))
-        return _r(o.transpose(1, 2).reshape(B, L, S))
+        return attend(q, k, v, self.cfg.n_head)
 
     def forward(self, x):
         return self.out(self.attend(self.query(x), self.key(x), self.value(x)))
@@ -137,8 +179,8 @@ class ResidualAttentionBlock(nn.Module):
         self.mlp_ln = LayerNorm(cfg.n_state, cfg.eps, device)
 
     def forward(self, x):
-        x = _r(x.float() + self.attn(self.attn_ln(x)).float())
-        return _r(x.float() + self.mlp2(gelu(self.mlp1(self.mlp_ln(x)))).float())
+        x = residual_add(x, self.attn(self.attn_ln(x)))
+        return residual_add(x, self.mlp2(gelu(self.mlp1(self.mlp_ln(x)))))
 
 
 class AudioEncoder(nn.Module):
@@ -154,7 +196,7 @@ class AudioEncoder(nn.Module):
         """mel [B, frames, n_mels] fp16 -> [B, n_ctx, n_state] fp16."""
         x = gelu(self.conv1(mel))
         x = gelu(self.conv2(x))
-        x = _r(x.float() + self.positional_embedding.float())
+        x = residual_add(x, self.positional_embedding)
         for blk in self.blocks:
             x = blk(x)
         return self.ln_post(x)
