@@ -123,6 +123,133 @@ __global__ void __launch_bounds__(256) mamba_scan_kernel(const void* __restrict_
   if (hstate && active) hstate[static_cast<int64_t>(c) * NS + s] = h;
 }
 
+// Chunked scan for long prompts. The sequential kernel above runs one lane
+// per (channel, state): 32768 lanes for a Mamba-370m layer, about 7 warps per
+// SM, so every step waits on its predecessor's latency. Here the L steps
+// are cut into KC chunks and warp k of a CTA runs chunk k of the CTA's
+// channels, KC times the parallelism:
+//   pass 1  each chunk's recurrence from h = 0: its end state e_k and the
+//           product P_k of its decays exp(dt A) (the same a_t and u_t as pass 3);
+//   fold    chunk k's carry-in h_k = P_{k-1} h_{k-1} + e_{k-1} (h_0 the state
+//           carried into the call), from shared memory;
+//   pass 3  the recurrence again from h_k, emitting y_t = (C_t h_t + D x_t) z_t sigma(z_t).
+// Every step's a_t, u_t and h update are the sequential kernel's operations
+// (no contraction); only the chunk carry-ins are reassociated. Steps run in
+// blocks of NS: lane s of a channel's group computes the softplus of step s
+// of the block and loads its x and z, shared by shuffles; the NS per-step
+// state reductions of a block are interleaved, and lane s finishes step s.
+template <int DT, int NS, int KC>
+__global__ void __launch_bounds__(KC * 32) mamba_scan_chunked_kernel(
+    const void* __restrict__ xp, const void* __restrict__ dtp, const float* __restrict__ dt_bias,
+    const float* __restrict__ A, const void* __restrict__ Bp, const void* __restrict__ Cp,
+    const float* __restrict__ Dv, const void* __restrict__ zp, void* __restrict__ yp, float* __restrict__ hstate,
+    int L, int d_inner, int CL) {
+  using T = typename Elem<DT>::T;
+  constexpr int CPW = 32 / NS;  // channels per warp (and per CTA)
+  __shared__ float s_end[KC][CPW][NS];
+  __shared__ float s_prod[KC][CPW][NS];
+  griddep_wait();
+  griddep_launch();  // dependents may launch now; their own wait covers this grid
+  const int lane = threadIdx.x & 31;
+  const int k = threadIdx.x >> 5;  // chunk
+  const int s = lane % NS;
+  const int g = lane / NS;         // channel within the CTA
+  const int gbase = lane - s;
+  const int c = blockIdx.x * CPW + g;
+  const bool active = c < d_inner;
+  const int cc = active ? c : 0;
+  const T* x = static_cast<const T*>(xp);
+  const T* dtr = static_cast<const T*>(dtp);
+  const T* Bm = static_cast<const T*>(Bp);
+  const T* Cm = static_cast<const T*>(Cp);
+  const T* z = static_cast<const T*>(zp);
+  T* y = static_cast<T*>(yp);
+  const float a = A[static_cast<int64_t>(cc) * NS + s];
+  const float bias = dt_bias ? dt_bias[cc] : 0.f;
+  const float dd = Dv ? Dv[cc] : 0.f;
+  const int t_lo = k * CL;
+  const int t_hi = min(L, t_lo + CL);
+
+  // one block of NS steps from t0: this lane's step t0 + s supplies dt, x (and z)
+  auto step_inputs = [&](int t0, float& dtm, float& xm, float& zm, bool want_z) {
+    const int t = t0 + s;
+    dtm = xm = zm = 0.f;
+    if (t < t_hi) {
+      dtm = softplus_f32(__fadd_rn(Elem<DT>::to_f(dtr[static_cast<int64_t>(t) * d_inner + cc]), bias));
+      xm = Elem<DT>::to_f(x[static_cast<int64_t>(t) * d_inner + cc]);
+      if (want_z) zm = Elem<DT>::to_f(z[static_cast<int64_t>(t) * d_inner + cc]);
+    }
+  };
+
+  // ---- pass 1: the chunk from h = 0
+  float h = 0.f, prod = 1.f;
+  for (int t0 = t_lo; t0 < t_hi; t0 += NS) {
+    float dtm, xm, zm;
+    step_inputs(t0, dtm, xm, zm, false);
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      const float dt = __shfl_sync(0xffffffffu, dtm, gbase + j);
+      const float xv = __shfl_sync(0xffffffffu, xm, gbase + j);
+      if (t0 + j < t_hi) {
+        const float bv = Elem<DT>::to_f(Bm[static_cast<int64_t>(t0 + j) * NS + s]);
+        const float dA = expf(__fmul_rn(dt, a));
+        const float u = __fmul_rn(__fmul_rn(dt, bv), xv);
+        h = __fadd_rn(__fmul_rn(dA, h), u);
+        prod = __fmul_rn(prod, dA);
+      }
+    }
+  }
+  s_end[k][g][s] = h;
+  s_prod[k][g][s] = prod;
+  // the carried-in state is read before the barrier: after it the last chunk may overwrite it
+  h = (hstate && active) ? hstate[static_cast<int64_t>(cc) * NS + s] : 0.f;
+  __syncthreads();
+
+  // ---- carry-in of chunk k
+  for (int j = 0; j < k; ++j) h = __fadd_rn(__fmul_rn(s_prod[j][g][s], h), s_end[j][g][s]);
+
+  // ---- pass 3: the chunk from its carry-in, emitting y
+  for (int t0 = t_lo; t0 < t_hi; t0 += NS) {
+    float dtm, xm, zm;
+    step_inputs(t0, dtm, xm, zm, true);
+    float part[NS];
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      const float dt = __shfl_sync(0xffffffffu, dtm, gbase + j);
+      const float xv = __shfl_sync(0xffffffffu, xm, gbase + j);
+      part[j] = 0.f;
+      if (t0 + j < t_hi) {
+        const float bv = Elem<DT>::to_f(Bm[static_cast<int64_t>(t0 + j) * NS + s]);
+        const float cv = Elem<DT>::to_f(Cm[static_cast<int64_t>(t0 + j) * NS + s]);
+        const float dA = expf(__fmul_rn(dt, a));
+        const float u = __fmul_rn(__fmul_rn(dt, bv), xv);
+        h = __fadd_rn(__fmul_rn(dA, h), u);
+        part[j] = __fmul_rn(cv, h);
+      }
+    }
+#pragma unroll
+    for (int o = NS / 2; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < NS; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j], o);
+    float pm = part[0];
+#pragma unroll
+    for (int j = 1; j < NS; ++j)
+      if (j == s) pm = part[j];
+    const int t = t0 + s;
+    if (active && t < t_hi) {
+      const float yv = __fadd_rn(pm, __fmul_rn(dd, xm));
+      const float sg = 1.0f / (1.0f + expf(-zm));
+      y[static_cast<int64_t>(t) * d_inner + c] = Elem<DT>::from_f(__fmul_rn(yv, __fmul_rn(zm, sg)));
+    }
+  }
+  // the state after the last step: the last chunk's final h (chunks past L end where they start)
+  if (hstate && active && t_lo < L && t_hi == L) hstate[static_cast<int64_t>(c) * NS + s] = h;
+}
+
+// prompts of at least this many steps take the chunked scan, in kScanChunks chunks
+constexpr int kScanChunkedMinL = 128;
+constexpr int kScanChunks = 8;
+
 template <int DT>
 __global__ void __launch_bounds__(256) causal_conv1d_kernel(const void* __restrict__ xp, const void* __restrict__ wp,
                                                             const void* __restrict__ bp, const void* __restrict__ sp,
@@ -187,9 +314,27 @@ int mt_mamba_scan(const void* x, const void* dt_raw, const float* dt_bias, const
   MT_CHECK_ARG(dtype == MT_BF16 || dtype == MT_F16 || dtype == MT_F32, "mt_mamba_scan: bad dtype");
   if (L == 0) return MT_OK;
   const int cpw = 32 / static_cast<int>(d_state);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (L >= kScanChunkedMinL) {
+    // chunked in time: kScanChunks warps per CTA (one per chunk), the CTA's cpw channels
+    constexpr int KC = kScanChunks;
+    const int CL = static_cast<int>((((L + KC - 1) / KC) + d_state - 1) / d_state * d_state);
+    const dim3 cgrid(static_cast<unsigned>((d_inner + cpw - 1) / cpw));
+#define MT_CSCAN(DTV, NSV)                                                                                        \
+  return launch(mamba_scan_chunked_kernel<DTV, NSV, KC>, cgrid, dim3(KC * 32), 0, s, x, dt_raw, dt_bias, A, Bm, \
+                Cm, Dv, z, y, h_state, (int)L, (int)d_inner, CL)
+#define MT_CSCAN_NS(DTV)                  \
+  if (d_state == 8) MT_CSCAN(DTV, 8);    \
+  if (d_state == 16) MT_CSCAN(DTV, 16);  \
+  MT_CSCAN(DTV, 32)
+    if (dtype == MT_BF16) { MT_CSCAN_NS(MT_BF16); }
+    if (dtype == MT_F16) { MT_CSCAN_NS(MT_F16); }
+    MT_CSCAN_NS(MT_F32);
+#undef MT_CSCAN_NS
+#undef MT_CSCAN
+  }
   const int64_t warps = (d_inner + cpw - 1) / cpw;
   const dim3 grid(static_cast<unsigned>((warps + 7) / 8));
-  cudaStream_t s = (cudaStream_t)stream;
 #define MT_SCAN(DTV, NSV)                                                                                   \
   return launch(mamba_scan_kernel<DTV, NSV>, grid, dim3(256), 0, s, x, dt_raw, dt_bias, A, Bm, Cm, Dv, z, y, \
                 h_state, (int)L, (int)d_inner)

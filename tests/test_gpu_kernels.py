@@ -309,13 +309,20 @@ def test_gelu_erf_against_double_erf(cuda, oracle):
     assert ((g.double() - ref).abs() <= bound).all()
 
 
-@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
-def test_mamba_scan(cuda, oracle, dtype):
+@pytest.mark.parametrize("dtype,L,NS,decay", [("float16", 64, 16, 1.0), ("bfloat16", 64, 16, 1.0),
+                                              ("float16", 512, 16, 1.0), ("float16", 512, 16, 0.002),
+                                              ("bfloat16", 300, 16, 0.002), ("float16", 128, 8, 0.002),
+                                              ("float16", 257, 32, 0.002)])
+def test_mamba_scan(cuda, oracle, dtype, L, NS, decay):
+    """Sequential kernel below 128 steps, chunked in time from 128 up (ragged
+    chunk ends, an empty last chunk at L=300, the carried-in state). With
+    decay 0.002 (A = -0.002 * (1..NS)) a chunk's carry-in still weighs in
+    hundreds of steps later, so a wrong carry between chunks shows."""
     tdt = torch.float16 if dtype == "float16" else BF
-    L, C, NS = 64, 96, 16
+    C = 96
     x, dtr, z = (oracle.round_to(rng.standard_normal((L, C)).astype(np.float32), dtype) for _ in range(3))
     Bm, Cm = (oracle.round_to(rng.standard_normal((L, NS)).astype(np.float32), dtype) for _ in range(2))
-    A = -np.tile(np.arange(1, NS + 1, dtype=np.float32), (C, 1))
+    A = -np.tile(np.arange(1, NS + 1, dtype=np.float32), (C, 1)) * np.float32(decay)
     dtb = (rng.standard_normal(C) * 0.1).astype(np.float32)
     Dv = np.ones(C, np.float32)
     h0 = (rng.standard_normal((C, NS)) * 0.1).astype(np.float32)
