@@ -12,6 +12,8 @@
 // merge), so the fp64 cosine sums do not depend on scheduling either. The
 // block count depends only on n. Inputs are read as 16-byte vectors when both
 // are 16-byte aligned, the next vectors in flight while one is visited.
+#include <type_traits>
+
 #include "mt_common.cuh"
 
 namespace mt {
@@ -114,6 +116,111 @@ __device__ __forceinline__ void visit_float(const T av, const T bv, int64_t i, f
   p.dbb += static_cast<double>(b0) * static_cast<double>(b0);
 }
 
+// Eight 16-bit elements (one 16-byte vector of each input) at indices
+// i0 .. i0+7. When no element of either vector is Inf or NaN (the exponent
+// test runs on packed pairs) the policy reduces to its finite branch:
+// excess = |a - b| - max(atol + rtol |b|, wobble) per element, and the
+// vector's bit mismatches are counted on packed pairs. The maximum excess
+// keeps the first index of its value (elements visited in order, a strict
+// comparison), as the element-by-element visit does. The cosine sums take
+// the vector's three fp32 sums of exact products and add them in fp64 (fp64
+// products when a magnitude in the vector is above 2^62 or below 2^-60). A
+// vector holding a non-finite value takes the full per-element policy; an
+// element whose excess is NaN (|b| and |a - b| both overflowing) gets the
+// policy's scaled form, as in the full visit.
+template <typename T>
+__device__ __forceinline__ void visit_vec16(const uint4 va, const uint4 vb, int64_t i0, float rtol, float atol,
+                                            float wobble, DiffPartial& p) {
+  // a half's exponent field is all ones (Inf or NaN) exactly when adding its
+  // lowest exponent bit carries into the half's sign position; the masked
+  // fields cannot carry across halves
+  constexpr bool kBf = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kExp = kBf ? 0x7F807F80u : 0x7C007C00u;
+  constexpr uint32_t kLsb = kBf ? 0x00800080u : 0x04000400u;
+  const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+  const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+  uint32_t special = 0, diff = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    special |= ((wa[k] & kExp) + kLsb) | ((wb[k] & kExp) + kLsb);
+    diff |= wa[k] ^ wb[k];
+  }
+  special &= 0x80008000u;
+  const T* ea = reinterpret_cast<const T*>(wa);
+  const T* eb = reinterpret_cast<const T*>(wb);
+  if (special) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) visit_float<T>(ea[e], eb[e], i0 + e, rtol, atol, wobble, p);
+    return;
+  }
+  if (diff) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p.mism += __popc(__vcmpne2(wa[k], wb[k])) >> 4;
+    if (p.first_mism < 0) {
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t x = (wa[e >> 1] ^ wb[e >> 1]) >> ((e & 1) * 16);
+        if (x & 0xFFFFu) {
+          p.first_mism = i0 + e;
+          break;
+        }
+      }
+    }
+  }
+  float best = 0.f;
+  int best_e = -1;
+  float sab = 0.f, saa = 0.f, sbb = 0.f, vmax = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float c = fval<T>(ea[e]), r = fval<T>(eb[e]);
+    vmax = fmaxf(vmax, fmaxf(fabsf(c), fabsf(r)));
+    const float allowed = fmaxf(__fadd_rn(atol, __fmul_rn(rtol, fabsf(r))), wobble);
+    const float ad = fabsf(__fsub_rn(c, r));
+    float excess = __fsub_rn(ad, allowed);
+    if (excess != excess) {
+      // |b| and |a - b| overflowed together: the policy's scaled form
+      const float scale = fmaxf(fmaxf(fabsf(c), fabsf(r)), 1.0f);
+      const float cs = __fdiv_rn(c, scale), rs = __fdiv_rn(r, scale);
+      const float se = __fsub_rn(fabsf(__fsub_rn(cs, rs)),
+                                 __fadd_rn(__fdiv_rn(atol, scale), __fmul_rn(rtol, fabsf(rs))));
+      excess = __fmul_rn(se, scale);
+    }
+    p.max_abs = fmaxf(p.max_abs, ad);
+    if (excess != excess) {
+      ++p.nan_ex;
+    } else {
+      if (excess > 0.f) ++p.over;
+      if (best_e < 0 || excess > best) {
+        best = excess;
+        best_e = e;
+      }
+    }
+    p.amax_a = fmaxf(p.amax_a, fabsf(c));
+    p.amax_b = fmaxf(p.amax_b, fabsf(r));
+    sab = fmaf(c, r, sab);
+    saa = fmaf(c, c, saa);
+    sbb = fmaf(r, r, sbb);
+  }
+  if (best_e >= 0 && (p.excess_index < 0 || best > p.max_excess)) {
+    p.max_excess = best;
+    p.excess_index = i0 + best_e;
+  }
+  if (vmax <= 0x1p62f && vmax >= 0x1p-60f) {
+    // products and 8-term sums stay well inside fp32's range
+    p.dab += static_cast<double>(sab);
+    p.daa += static_cast<double>(saa);
+    p.dbb += static_cast<double>(sbb);
+  } else if (vmax != 0.f) {
+    // magnitudes whose fp32 products could overflow or vanish: fp64 products
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const double c = fval<T>(ea[e]), r = fval<T>(eb[e]);
+      p.dab += c * r;
+      p.daa += c * c;
+      p.dbb += r * r;
+    }
+  }
+}
+
 template <typename U>
 __device__ __forceinline__ void visit_bits(const U av, const U bv, int64_t i, DiffPartial& p) {
   if (av != bv) {
@@ -130,7 +237,7 @@ static inline int diff_blocks(int64_t n) {
 }
 
 template <typename T, bool FLOAT>
-__global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict__ a, const T* __restrict__ b, int64_t n,
+__global__ void __launch_bounds__(kDiffThreads, 3) diff_kernel(const T* __restrict__ a, const T* __restrict__ b, int64_t n,
                                                             float rtol, float atol, float wobble,
                                                             DiffPartial* __restrict__ parts, uint32_t* counter,
                                                             mt_diff_stats* __restrict__ out) {
@@ -167,11 +274,15 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(const T* __restrict_
         nb = *reinterpret_cast<const uint4*>(b + nx);
       }
       if (i + V <= hi) {
-        const T* ea = reinterpret_cast<const T*>(&va);
-        const T* eb = reinterpret_cast<const T*>(&vb);
+        if constexpr (FLOAT && sizeof(T) == 2) {
+          visit_vec16<T>(va, vb, i, rtol, atol, wobble, p);
+        } else {
+          const T* ea = reinterpret_cast<const T*>(&va);
+          const T* eb = reinterpret_cast<const T*>(&vb);
 #pragma unroll
-        for (int e = 0; e < V; ++e) {
-          if constexpr (FLOAT) visit_float<T>(ea[e], eb[e], i + e, rtol, atol, wobble, p);
+          for (int e = 0; e < V; ++e) {
+            if constexpr (FLOAT) visit_float<T>(ea[e], eb[e], i + e, rtol, atol, wobble, p);
+          }
         }
       } else {
         for (int64_t j = i; j < hi; ++j) {

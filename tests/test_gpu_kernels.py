@@ -373,6 +373,42 @@ def test_diff_reduce_matches_contract(cuda, size):
     assert s.max_abs == pytest.approx(NR.max_abs_diff(cand, ref), rel=0, abs=0)
 
 
+@pytest.mark.parametrize("dtype", [BF, torch.float16])
+@pytest.mark.parametrize("rtol", [1e-2, 2.0])
+def test_diff_reduce_16bit_equals_its_fp32_upcast(cuda, dtype, rtol):
+    """A 16-bit pair is visited 8 elements at a time (packed checks, the
+    finite branch of the policy); its fp32 upcast takes the element-by-
+    element policy. Every statistic but the cosine sums must be identical:
+    Inf / NaN spread over some vectors, +0 vs -0, equal and unequal vectors,
+    the largest finite magnitudes (with rtol 2 their allowed error and
+    |a - b| both overflow: the scaled form) and a ragged tail."""
+    n = 8 * 4099 + 5
+    g = torch.Generator(device="cuda").manual_seed(11)
+    b = torch.randn(n, generator=g, device="cuda")
+    a = b + torch.randn(n, generator=g, device="cuda") * 0.05
+    a[:64] = b[:64]                                       # whole equal vectors
+    big = torch.finfo(dtype).max
+    a[100], b[100] = 0.0, -0.0                             # bits differ, values equal
+    a[205], b[205] = float("inf"), float("inf")
+    a[317], b[317] = float("nan"), 1.0                     # a non-finite where b is finite
+    a[333], b[333] = 2.0, float("-inf")
+    a[900], b[900] = big, -big                             # |a - b| overflows fp32 for bf16
+    a[901], b[901] = -big, big
+    a[n - 2] = float("nan")                                # in the tail
+    a16, b16 = a.to(dtype), b.to(dtype)
+    s16 = _stats(a16, b16, rtol=rtol, atol=1e-3)
+    s32 = _stats(a16.float(), b16.float(), rtol=rtol, atol=1e-3)
+    for f in ("max_excess", "excess_index", "over_count", "nonfinite_violations", "first_violation",
+              "nan_excess", "max_abs", "amax_a", "amax_b"):
+        assert getattr(s16, f) == getattr(s32, f), f
+    # bit mismatches of the 16-bit values (the fp32 upcast keeps them one for one)
+    diff = (a16.view(torch.int16) != b16.view(torch.int16)).cpu().numpy()
+    assert s16.bit_mismatches == s32.bit_mismatches == int(diff.sum())
+    assert s16.first_mismatch == s32.first_mismatch == int(np.argmax(diff))
+    for f in ("dot_ab", "dot_aa", "dot_bb"):
+        assert getattr(s16, f) == pytest.approx(getattr(s32, f), rel=1e-6), f
+
+
 def test_numeric_compare_on_golden_cases(cuda):
     from metal_autotune_b200.autotuner_runtime import numeric
     from tests.conftest import fval, golden
