@@ -5,7 +5,9 @@ watchdog, autotuner/sandbox/watchdog.py:7-31).
 
 A verification job is one bundle checked in a fresh worker process
 (bundles/artifact.validate: original vs bundle-applied target on the
-bundle's workloads). `fan_out` runs the jobs on the given GPUs, at most one
+bundle's workloads), or one candidate kernel climbing the verification
+ladder (ladder.run_ladder on the LadderJob a named builder returns in the
+worker), as the reference's sandbox runs each evaluation in its own child. `fan_out` runs the jobs on the given GPUs, at most one
 worker per GPU at a time (CUDA_VISIBLE_DEVICES pins each worker), and
 returns one Verdict per job. No collective: the jobs are independent.
 
@@ -188,7 +190,8 @@ def _verdict_from(res, job: str) -> Verdict:
 def fan_out(jobs: list[dict], gpus: list[int], *, timeout_s: float = 900.0, gpu_timeout_s: float = GPU_WINDOW_S,
             command: list[str] | None = None) -> list[Verdict]:
     """Run every job in its own worker, at most one worker per GPU at a time.
-    A job is {"name": ..., "bundle": path} (or anything a custom `command`
+    A job is {"name": ..., "bundle": path}, {"name": ..., "ladder":
+    "module:function", "args": [...]} (or anything a custom `command`
     worker reads from its stdin). Verdicts come back in job order. After a
     verdict with abort_job set, no further job is started."""
     if not gpus:
@@ -225,10 +228,27 @@ def fan_out(jobs: list[dict], gpus: list[int], *, timeout_s: float = 900.0, gpu_
 
 
 # ------------------------------------------------------------------ worker
+def _ladder_verdict(job: dict, name: str) -> Verdict:
+    """A ladder job: {"ladder": "module:function", "args": [...]}; the
+    function builds a ladder.LadderJob in this worker, which climbs it."""
+    import importlib
+
+    from . import ladder
+    module, _, fn = job["ladder"].partition(":")
+    build = getattr(importlib.import_module(module), fn)
+    with gpu_window():
+        res = ladder.run_ladder(build(*job.get("args", [])))
+    return Verdict(res.passed, name, {"failed_gate": res.failed_gate, "gates_passed": list(res.gates_passed),
+                                      "detail": res.detail, "info": res.info})
+
+
 def _worker() -> int:
     job = json.loads(sys.stdin.read() or "{}")
     name = job.get("name", "")
     try:
+        if "ladder" in job:
+            print(_ladder_verdict(job, name).to_json(), flush=True)
+            return 0
         with gpu_window():
             from .bundles import artifact
             checks = artifact.validate(Path(job["bundle"]))

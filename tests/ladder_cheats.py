@@ -165,3 +165,43 @@ def atomic_sum_job(candidate, device) -> LadderJob:
     sets = [EvalSet("primary", [[x]])]
     return LadderJob(candidate, row_sum_original, RegionContract.traced(row_sum_original, [x]), sets,
                      exact=False, tolerances=(1e-3, 1e-2))
+
+
+# name -> (job builder on a device, the gate that must stop it); None: passes every gate
+def _spec_job(builder, **kw):
+    return lambda device: rms_norm_job(builder()[0], device, **kw)
+
+
+def _live_output_job(device):
+    g = torch.Generator().manual_seed(5)
+    x, r = (torch.randn(ROWS, DIM, generator=g).bfloat16().to(device) for _ in range(2))
+    w = torch.ones(DIM, dtype=torch.bfloat16, device=device)
+    contract = RegionContract.traced(add_rms_norm_original, [x, r, w])
+    return LadderJob(live_output_dropping()[0], add_rms_norm_original, contract, [EvalSet("primary", [[x, r, w]])])
+
+
+def _cached_job(device):
+    job = rms_norm_job(None, device)
+    job.candidate = cached_by_shape(rms_norm_original(job.eval_sets[0].input_sets[0])[0])[0]
+    job.exact = True
+    return job
+
+
+ZOO = {
+    "correct": (lambda device: rms_norm_job(rms_norm_spec(), device), None),
+    "partial_write": (_spec_job(partial_write), "poison"),
+    "shape_hardcoded": (_spec_job(shape_hardcoded), "sweep"),
+    "stride_lying": (_spec_job(stride_lying), "sweep"),
+    "eps_dropping": (_spec_job(eps_dropping), "smoke"),
+    "fallback_declared_but_dead": (_spec_job(fallback_declared_but_dead), "sweep"),
+    "fallback_missing": (_spec_job(fallback_missing, requires_fallback=True), "static"),
+    "live_output_dropping": (_live_output_job, "static"),
+    "cached_by_shape": (_cached_job, "smoke"),
+    "fp16_sloppy_accumulation": (lambda device: fp16_sum_job(fp16_sloppy_accumulation()[0], device), "smoke"),
+    "atomic_racy": (lambda device: atomic_sum_job(atomic_racy()[0], device), "determinism"),
+}
+
+
+def zoo_job(name: str, device: str = "cuda") -> LadderJob:
+    """The ladder job of a zoo entry (the builder a verification worker calls)."""
+    return ZOO[name][0](device)

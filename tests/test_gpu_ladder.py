@@ -124,3 +124,15 @@ def test_an_original_that_does_not_repeat_fails_before_any_gate(cuda):
     res = _climb(job)
     assert res.failed_gate == "determinism" and res.gates_passed == []
     assert "repeatable" in res.detail["reason"]
+
+
+@pytest.mark.parametrize("name", list(Z.ZOO))
+def test_zoo_map_every_entry_stops_at_its_gate(cuda, name):
+    """The zoo as a map (the reference's CHEATS dict): every entry climbs to
+    exactly the gate it names, the correct kernel to the top."""
+    gate = Z.ZOO[name][1]
+    res = _climb(Z.zoo_job(name))
+    assert res.failed_gate == gate, (name, res.detail)
+    assert res.passed == (gate is None)
+    if gate is not None:
+        assert gate not in res.gates_passed

@@ -9,6 +9,7 @@ import os
 import subprocess
 import sys
 import time
+from pathlib import Path
 
 import pytest
 
@@ -95,3 +96,21 @@ def test_fan_out_stops_after_an_unresponsive_worker():
 def test_worker_without_a_verdict_line_fails():
     vs = verify.fan_out([{"name": "x"}], [0], command=_fake_worker("print('no json here')"))
     assert not vs[0].passed and vs[0].detail["failure"] == "no_verdict"
+
+
+def test_ladder_job_climbs_in_its_own_worker(monkeypatch):
+    """A ladder job names a builder; the worker builds the LadderJob and runs
+    the ladder. Static failures need no GPU, so two zoo cheats stopped at
+    gate 1 check the whole round trip on the host."""
+    tests_dir = str(Path(__file__).resolve().parent)
+    root = str(Path(__file__).resolve().parents[1])
+    monkeypatch.setenv("PYTHONPATH", os.pathsep.join([tests_dir, root, os.environ.get("PYTHONPATH", "")]))
+    jobs = [{"name": n, "ladder": "ladder_cheats:zoo_job", "args": [n, "cpu"]}
+            for n in ("fallback_missing", "live_output_dropping")]
+    vs = verify.fan_out(jobs, [0], timeout_s=300)
+    assert [v.job for v in vs] == ["fallback_missing", "live_output_dropping"]
+    for v in vs:
+        assert not v.passed and v.detail["failed_gate"] == "static", v.detail
+        assert v.detail["gates_passed"] == []
+    assert [f["check"] for f in vs[0].detail["detail"]["failures"]] == ["fallback_missing"]
+    assert "live_output_dropped" in [f["check"] for f in vs[1].detail["detail"]["failures"]]
