@@ -49,7 +49,6 @@ fault a GPU: a wrong candidate only ever gives wrong values.
 """
 from __future__ import annotations
 
-import random
 import re
 from dataclasses import dataclass, field
 from typing import Callable, Sequence
@@ -154,34 +153,40 @@ class LadderResult:
 # ----------------------------------------------------------------- value regimes
 def value_regimes(inputs: Sequence[torch.Tensor], seed: int, weights: Sequence[bool] = (),
                   outlier: float = OUTLIER_VALUE) -> dict:
-    """The adversarial regimes at the recorded shapes (numeric.py:38-78):
-    scaled down by SCALE_DOWN, OUTLIER_COUNT elements set to `outlier`, all
-    zeros, and one leading-axis lane of inf plus another of NaN. Weights and
-    non-float inputs pass through unchanged (their values are the model's
-    constants, indices or masks). Deterministic for a seed."""
-    rng = random.Random(seed)
+    """Each input under the four adversarial regimes, at its recorded shape
+    (the regimes of the reference's ladder, numeric.py:38-78):
+
+      scaled_down  every value times SCALE_DOWN
+      outliers     OUTLIER_COUNT distinct elements replaced by `outlier`
+      zeros        all zeros
+      nonfinite    one leading-axis lane of +inf and a different one of NaN
+                   (a single lane, or a scalar, becomes NaN)
+
+    Model weights and non-float inputs (indices, masks, packed words) are
+    returned as they are in every regime. Positions come from a torch
+    generator seeded with (seed, input index), so a seed fixes them."""
     out = {name: [] for name in REGIMES}
     for k, a in enumerate(inputs):
         if not a.is_floating_point() or a.numel() == 0 or (k < len(weights) and weights[k]):
             for name in REGIMES:
                 out[name].append(a)
             continue
+        gen = torch.Generator().manual_seed(seed * 7919 + k)
         out["scaled_down"].append((a.float() * SCALE_DOWN).to(a.dtype))
-        b = a.clone().reshape(-1)
-        for pos in rng.sample(range(b.numel()), min(OUTLIER_COUNT, b.numel())):
-            b[pos] = outlier
-        out["outliers"].append(b.view(a.shape))
+        spiked = a.clone(memory_format=torch.contiguous_format)
+        flat = spiked.view(-1)
+        picks = torch.randperm(flat.numel(), generator=gen)[:OUTLIER_COUNT].to(flat.device)
+        flat[picks] = outlier
+        out["outliers"].append(spiked)
         out["zeros"].append(torch.zeros_like(a))
-        c = a.clone()
-        if c.dim() == 0:
-            c.fill_(float("nan"))
+        lanes = a.clone()
+        if lanes.dim() == 0:
+            lanes.fill_(float("nan"))
         else:
-            n0 = c.shape[0]
-            i_inf = rng.randrange(n0)
-            i_nan = i_inf if n0 == 1 else (i_inf + 1 + rng.randrange(n0 - 1)) % n0
-            c[i_inf] = float("inf")
-            c[i_nan] = float("nan")
-        out["nonfinite"].append(c)
+            order = torch.randperm(lanes.shape[0], generator=gen).tolist()
+            lanes[order[0]] = float("inf")
+            lanes[order[-1]] = float("nan")   # the same lane when there is only one
+        out["nonfinite"].append(lanes)
     return out
 
 
@@ -231,10 +236,10 @@ def _entry_point_failures(spec, n_inputs: int, n_outputs: int, shapes, where: st
     fails: list[Failure] = []
     cuda = spec.cuda
     if cuda is None:
-        return [Failure("entry_point", f"{where}a plain kernel needs a cuda record")]
+        return [Failure("entry_point", f"{where}no cuda record names an entry point to call")]
     sym = cuda.get("symbol")
     if sym not in _mt.SIGNATURES:
-        return [Failure("entry_point", f"{where}{sym!r} is not a libmt entry point")]
+        return [Failure("entry_point", f"{where}libmt exports no {sym!r}")]
     params = _mt.SIGNATURES[sym][1]
     args = cuda.get("args", [])
     if len(args) != len(params):
@@ -252,81 +257,100 @@ def _entry_point_failures(spec, n_inputs: int, n_outputs: int, shapes, where: st
     return fails
 
 
-def static_check(spec, contract: RegionContract) -> list[Failure]:
-    """Every static failure of a KernelSpec against the region contract
-    (static_checks.py:132-281); empty means gate 1 passes. No GPU work."""
-    if spec.input_signature != contract.input_signature:
-        return [Failure("input_signature", "input specialisation differs from the region contract")]
-    if spec.input_signatures != contract.input_signatures:
-        return [Failure("input_signatures", "input specialisations differ from the region contract")]
-    fails: list[Failure] = []
+def _names(spec, contract: RegionContract, shapes):
     if not _C_IDENTIFIER.match(spec.name):
-        fails.append(Failure("kernel_name", f"{spec.name!r} is not a valid C identifier"))
+        yield Failure("kernel_name", f"name {spec.name!r} cannot be a C symbol")
     if tuple(spec.input_names) != tuple(contract.input_names):
-        fails.append(Failure("input_names", f"kernel inputs {tuple(spec.input_names)} != region inputs "
-                                            f"{tuple(contract.input_names)}"))
-    n_region = len(contract.output_names)
-    head, extras = tuple(spec.output_names[:n_region]), tuple(spec.output_names[n_region:])
-    if head != tuple(contract.output_names) or not all(_TMP.match(e) for e in extras):
-        fails.append(Failure("output_names", f"kernel outputs {tuple(spec.output_names)} must start with the "
-                                             f"region outputs {tuple(contract.output_names)}, extras all tmp<N>"))
+        yield Failure("input_names", f"inputs {tuple(spec.input_names)}; the region's are "
+                                     f"{tuple(contract.input_names)}")
+    k = len(contract.output_names)
+    extras = spec.output_names[k:]
+    if tuple(spec.output_names[:k]) != tuple(contract.output_names) or any(not _TMP.match(e) for e in extras):
+        yield Failure("output_names", f"outputs {tuple(spec.output_names)}: the region's "
+                                      f"{tuple(contract.output_names)} first, then only tmp<N> scratch")
     for name in contract.live_outputs:
         if name not in spec.output_names:
-            fails.append(Failure("live_output_dropped", f"live value {name!r} is neither produced nor listed "
-                                                        "as an output"))
-    n_out = len(spec.output_names)
-    if len(spec.output_shapes) != n_out or len(spec.output_dtypes) != n_out:
-        fails.append(Failure("output_arity", f"{n_out} output names but {len(spec.output_shapes)} shape tuples "
-                                             f"and {len(spec.output_dtypes)} dtypes"))
+            yield Failure("live_output_dropped", f"{name!r} is read after the region but the spec never "
+                                                 "writes it")
+
+
+def _outputs(spec, contract: RegionContract, shapes):
+    n = len(spec.output_names)
+    if (len(spec.output_shapes), len(spec.output_dtypes)) != (n, n):
+        yield Failure("output_arity", f"{len(spec.output_shapes)} shapes and {len(spec.output_dtypes)} dtypes "
+                                      f"for {n} outputs")
     for name, dt, want in zip(spec.output_names, spec.output_dtypes, contract.output_dtypes):
         if _resolved_dtype(dt, contract) != want:
-            fails.append(Failure("output_dtype", f"output {name!r}: {dt} != boundary dtype {want}"))
-    for name, exprs, want in zip(spec.output_names, spec.output_shapes, contract.output_ranks):
-        if len(exprs) != want:
-            fails.append(Failure("output_rank", f"output {name!r}: {len(exprs)} shape expressions, "
-                                                f"region rank is {want}"))
-    shapes = [tuple(s) for s in contract.input_shapes] or [(4,) * r for r in contract.input_ranks]
+            yield Failure("output_dtype", f"{name!r} would be {dt}; the region produces {want}")
+    for name, exprs, rank in zip(spec.output_names, spec.output_shapes, contract.output_ranks):
+        if len(exprs) != rank:
+            yield Failure("output_rank", f"{name!r} has {len(exprs)} extents; the region's value has rank {rank}")
+    probes: list[Failure] = []
     for j, exprs in enumerate(spec.output_shapes):
         for i, text in enumerate(exprs):
-            _probe(f"output_shapes[{j}][{i}]", text, shapes, fails)
+            _probe(f"output_shapes[{j}][{i}]", text, shapes, probes)
+    yield from probes
     for name, exprs, want in zip(spec.output_names, spec.output_shapes, contract.output_shapes):
         try:
             got = tuple(Expr(e).evaluate(shapes) for e in exprs)
         except (GrammarError, ArithmeticError):
-            continue  # reported by the probe
+            continue  # the probe above names it
         if got != tuple(want):
-            fails.append(Failure("output_shape", f"output {name!r}: the expressions give {got} at the traced "
-                                                 f"size, the region records {tuple(want)}"))
-    if spec.fallback_predicate is not None:
-        _probe("fallback_predicate", spec.fallback_predicate, shapes, fails)
-        if contract.input_shapes:
-            try:
-                if Expr(spec.fallback_predicate).evaluate(shapes):
-                    fails.append(Failure("fallback_on_primary", "fallback_predicate is true on the primary "
-                                         "workload: true hands the call to the original ops"))
-            except (GrammarError, ArithmeticError):
-                pass
-    elif contract.requires_fallback:
-        fails.append(Failure("fallback_missing", "shape-specialised kernel declares no fallback predicate"))
-    if spec.stages:
-        from .autotuner_runtime.stages import StageError, build_graph
-        try:
-            graph = build_graph(spec)
-            dtypes = [_kernels.DTYPES[d] for d in contract.input_dtypes]
-            per_stage, outs = graph.walk_shapes(shapes, dtypes)
-            want = list(zip((tuple(s) for s in contract.output_shapes),
-                            (_kernels.DTYPES[d] for d in contract.output_dtypes)))
-            if contract.output_shapes and [(tuple(s), d) for s, d in outs][:n_region] != want:
-                fails.append(Failure("stage_boundary", "stage results must match every region output shape "
-                                                       "and dtype"))
-            for i, (kernel, ins, outs_i) in enumerate(per_stage):
-                fails.extend(_entry_point_failures(kernel, len(ins), len(outs_i), [s for s, _ in ins],
-                                                   where=f"stage {i}: "))
-        except (StageError, ValueError, ArithmeticError, GrammarError) as e:
-            fails.append(Failure("stages", str(e)))
-    else:
-        fails.extend(_entry_point_failures(spec, len(spec.input_names), n_out, shapes))
-    return fails
+            yield Failure("output_shape", f"{name!r} evaluates to {got} at the traced inputs; the region's is "
+                                          f"{tuple(want)}")
+
+
+def _fallback(spec, contract: RegionContract, shapes):
+    if spec.fallback_predicate is None:
+        if contract.requires_fallback:
+            yield Failure("fallback_missing", "the candidate serves only some shapes and names no fallback "
+                                              "predicate for the rest")
+        return
+    probes: list[Failure] = []
+    _probe("fallback_predicate", spec.fallback_predicate, shapes, probes)
+    yield from probes
+    if probes or not contract.input_shapes:
+        return
+    try:
+        on_primary = bool(Expr(spec.fallback_predicate).evaluate(shapes))
+    except (GrammarError, ArithmeticError):
+        return
+    if on_primary:
+        yield Failure("fallback_on_primary", "the fallback predicate holds on the primary workload, so the "
+                                             "candidate would never run where it is measured")
+
+
+def _launch(spec, contract: RegionContract, shapes):
+    if not spec.stages:
+        yield from _entry_point_failures(spec, len(spec.input_names), len(spec.output_names), shapes)
+        return
+    from .autotuner_runtime.stages import StageError, build_graph
+    try:
+        per_stage, outs = build_graph(spec).walk_shapes(shapes, [_kernels.DTYPES[d] for d in contract.input_dtypes])
+    except (StageError, ValueError, ArithmeticError, GrammarError) as e:
+        yield Failure("stages", str(e))
+        return
+    k = len(contract.output_names)
+    want = [(tuple(sh), _kernels.DTYPES[d]) for sh, d in zip(contract.output_shapes, contract.output_dtypes)]
+    if contract.output_shapes and [(tuple(sh), d) for sh, d in outs][:k] != want:
+        yield Failure("stage_boundary", "the last stages do not produce the region's output shapes and dtypes")
+    for i, (kernel, ins, outs_i) in enumerate(per_stage):
+        yield from _entry_point_failures(kernel, len(ins), len(outs_i), [sh for sh, _ in ins], where=f"stage {i}: ")
+
+
+_STATIC_CHECKS = (_names, _outputs, _fallback, _launch)
+
+
+def static_check(spec, contract: RegionContract) -> list[Failure]:
+    """Gate 1 (the reference's static_checks.py:132-281): everything a
+    KernelSpec can be checked for against the region contract without a GPU,
+    as a list of named failures; empty means the gate passes. A spec pinned
+    to other input shapes than the contract's fails on that alone."""
+    if (spec.input_signature, spec.input_signatures) != (contract.input_signature, contract.input_signatures):
+        return [Failure("input_signature", "the spec pins input shapes other than those the region was "
+                                           "traced with")]
+    shapes = [tuple(sh) for sh in contract.input_shapes] or [(4,) * r for r in contract.input_ranks]
+    return [f for check in _STATIC_CHECKS for f in check(spec, contract, shapes)]
 
 
 # ----------------------------------------------------------------- gates 2-8
@@ -344,7 +368,7 @@ def _original_outputs(job: LadderJob, inputs, n_out: int) -> list:
     first = [t.clone() for t in list(job.original(list(inputs)))[:n_out]]
     again = list(job.original(list(inputs)))[:n_out]
     if len(first) != len(again) or not all(bitwise_equal(a, b) for a, b in zip(first, again)):
-        raise _OriginalUnstable("the region's original ops are not bitwise repeatable")
+        raise _OriginalUnstable("two runs of the region's original ops gave different bits: it is not repeatable")
     return first
 
 
@@ -382,14 +406,14 @@ def _run(job: LadderJob) -> LadderResult:
     def launch(inputs) -> list:
         if spec is not None:
             if _kernels.fallback_fires(spec, list(inputs)):
-                raise _Rejected("fallback_on_workload: this workload selects the original ops instead "
-                                "of the candidate")
+                raise _Rejected("fallback_on_workload: the fallback predicate sends a measured workload back "
+                                "to the original ops")
             return list(_kernels.call(spec, list(inputs), init_value=nan))[:n_out]
         return list(job.candidate(list(inputs), nan))
 
     def mismatch(got, want) -> dict | None:
         if len(got) != len(want):
-            return {"reason": "output count changed", "got": len(got), "want": len(want)}
+            return {"reason": f"{len(got)} outputs where the region has {len(want)}"}
         for name, g, w in zip(out_names, got, want):
             rtol, atol = numeric.tolerance_for(w.dtype, job.tolerances)
             r = numeric.check(g, w, exact=exact, rtol=rtol, atol=atol)
@@ -475,7 +499,7 @@ def _run(job: LadderJob) -> LadderResult:
                     break
             if found is None:
                 info.setdefault("regime_skipped", {})[regime] = \
-                    "the original's own output overflows at every magnitude tried"
+                    "no outlier magnitude left the original's outputs finite where they were finite"
                 continue
             rin, ref, magnitude = found
             if magnitude is not None:
