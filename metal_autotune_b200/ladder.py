@@ -242,9 +242,10 @@ def _entry_point_failures(spec, n_inputs: int, n_outputs: int, shapes, where: st
         return [Failure("entry_point", f"{where}libmt exports no {sym!r}")]
     params = _mt.SIGNATURES[sym][1]
     args = cuda.get("args", [])
-    if len(args) != len(params):
+    bound = sum(2 if "workspace" in a else 1 for a in args)  # a workspace is a pointer and its size
+    if bound != len(params):
         fails.append(Failure("entry_point", f"{where}{sym} takes {len(params)} arguments, "
-                                            f"the record binds {len(args)}"))
+                                            f"the record binds {bound}"))
     for j, a in enumerate(args):
         if "in" in a and not 0 <= int(a["in"]) < n_inputs:
             fails.append(Failure("entry_point", f"{where}argument {j} binds input {a['in']}; "

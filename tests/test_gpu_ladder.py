@@ -136,3 +136,39 @@ def test_zoo_map_every_entry_stops_at_its_gate(cuda, name):
     assert res.passed == (gate is None)
     if gate is not None:
         assert gate not in res.gates_passed
+
+
+def test_qwen3_gate_up_kernel_climbs_every_gate(cuda):
+    """The hot path's heaviest region (gate/up projections + SwiGLU, 4-bit
+    g64, Qwen3-4B widths) through the ladder against its original ops
+    (MLX-affine dequantisation, two matmuls, SwiGLU with each op rounded):
+    prefill and decode sizes, the qmv dispatch at one row and a ragged row
+    count in the sweep."""
+    from metal_autotune_b200 import workload
+    from metal_autotune_b200.bundles import qwen3_specs
+    from metal_autotune_b200.targets import qwen3
+
+    spec = next(s for s in qwen3_specs() if s.kernel_id == "gate_up_swiglu")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    wg = workload.random_quantized(9728, 2560, generator=g)
+    wu = workload.random_quantized(9728, 2560, generator=g)
+
+    def original(inputs):
+        x, gw, gs, gb, uw, us, ub = inputs
+        gate = torch.matmul(x, workload.dequantize(gw, gs, gb, 64, 4).t())
+        up = torch.matmul(x, workload.dequantize(uw, us, ub, 64, 4).t())
+        return [qwen3._swiglu(gate, up)]
+
+    def inputs(rows, seed):
+        x = torch.randn(rows, 2560, generator=torch.Generator().manual_seed(seed)).bfloat16().cuda()
+        return [x, *wg, *wu]
+
+    sets = [L.EvalSet("prefill128", [inputs(128, 0), inputs(128, 1)]),
+            L.EvalSet("rows16", [inputs(16, 2)]),
+            L.EvalSet("rows300", [inputs(300, 3)], correctness_only=True),
+            L.EvalSet("decode1", [inputs(1, 4)], correctness_only=True)]
+    contract = L.RegionContract.traced(original, sets[0].input_sets[0])
+    res = _climb(L.LadderJob(spec, original, contract, sets, weights=(False,) + (True,) * 6))
+    assert res.passed, (res.failed_gate, res.detail)
+    assert res.gates_passed == ALL
+    assert res.info["timing"]["candidate_ms"] < res.info["timing"]["original_ms"]

@@ -150,3 +150,22 @@ def test_transposed_layout_keeps_values_and_storage_size():
     assert torch.equal(xt, x) and not xt.is_contiguous() and xt.stride() == (1, 5)
     assert xt.untyped_storage().nbytes() == x.untyped_storage().nbytes()
     assert L.transposed_layout([w])[1] is False
+
+
+def test_every_committed_bundle_spec_binds_its_entry_point():
+    """Gate 1's entry-point check on every launch record the bundles ship:
+    the symbol exists and the record binds each of its parameters (a
+    workspace binds two: pointer and size)."""
+    from pathlib import Path
+
+    from metal_autotune_b200.autotuner_runtime.kernels import load_spec
+    bundles = Path(L.__file__).resolve().parent / "bundles"
+    paths = sorted(bundles.glob("*/kernels/*.launch.json"))
+    assert paths
+    for path in paths:
+        spec = load_spec(path)
+        kernels = [st.kernel for st in spec.stages] if spec.stages else [spec]
+        for k in kernels:
+            bad = [f for f in L._entry_point_failures(k, len(k.input_names), len(k.output_names), [])
+                   if f.check == "entry_point"]
+            assert bad == [], (path.name, bad)
