@@ -92,6 +92,14 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append((time.time(), line.strip()))
 
+    def wait_first_sample(self, timeout_s: float = 5.0):
+        """Block until nvidia-smi has reported once: it takes a few hundred
+        ms to start, longer than a short timed region (5 tensor-parallel
+        forwards at tp 8 take under 0.5 s)."""
+        t_end = time.time() + timeout_s
+        while self.proc is not None and not self.lines and time.time() < t_end:
+            time.sleep(0.01)
+
     def mark_start(self):
         self.timed[0] = time.time()
 
@@ -624,6 +632,7 @@ def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local, overlap=True):
     torch.cuda.synchronize()
     calls0 = lib.CALLS[0]
     with ClockSampler(local) as clk:
+        clk.wait_first_sample()
         clk.mark_start()
         ms_total = time_region(step, steps, world)
         clk.mark_end()
@@ -888,6 +897,7 @@ def run_model_line(args):
         step.replay()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        clk.wait_first_sample()
         soak(step.replay, 0.3)
         clk.mark_start()
         ms_total = time_region(step.replay, args.steps, world)
@@ -1003,6 +1013,7 @@ def main():
         log(f"launch list: {args.steps} request(s) of {req.launches_per_step} launches")
         return 0
     with ClockSampler(local) as clk:
+        clk.wait_first_sample()
         soak(req.replay, 0.5)
         clk.mark_start()
         ms_total = time_region(req.replay, args.steps, world)
