@@ -31,6 +31,9 @@ stops:
                same values, column-major storage)
   determinism  three re-poisoned runs bitwise identical, then the numeric
                rule on the primary set
+  clock        (scoring phase, LadderJob.clock) original and candidate timed
+               as interleaved loops; never fails, records whether the
+               candidate ships (a resolved win over the original)
 
 The numeric rule is exact (bit for bit) for a spec that keeps the original's
 evaluation order and within tolerance for one that reassociates
@@ -50,6 +53,7 @@ fault a GPU: a wrong candidate only ever gives wrong values.
 from __future__ import annotations
 
 import re
+import statistics
 from dataclasses import dataclass, field
 from typing import Callable, Sequence
 
@@ -65,6 +69,12 @@ GATES = ("static", "compile", "poison", "watchdog", "smoke", "workloads", "sweep
 DETERMINISM_RUNS = 3
 WATCHDOG_FACTOR = 20.0
 WATCHDOG_ITERS = 4
+# the scoring phase's ninth gate (child.py:436-492): always passed, it records
+# whether the candidate resolves as faster than the original
+CLOCK_GATE = "clock"
+CLOCK_PAIRS = 4          # ABBA / BAAB blocks
+CLOCK_TARGET_MS = 20.0   # each timed arm is a loop of about this long
+CLOCK_MARGIN = 0.01      # a win must beat 1% of the original's time (and 3 standard errors)
 
 SCALE_DOWN = 1e-4
 OUTLIER_VALUE = 1e4    # fits fp16 (max 65504)
@@ -139,6 +149,7 @@ class LadderJob:
     tolerances: tuple | None = None         # (rtol, atol); None: per-output dtype defaults
     exact: bool | None = None               # None: exact unless the spec reassociates
     seed: int = 0
+    clock: bool = False                     # scoring phase: run the clock gate after determinism
 
 
 @dataclass
@@ -568,4 +579,35 @@ def _run(job: LadderJob) -> LadderResult:
     if bad:
         return fail("determinism", {**bad, "eval_set": primary.label, "kind": "numeric"})
     passed.append("determinism")
+
+    # gate 9, clock (scoring phase only): the original and the candidate as
+    # loops over the primary set's input sets in turn, interleaved ABBA / BAAB
+    # in one measurement session; the candidate ships when its median gain
+    # beats max(CLOCK_MARGIN of the original's time, 3 standard errors)
+    if job.clock:
+        from .autotuner_runtime import measure
+        sets = [list(x) for x in primary.input_sets]
+        turn = [0]
+
+        def arm(fn):
+            def one():
+                fn(sets[turn[0] % len(sets)])
+                turn[0] += 1
+            return one
+
+        cand_one = arm((lambda inputs: _kernels.call(spec, inputs)) if spec is not None
+                       else (lambda inputs: job.candidate(inputs, None)))
+        orig_one = arm(job.original)
+        single = measure.time_steps(orig_one, 4) / 4
+        iters = measure.loop_iterations(single, CLOCK_TARGET_MS)
+        comp = measure.compare(measure.Session(), measure.chained_loop(orig_one, iters),
+                               measure.chained_loop(cand_one, iters), pairs=CLOCK_PAIRS)
+        margin = CLOCK_MARGIN * comp.median_baseline_ms
+        info.setdefault("timing", {}).update({
+            "library_ms": comp.median_baseline_ms,
+            "region_ms": statistics.median(comp.candidate_ms),
+            "win_ms": comp.median_delta_ms, "sigma_ms": comp.sigma_ms,
+            "clock_iters": iters, "clock_sets": len(sets), "clock_deltas": comp.n})
+        info.update({"ship": comp.wins_by(margin), "margin_ms": max(margin, 3.0 * comp.sigma_ms)})
+        passed.append(CLOCK_GATE)
     return LadderResult(True, None, {}, passed, info)

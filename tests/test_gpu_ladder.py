@@ -168,7 +168,24 @@ def test_qwen3_gate_up_kernel_climbs_every_gate(cuda):
             L.EvalSet("rows300", [inputs(300, 3)], correctness_only=True),
             L.EvalSet("decode1", [inputs(1, 4)], correctness_only=True)]
     contract = L.RegionContract.traced(original, sets[0].input_sets[0])
-    res = _climb(L.LadderJob(spec, original, contract, sets, weights=(False,) + (True,) * 6))
+    res = _climb(L.LadderJob(spec, original, contract, sets, weights=(False,) + (True,) * 6, clock=True))
     assert res.passed, (res.failed_gate, res.detail)
-    assert res.gates_passed == ALL
+    assert res.gates_passed == ALL + [L.CLOCK_GATE]
+    # one fused launch against dequantising 50 M weights and two GEMMs: a resolved win
+    assert res.info["ship"] is True, res.info["timing"]
     assert res.info["timing"]["candidate_ms"] < res.info["timing"]["original_ms"]
+
+
+def test_clock_gate_scores_a_passing_candidate(cuda):
+    """The scoring phase: after determinism the clock gate times the original
+    and the candidate as interleaved loops over the primary set's input sets
+    and records the ship decision (both arms are launch-bound at this size, so
+    the decision itself is not asserted here)."""
+    job = Z.rms_norm_job(Z.rms_norm_spec(), "cuda")
+    job.clock = True
+    res = _climb(job)
+    assert res.passed and res.gates_passed == ALL + [L.CLOCK_GATE], res.detail
+    t = res.info["timing"]
+    assert t["clock_sets"] == 2 and t["clock_deltas"] == L.CLOCK_PAIRS
+    assert t["region_ms"] > 0 and t["library_ms"] > 0 and t["clock_iters"] >= 1
+    assert isinstance(res.info["ship"], bool) and res.info["margin_ms"] > 0
