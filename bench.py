@@ -249,13 +249,13 @@ class Request:
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
-        before = lib.CALLS[0]
+        before = lib.kernel_launches()
         with torch.cuda.graph(self.graph):
             self.out = self.eager()
             # the three results in one buffer, so e2e reads them back with one copy
             self.res_dev = torch.cat([self.out[0].view(1), self.out[1].view(1),
                                       self.out[2].view(torch.int32).view(1)])
-        self.launches_per_step = lib.CALLS[0] - before
+        self.launches_per_step = lib.kernel_launches() - before
 
     def replay(self):
         self.graph.replay()
@@ -630,14 +630,14 @@ def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local, overlap=True):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    calls0 = lib.CALLS[0]
+    calls0 = lib.kernel_launches()
     with ClockSampler(local) as clk:
         clk.wait_first_sample()
         clk.mark_start()
         ms_total = time_region(step, steps, world)
         clk.mark_end()
         ms_e2e_total = time_region(e2e_step, steps, world)
-    launches = lib.CALLS[0] - calls0
+    launches = lib.kernel_launches() - calls0
     ms = max_over_ranks(ms_total / steps, world)
     ms_e2e = max_over_ranks(ms_e2e_total / steps, world)
     status = lib.device_status(clear=True)
@@ -782,11 +782,11 @@ class ModelStep:
             self.model(self.x)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
-        before = lib.CALLS[0]
+        before = lib.kernel_launches()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             out = self.model(self.x)
-        self.launches_per_step = lib.CALLS[0] - before
+        self.launches_per_step = lib.kernel_launches() - before
         self.out = out[0] if isinstance(out, tuple) else out  # the pick for Mamba, the activations otherwise
         self.host_out = torch.empty_like(self.out, device="cpu").pin_memory()
         # A forward of a few microseconds replays faster on the GPU than the host can launch graphs, so

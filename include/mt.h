@@ -77,6 +77,14 @@ int mt_device_status(int* status_out, int clear);
 /* Number of streaming multiprocessors of the current device (host query). */
 int mt_sm_count(int* sm_count_out);
 
+/*
+ * Kernels this library has launched in the process so far: a host-side count
+ * of successful launches (one entry point may launch several kernels; a
+ * launch recorded into a CUDA graph counts once, when it is captured).
+ * Library plumbing, no reference counterpart.
+ */
+uint64_t mt_kernel_launches(void);
+
 /* ------------------------------------------------------------------------ */
 /* a-1 / a-2: MLX-affine quantized matmul, y = x · dequant(w)^T              */
 /* ------------------------------------------------------------------------ */
@@ -98,8 +106,12 @@ int mt_sm_count(int* sm_count_out);
  * bits = 4 or 8; K a multiple of group_size and of 128 / bits * 8.
  * M <= 8 runs the vector kernel (qmv); larger M the tcgen05/TMEM kernel,
  * which may split K and then needs `workspace` (see mt_qmm_workspace_bytes;
- * the workspace must be zero-filled once before first use and is left
- * zeroed by every call that completes).
+ * the workspace must be zero-filled once before first use, and every call
+ * that completes leaves the counters at its start zeroed). From 1024 rows of
+ * x (environment variable MT_QMM_GEMM_MIN_ROWS overrides it), given the
+ * workspace mt_qmm_workspace_bytes asks for, the weights are dequantised into
+ * the workspace past those counters and multiplied on the tcgen05 GEMM of
+ * mt_linear: same dequantised values, fp32 sums in another order.
  * A product whose x rows or weight rows exceed an L2-sized block (60 MB of
  * operand bytes; environment variable MT_QMM_L2_BLOCK_BYTES overrides it) is
  * issued as several launches on `stream`, one per block, reusing the same
@@ -205,7 +217,11 @@ int mt_rms_norm_quantized_matmul_swiglu(
 /*
  * Bytes of workspace the quantized-matmul entry points need for this shape.
  * `n_total` is the summed N over all sets (2N for the SwiGLU pair);
- * `kind` is 0 (plain/residual/multi) or 1 (SwiGLU pair).
+ * `kind` is 0 (plain/residual/multi) or 1 (SwiGLU pair). From M = 1024 rows
+ * up it includes room for one set's dequantised weights (n_total*K elements)
+ * and, for the SwiGLU pair, its two [M, N] products: those shapes dequantise
+ * the weights once and multiply on the tcgen05 GEMM. Given less than this,
+ * they run the fused kernel instead.
  */
 size_t mt_qmm_workspace_bytes(int64_t M, int64_t n_total, int64_t K, int bits,
                               int kind);

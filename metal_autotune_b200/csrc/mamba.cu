@@ -384,6 +384,7 @@ int mt_causal_conv1d(const void* x, const void* weight, const void* bias, void* 
     default: conv_state_kernel<MT_F32><<<g2, 256, 0, s>>>(x, conv_state, (int)L, (int)C, width); break;
   }
   MT_CUDA(cudaGetLastError());
+  count_launch();
   return MT_OK;
 }
 

@@ -142,6 +142,8 @@ extern "C" {
 
 int mt_version(void) { return (0 << 16) | (1 << 8) | 0; }
 
+uint64_t mt_kernel_launches(void) { return mt::g_kernel_launches.load(std::memory_order_relaxed); }
+
 const char* mt_last_error_string(void) { return mt::g_err; }
 
 int mt_device_status(int* status_out, int clear) {

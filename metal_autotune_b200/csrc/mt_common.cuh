@@ -1,6 +1,7 @@
 // Shared device/host helpers for libmt.so (sm_100a only).
 #pragma once
 
+#include <atomic>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -37,6 +38,11 @@ int cuda_fail(cudaError_t e, const char* what);
     if (e_ != cudaSuccess) return ::mt::cuda_fail(e_, #call); \
   } while (0)
 
+// Kernels this library has launched in the process (successful launches; a
+// launch recorded into a CUDA graph counts once, when it is captured).
+inline std::atomic<unsigned long long> g_kernel_launches{0};
+inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+
 // Launch with programmatic dependent launch enabled: the kernel may begin
 // while its predecessor on the stream finishes; every kernel in this library
 // calls griddep_wait() before it touches memory a predecessor may write or
@@ -56,6 +62,7 @@ inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+  count_launch();
   return MT_OK;
 }
 
@@ -79,6 +86,7 @@ inline int launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   cfg.numAttrs = cluster > 1 ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+  count_launch();
   return MT_OK;
 }
 

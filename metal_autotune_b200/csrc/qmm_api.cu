@@ -118,12 +118,147 @@ static int run_tc_blocked(const QmmRequest& r, cudaStream_t stream) {
   return MT_OK;
 }
 
+// ---------------------------------------------------------------- many rows
+// From kGemmMinRows rows of x up, the weights are dequantised once into the
+// workspace (MLX rounding, the same dequant_chunk as the fused kernels) and
+// the product runs on the tcgen05 bf16/f16 GEMM of the dense path. The fused
+// kernel dequantises every weight tile once per 128-token tile, so at large M
+// its dequantiser warps bound it near a third of the tensor peak; one
+// HBM-bound dequantisation pass (read N*K*bits/8, write N*K*2 bytes) plus a
+// GEMM near 80% of the peak is the faster form there (Llama-3-8B prefill,
+// M = 16384, 8-bit: gate 1.49 vs 3.68 ms, down 1.44 vs 3.92 ms). The products
+// are the same dequantised weights times x, accumulated in fp32 in another
+// order. MT_QMM_GEMM_MIN_ROWS overrides the threshold (tests use it to compare
+// both forms).
+constexpr int64_t kGemmMinRows = 1024;
+
+static int64_t gemm_min_rows() {
+  const char* e = getenv("MT_QMM_GEMM_MIN_ROWS");
+  const long long v = e ? atoll(e) : 0;
+  return v > 0 ? static_cast<int64_t>(v) : kGemmMinRows;
+}
+
+int gemm_tc_run(const void* x, const void* w, const void* bias, const void* residual, void* y, int64_t B,
+                int64_t L, int64_t Cin, int64_t Cout, int taps, int stride, int padding, int act, int dtype,
+                int bias_fused, int64_t ldy, cudaStream_t stream);
+
+// One thread per 16-byte chunk of packed weights (32 values at 4 bits, 16 at
+// 8): out[n, k] = round(round(s * q) + b), rows of K values.
+template <int DT, int BITS>
+__global__ void __launch_bounds__(256) dequant_rows_kernel(const uint8_t* __restrict__ w,
+                                                           const uint16_t* __restrict__ s,
+                                                           const uint16_t* __restrict__ b,
+                                                           uint4* __restrict__ out, int64_t N, int K, int G,
+                                                           int gshift) {
+  constexpr int kVals = 128 / BITS;  // values per chunk
+  // the previous kernel on the stream may still read `out` (the GEMM of the
+  // set before, which shares this buffer)
+  griddep_wait();
+  griddep_launch();
+  const int64_t per_row = K / kVals;
+  const int64_t total = N * per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t n = i / per_row;
+    const int c = static_cast<int>(i - n * per_row);
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + n * (K * BITS / 8)) + c);
+    const int g = (c * kVals) >> gshift;
+    const uint16_t sb = __ldg(s + n * G + g), bb = __ldg(b + n * G + g);
+    float sf, bf;
+    if constexpr (DT == MT_BF16) {
+      sf = __uint_as_float(static_cast<uint32_t>(sb) << 16);
+      bf = __uint_as_float(static_cast<uint32_t>(bb) << 16);
+    } else {
+      sf = __half2float(__ushort_as_half(sb));
+      bf = __half2float(__ushort_as_half(bb));
+    }
+    uint32_t o[kVals / 2];
+    dequant_chunk<DT, BITS>(wv, sf, bf, o);
+    uint4* dst = out + (n * K + static_cast<int64_t>(c) * kVals) / 8;
+#pragma unroll
+    for (int v = 0; v < kVals / 8; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+  }
+}
+
+static int dequant_rows(const QmmSetReq& q, int64_t K, int group, int bits, int dtype, void* out,
+                        cudaStream_t stream) {
+  int sms = 148;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const int64_t chunks = q.N * (K * bits / 128);
+  const int64_t want = (chunks + 255) / 256;
+  const dim3 grid(static_cast<unsigned>(want < sms * 16 ? want : sms * 16));
+  const int G = static_cast<int>(K / group), gshift = group == 32 ? 5 : group == 64 ? 6 : 7;
+  const auto* w = reinterpret_cast<const uint8_t*>(q.w);
+  const auto* s = static_cast<const uint16_t*>(q.s);
+  const auto* b = static_cast<const uint16_t*>(q.b);
+  auto* o = static_cast<uint4*>(out);
+  const int k = static_cast<int>(K);
+  if (dtype == MT_BF16)
+    return bits == 4 ? launch(dequant_rows_kernel<MT_BF16, 4>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift)
+                     : launch(dequant_rows_kernel<MT_BF16, 8>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift);
+  return bits == 4 ? launch(dequant_rows_kernel<MT_F16, 4>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift)
+                   : launch(dequant_rows_kernel<MT_F16, 8>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift);
+}
+
+// The path's buffers sit past the fused kernel's workspace area, whose
+// counters the fused kernel expects to find zeroed.
+static size_t gemm_ws_offset(int64_t M, int64_t n_total, int64_t K, int bits, int kind) {
+  return (qmm_tc_workspace(M, n_total, K, bits, kind) + 4095) / 4096 * 4096;
+}
+static size_t gemm_ws_bytes(int64_t M, int64_t n_total, int64_t K, int kind) {
+  // one set's dequantised weights (n_total bounds every set), and for SwiGLU
+  // the gate and up products
+  return static_cast<size_t>(n_total) * K * 2 + (kind == 1 ? static_cast<size_t>(M) * n_total * 2 : 0);
+}
+
+// MT_ERR_UNSUPPORTED (nothing written) when the request does not fit this
+// path: the caller then runs the fused kernel.
+static int run_dequant_gemm(const QmmRequest& r, cudaStream_t stream) {
+  const bool dual = r.kind == QMM_SWIGLU;
+  int64_t n_total = 0;
+  for (int s = 0; s < 3; ++s) n_total += r.set[s].N;
+  const int kind = dual ? 1 : 0;
+  const size_t off = gemm_ws_offset(r.M, n_total, r.K, r.bits, kind);
+  if (!r.ws || r.ws_bytes < off + gemm_ws_bytes(r.M, n_total, r.K, kind)) return MT_ERR_UNSUPPORTED;
+  if (dual && r.set[0].ldy > 0 && r.set[0].ldy != r.set[0].N) return MT_ERR_UNSUPPORTED;
+  char* wbuf = static_cast<char*>(r.ws) + off;
+  const int64_t esz = 2;
+  if (dual) {
+    const int64_t N = r.set[0].N;
+    char* tmp_g = wbuf + static_cast<size_t>(n_total) * r.K * esz;
+    char* tmp_u = tmp_g + static_cast<size_t>(r.M) * N * esz;
+    void* tmps[2] = {tmp_g, tmp_u};
+    for (int s = 0; s < 2; ++s) {
+      if (int rc = dequant_rows(r.set[s], r.K, r.group, r.bits, r.dtype, wbuf, stream)) return rc;
+      if (int rc = gemm_tc_run(r.x, wbuf, nullptr, nullptr, tmps[s], 1, r.M, r.K, N, 1, 1, 0, 0, r.dtype, 1, N,
+                               stream))
+        return rc;
+    }
+    return mt_swiglu(tmp_g, tmp_u, r.set[0].y, r.M * N, r.dtype, stream);
+  }
+  for (int s = 0; s < 3; ++s) {
+    const QmmSetReq& q = r.set[s];
+    if (q.N == 0) continue;
+    const int64_t ldy = q.ldy > 0 ? q.ldy : q.N;
+    if (int rc = dequant_rows(q, r.K, r.group, r.bits, r.dtype, wbuf, stream)) return rc;
+    const void* res = r.kind == QMM_RESIDUAL ? r.residual : nullptr;
+    if (int rc = gemm_tc_run(r.x, wbuf, nullptr, res, q.y, 1, r.M, r.K, q.N, 1, 1, 0, 0, r.dtype, 1, ldy, stream))
+      return rc;
+  }
+  return MT_OK;
+}
+
 static int run(const QmmRequest& r, cudaStream_t stream, const char* who) {
   clear_error();
   const int rc = check_common(r, who);
   if (rc != MT_OK) return rc;
   if (r.M == 0) return MT_OK;
   if (r.M <= kQmvMaxRows) return qmv_run(r, stream);
+  if (r.M >= gemm_min_rows()) {
+    const int g = run_dequant_gemm(r, stream);
+    if (g != MT_ERR_UNSUPPORTED) return g;
+    clear_error();
+  }
   return run_tc_blocked(r, stream);
 }
 
@@ -284,6 +419,8 @@ int mt_rms_norm_quantized_matmul_swiglu(const void* x, const void* norm_w, float
 
 size_t mt_qmm_workspace_bytes(int64_t M, int64_t n_total, int64_t K, int bits, int kind) {
   if (M <= kQmvMaxRows) return 0;
+  if (M >= gemm_min_rows() && kind <= 1)
+    return gemm_ws_offset(M, n_total, K, bits, kind) + gemm_ws_bytes(M, n_total, K, kind);
   return qmm_tc_workspace(M, n_total, K, bits, kind);
 }
 

@@ -56,6 +56,7 @@ P, I64, I32, F32, SZ = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
 # symbol -> (restype, argtypes), in include/mt.h order
 SIGNATURES = {
     "mt_version": (C.c_int, []),
+    "mt_kernel_launches": (C.c_uint64, []),
     "mt_last_error_string": (C.c_char_p, []),
     "mt_device_status": (C.c_int, [C.POINTER(C.c_int), I32]),
     "mt_sm_count": (C.c_int, [C.POINTER(C.c_int)]),
@@ -122,6 +123,12 @@ def load(path: str | Path | None = None) -> C.CDLL:
             fn.argtypes = args
         _lib = lib
         return lib
+
+
+def kernel_launches() -> int:
+    """Kernels libmt has launched in this process (host-side count; a launch
+    captured into a CUDA graph counts once)."""
+    return int(load().mt_kernel_launches())
 
 
 def dtype_code(dt: torch.dtype) -> int:

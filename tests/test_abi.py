@@ -17,7 +17,7 @@ def declared() -> dict[str, int]:
     """name -> parameter count of every function declared in mt.h."""
     text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
     out = {}
-    for m in re.finditer(r"\b(?:int|size_t|const char\s*\*)\s+(mt_\w+)\s*\(([^)]*)\)\s*;", text):
+    for m in re.finditer(r"\b(?:int|size_t|uint64_t|const char\s*\*)\s+(mt_\w+)\s*\(([^)]*)\)\s*;", text):
         params = m.group(2).strip()
         out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
     return out
