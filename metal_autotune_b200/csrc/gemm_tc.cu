@@ -39,6 +39,7 @@
 // MMAs (bounded) and frees its tensor memory.
 #include "mt_common.cuh"
 #include "mt_tma.h"
+#include "qmm_common.cuh"
 
 namespace mt {
 
@@ -62,6 +63,7 @@ struct GemmTcParams {
   int dc[kGtMaxTaps];  // channel offset of each tap
   int mt_per_b, num_mt, num_nt, tiles;
   int bias_fused, vec;
+  int Nout;  // SwiGLU form: output columns (the weight rows are gate/up blocks of 128)
 };
 
 template <int BN>
@@ -236,21 +238,33 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
       const int t = tl.t0 + row;
       const bool live = t < p.Lout;
       const long long yrow = (static_cast<long long>(tl.b) * p.Lout + t) * p.ldy;
+      // SwiGLU form (ACT 2, BN 256): columns [0, 128) of a tile are gate rows,
+      // [128, 256) the up rows of the same 128 outputs
+      constexpr int kChunks = ACT == 2 ? 4 : BN / 32;
+      const int ncol = ACT == 2 ? p.Nout : p.Cout;
 #pragma unroll 1
-      for (int ch = half; ch < BN / 32; ch += 2) {
+      for (int ch = half; ch < kChunks; ch += 2) {
         uint32_t r[32];
         __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
         tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + ch * 32, r);
+        uint32_t r2[ACT == 2 ? 32 : 1];
+        if constexpr (ACT == 2) tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + 128 + ch * 32, r2);
         tmem_wait_ld();
-        const int n0 = tl.n0 * BN + ch * 32;
-        if (!live || n0 >= p.Cout) continue;
+        const int n0 = (ACT == 2 ? tl.n0 * 128 : tl.n0 * BN) + ch * 32;
+        if (!live || n0 >= ncol) continue;
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if constexpr (ACT == 2) {
+          // silu(gate) * up on the rounded products, each op rounded
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            v[i] = round_to<DT>(swiglu_rounded<DT>(round_to<DT>(v[i]), round_to<DT>(__uint_as_float(r2[i]))));
+        }
         // bias, in 16-byte pieces when the chunk is whole
         float bv[32];
         if (bias) {
-          if (p.vec && n0 + 32 <= p.Cout) {
+          if (p.vec && n0 + 32 <= ncol) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const uint4 u = *reinterpret_cast<const uint4*>(bias + n0 + 8 * q);
@@ -264,7 +278,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) bv[i] = n0 + i < p.Cout ? Elem<DT>::to_f(bias[n0 + i]) : 0.f;
+            for (int i = 0; i < 32; ++i) bv[i] = n0 + i < ncol ? Elem<DT>::to_f(bias[n0 + i]) : 0.f;
           }
         }
 #pragma unroll
@@ -275,10 +289,11 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
           else
             u = bias ? round_to<DT>(round_to<DT>(v[i]) + bv[i]) : round_to<DT>(v[i]);
           if (ACT == 1) u = round_to<DT>(gelu_as_f32(u));
+          if (ACT == 2) u = v[i];
           v[i] = u;
         }
         if (res) {
-          if (p.vec && n0 + 32 <= p.Cout) {
+          if (p.vec && n0 + 32 <= ncol) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const uint4 u = *reinterpret_cast<const uint4*>(res + yrow + n0 + 8 * q);
@@ -293,10 +308,10 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (n0 + i < p.Cout) v[i] = round_to<DT>(v[i] + Elem<DT>::to_f(res[yrow + n0 + i]));
+              if (n0 + i < ncol) v[i] = round_to<DT>(v[i] + Elem<DT>::to_f(res[yrow + n0 + i]));
           }
         }
-        if (p.vec && n0 + 32 <= p.Cout) {
+        if (p.vec && n0 + 32 <= ncol) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 u;
@@ -308,7 +323,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc_kernel(const __grid_con
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (n0 + i < p.Cout) y[yrow + n0 + i] = Elem<DT>::from_f(v[i]);
+            if (n0 + i < ncol) y[yrow + n0 + i] = Elem<DT>::from_f(v[i]);
         }
       }
       tc_fence_before();
@@ -337,10 +352,17 @@ int gemm_tc_run(const void* x, const void* w, const void* bias, const void* resi
   const int64_t Lout = (L + 2 * padding - taps) / stride + 1;
   if (Lout < 1 || B < 1) return MT_ERR_UNSUPPORTED;
   if (B * Lout >= (int64_t(1) << 31) || Cout >= (1 << 24) || taps * Cin >= (1 << 24)) return MT_ERR_UNSUPPORTED;
+  // act 2 (SwiGLU): Cout is the output width N; w holds 256 * ceil(N/128)
+  // rows, gate and up rows of each 128 outputs in consecutive blocks of 128
+  const int64_t Nout = Cout;
+  if (act == 2) {
+    if (bias || residual || taps != 1) return MT_ERR_UNSUPPORTED;
+    Cout = 256 * ((Nout + 127) / 128);
+  }
 
   GemmTcParams p;
   memset(&p, 0, sizeof(p));
-  const int BN = Cout <= 128 ? 128 : 256;
+  const int BN = act == 2 || Cout > 128 ? 256 : 128;
   const CUtensorMapDataType dt = dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(Cin * stride), static_cast<uint64_t>(L / stride),
@@ -378,6 +400,7 @@ int gemm_tc_run(const void* x, const void* w, const void* bias, const void* resi
   if (tiles >= (int64_t(1) << 31)) return MT_ERR_UNSUPPORTED;
   p.tiles = static_cast<int>(tiles);
   p.bias_fused = bias_fused;
+  p.Nout = static_cast<int>(Nout);
   p.vec = (ldy % 8 == 0) && aligned(y, 16) && (!bias || aligned(bias, 16)) && (!residual || aligned(residual, 16));
   int sms = 148;
   if (int e = device_sm_count(&sms)) return e;
@@ -393,6 +416,7 @@ int gemm_tc_run(const void* x, const void* w, const void* bias, const void* resi
     return act ? run(gemm_tc_kernel<MT_F16, 128, 1>, sm) : run(gemm_tc_kernel<MT_F16, 128, 0>, sm);
   }
   const size_t sm = GtSmem<256>::kTotal;
+  if (act == 2) return bf ? run(gemm_tc_kernel<MT_BF16, 256, 2>, sm) : run(gemm_tc_kernel<MT_F16, 256, 2>, sm);
   if (bf) return act ? run(gemm_tc_kernel<MT_BF16, 256, 1>, sm) : run(gemm_tc_kernel<MT_BF16, 256, 0>, sm);
   return act ? run(gemm_tc_kernel<MT_F16, 256, 1>, sm) : run(gemm_tc_kernel<MT_F16, 256, 0>, sm);
 }

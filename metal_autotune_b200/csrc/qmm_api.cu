@@ -125,7 +125,8 @@ static int run_tc_blocked(const QmmRequest& r, cudaStream_t stream) {
 // kernel dequantises every weight tile once per 128-token tile, so at large M
 // its dequantiser warps bound it near a third of the tensor peak; one
 // HBM-bound dequantisation pass (read N*K*bits/8, write N*K*2 bytes) plus a
-// GEMM near 80% of the peak is the faster form there (Llama-3-8B prefill,
+// GEMM near 80% of the peak (SwiGLU applied in its epilogue) is the faster
+// form there (Llama-3-8B prefill,
 // M = 16384, 8-bit: gate 1.49 vs 3.68 ms, down 1.44 vs 3.92 ms). The products
 // are the same dequantised weights times x, accumulated in fp32 in another
 // order. MT_QMM_GEMM_MIN_ROWS overrides the threshold (tests use it to compare
@@ -143,13 +144,17 @@ int gemm_tc_run(const void* x, const void* w, const void* bias, const void* resi
                 int bias_fused, int64_t ldy, cudaStream_t stream);
 
 // One thread per 16-byte chunk of packed weights (32 values at 4 bits, 16 at
-// 8): out[n, k] = round(round(s * q) + b), rows of K values.
+// 8): out[row, k] = round(round(s * q) + b), rows of K values. Weight row n
+// goes to row n, or with inter >= 0 (the SwiGLU pair) to row
+// 256 * (n / 128) + inter + n % 128: gate (inter 0) and up (inter 128) rows
+// of the same 128 outputs side by side, as the GEMM's SwiGLU epilogue reads
+// them.
 template <int DT, int BITS>
 __global__ void __launch_bounds__(256) dequant_rows_kernel(const uint8_t* __restrict__ w,
                                                            const uint16_t* __restrict__ s,
                                                            const uint16_t* __restrict__ b,
                                                            uint4* __restrict__ out, int64_t N, int K, int G,
-                                                           int gshift) {
+                                                           int gshift, int inter) {
   constexpr int kVals = 128 / BITS;  // values per chunk
   // the previous kernel on the stream may still read `out` (the GEMM of the
   // set before, which shares this buffer)
@@ -174,13 +179,14 @@ __global__ void __launch_bounds__(256) dequant_rows_kernel(const uint8_t* __rest
     }
     uint32_t o[kVals / 2];
     dequant_chunk<DT, BITS>(wv, sf, bf, o);
-    uint4* dst = out + (n * K + static_cast<int64_t>(c) * kVals) / 8;
+    const int64_t orow = inter < 0 ? n : (n >> 7) * 256 + inter + (n & 127);
+    uint4* dst = out + (orow * K + static_cast<int64_t>(c) * kVals) / 8;
 #pragma unroll
     for (int v = 0; v < kVals / 8; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
   }
 }
 
-static int dequant_rows(const QmmSetReq& q, int64_t K, int group, int bits, int dtype, void* out,
+static int dequant_rows(const QmmSetReq& q, int64_t K, int group, int bits, int dtype, void* out, int inter,
                         cudaStream_t stream) {
   int sms = 148;
   if (int rc = device_sm_count(&sms)) return rc;
@@ -194,10 +200,10 @@ static int dequant_rows(const QmmSetReq& q, int64_t K, int group, int bits, int 
   auto* o = static_cast<uint4*>(out);
   const int k = static_cast<int>(K);
   if (dtype == MT_BF16)
-    return bits == 4 ? launch(dequant_rows_kernel<MT_BF16, 4>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift)
-                     : launch(dequant_rows_kernel<MT_BF16, 8>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift);
-  return bits == 4 ? launch(dequant_rows_kernel<MT_F16, 4>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift)
-                   : launch(dequant_rows_kernel<MT_F16, 8>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift);
+    return bits == 4 ? launch(dequant_rows_kernel<MT_BF16, 4>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift, inter)
+                     : launch(dequant_rows_kernel<MT_BF16, 8>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift, inter);
+  return bits == 4 ? launch(dequant_rows_kernel<MT_F16, 4>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift, inter)
+                   : launch(dequant_rows_kernel<MT_F16, 8>, grid, dim3(256), 0, stream, w, s, b, o, q.N, k, G, gshift, inter);
 }
 
 // The path's buffers sit past the fused kernel's workspace area, whose
@@ -206,9 +212,11 @@ static size_t gemm_ws_offset(int64_t M, int64_t n_total, int64_t K, int bits, in
   return (qmm_tc_workspace(M, n_total, K, bits, kind) + 4095) / 4096 * 4096;
 }
 static size_t gemm_ws_bytes(int64_t M, int64_t n_total, int64_t K, int kind) {
-  // one set's dequantised weights (n_total bounds every set), and for SwiGLU
-  // the gate and up products
-  return static_cast<size_t>(n_total) * K * 2 + (kind == 1 ? static_cast<size_t>(M) * n_total * 2 : 0);
+  (void)M;
+  // one set's dequantised weights (n_total bounds every set); for SwiGLU the
+  // gate and up rows interleaved in blocks of 128 (n_total = 2N)
+  const int64_t rows = kind == 1 ? 256 * ((n_total / 2 + 127) / 128) : n_total;
+  return static_cast<size_t>(rows) * K * 2;
 }
 
 // MT_ERR_UNSUPPORTED (nothing written) when the request does not fit this
@@ -220,27 +228,21 @@ static int run_dequant_gemm(const QmmRequest& r, cudaStream_t stream) {
   const int kind = dual ? 1 : 0;
   const size_t off = gemm_ws_offset(r.M, n_total, r.K, r.bits, kind);
   if (!r.ws || r.ws_bytes < off + gemm_ws_bytes(r.M, n_total, r.K, kind)) return MT_ERR_UNSUPPORTED;
-  if (dual && r.set[0].ldy > 0 && r.set[0].ldy != r.set[0].N) return MT_ERR_UNSUPPORTED;
   char* wbuf = static_cast<char*>(r.ws) + off;
-  const int64_t esz = 2;
   if (dual) {
+    // gate and up rows interleaved in 128-row blocks, one GEMM whose epilogue
+    // applies SwiGLU to each (gate, up) column pair
     const int64_t N = r.set[0].N;
-    char* tmp_g = wbuf + static_cast<size_t>(n_total) * r.K * esz;
-    char* tmp_u = tmp_g + static_cast<size_t>(r.M) * N * esz;
-    void* tmps[2] = {tmp_g, tmp_u};
-    for (int s = 0; s < 2; ++s) {
-      if (int rc = dequant_rows(r.set[s], r.K, r.group, r.bits, r.dtype, wbuf, stream)) return rc;
-      if (int rc = gemm_tc_run(r.x, wbuf, nullptr, nullptr, tmps[s], 1, r.M, r.K, N, 1, 1, 0, 0, r.dtype, 1, N,
-                               stream))
-        return rc;
-    }
-    return mt_swiglu(tmp_g, tmp_u, r.set[0].y, r.M * N, r.dtype, stream);
+    const int64_t ldy = r.set[0].ldy > 0 ? r.set[0].ldy : N;
+    for (int s = 0; s < 2; ++s)
+      if (int rc = dequant_rows(r.set[s], r.K, r.group, r.bits, r.dtype, wbuf, 128 * s, stream)) return rc;
+    return gemm_tc_run(r.x, wbuf, nullptr, nullptr, r.set[0].y, 1, r.M, r.K, N, 1, 1, 0, 2, r.dtype, 1, ldy, stream);
   }
   for (int s = 0; s < 3; ++s) {
     const QmmSetReq& q = r.set[s];
     if (q.N == 0) continue;
     const int64_t ldy = q.ldy > 0 ? q.ldy : q.N;
-    if (int rc = dequant_rows(q, r.K, r.group, r.bits, r.dtype, wbuf, stream)) return rc;
+    if (int rc = dequant_rows(q, r.K, r.group, r.bits, r.dtype, wbuf, -1, stream)) return rc;
     const void* res = r.kind == QMM_RESIDUAL ? r.residual : nullptr;
     if (int rc = gemm_tc_run(r.x, wbuf, nullptr, res, q.y, 1, r.M, r.K, q.N, 1, 1, 0, 0, r.dtype, 1, ldy, stream))
       return rc;
