@@ -695,6 +695,31 @@ def llama_tp_record(cfg, B, L, steps, warmup, rank, world, local, overlap=True):
     return rec
 
 
+def llama_launch_list(cfg, B, L, steps, warmup, rank, world):
+    """W forwards, then K inside the NVTX range 'forward' (for ncu --nvtx
+    --nvtx-include forward/), and exit."""
+    import torch
+
+    from metal_autotune_b200 import workload
+    from metal_autotune_b200.targets import llama_tp
+    comm = llama_tp.ProcessGroupComm() if world > 1 else llama_tp.LocalComm()
+    model = llama_tp.LlamaTP(cfg, world, [rank], comm, seed=0, device="cuda")
+    tokens = workload.seeded_tokens((B, L), 0, cfg.vocab, seed=0)
+    for _ in range(warmup):
+        model(tokens)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("forward")
+    for _ in range(steps):
+        model(tokens)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    log(f"launch list: {steps} forward(s)")
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
 def run_llama_tp(args):
     """The Llama-3-8B tensor-parallel forward as its own JSON line."""
     from metal_autotune_b200 import build
@@ -703,6 +728,8 @@ def run_llama_tp(args):
     rank, world, local = dist_setup()
     cfg = llama_tp.LLAMA3_8B if args.config == "llama3_8b_tp" else llama_tp.TINY
     B, L = (LLAMA_B, LLAMA_L) if cfg.layers == 32 else (2, 128)
+    if args.launch_list:
+        return llama_launch_list(cfg, B, L, args.steps, args.warmup, rank, world)
     rec = llama_tp_record(cfg, B, L, args.steps, args.warmup, rank, world, local, overlap=not args.no_overlap)
     if rank == 0:
         line = {"metric": "Llama-3-8B-8bit prefill tok/s (batch 8 x 2048), tensor-parallel",
@@ -966,8 +993,8 @@ def main():
     ap.add_argument("--no-overlap", action="store_true",
                     help="Llama TP: all-reduces between the blocks instead of overlapped with the other micro-batch")
     ap.add_argument("--launch-list", action="store_true",
-                    help="replay the request W + K times, the K inside an NVTX range 'request', and exit "
-                         "(for ncu --nvtx --nvtx-include request/)")
+                    help="replay the request W + K times, the K inside an NVTX range 'request' ('forward' for "
+                         "the Llama line), and exit (for ncu --nvtx --nvtx-include request/)")
     args = ap.parse_args()
     llama = args.config.startswith("llama")
     if args.steps is None:
