@@ -27,12 +27,16 @@
 // copies' zero fill; such keys are masked, such rows not stored. Causal
 // blocks past the diagonal are never loaded.
 //
-// Roles (192 threads): warp 0 issues the TMA copies (Q once, K/V per block
-// into a 2-stage ring), warp 1 owns the tensor memory and issues the MMAs
+// Roles (192 threads): warp 0 issues the TMA copies (Q once, then K and V
+// per block into 2-stage rings of their own, K one block ahead of V: a K
+// stage is free again once its S = Q K^T has completed, a V stage only after
+// its P V), warp 1 owns the tensor memory and issues the MMAs
 // from one elected lane, warps 2-5 run the softmax, the O rescaling and the
 // final normalisation and store. Every mbarrier wait is bounded (2 s); on
 // expiry the CTA records a site code in the device status word, drains its
-// in-flight copies and MMAs (bounded) and frees its tensor memory.
+// in-flight copies and MMAs (bounded) and frees its tensor memory. Query
+// blocks run last-first, so under the causal mask the CTAs with the most key
+// blocks start first.
 #include "mt_common.cuh"
 #include "mt_tma.h"
 
@@ -60,9 +64,8 @@ template <int D>
 struct AtSmem {
   static constexpr int kTile = 128 * D * 2;            // one 128-row tile, D/64 slabs of 16 KB
   static constexpr int kQ = kTile;
-  static constexpr int kStage = 2 * kTile;             // K and V of one block
   static constexpr int kBars = 1024;
-  static constexpr int kUsed = kQ + kAtStages * kStage + kBars + 1024;
+  static constexpr int kUsed = kQ + 2 * kAtStages * kTile + kBars + 1024;  // Q, K ring, V ring
   // at least 120 KB so one CTA holds an SM (its tensor memory is all 512 columns)
   static constexpr int kTotal = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
 };
@@ -80,12 +83,15 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
   extern __shared__ uint8_t at_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;
-  uint8_t* ring = smem + S::kQ;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kAtStages * S::kStage);
+  uint8_t* kring = smem + S::kQ;
+  uint8_t* vring = kring + kAtStages * S::kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vring + kAtStages * S::kTile);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;               // [stages]
-  uint64_t* kv_empty = kv_full + kAtStages;   // [stages]
-  uint64_t* s_full = kv_empty + kAtStages;    // [2]
+  uint64_t* k_full = bars + 1;                // [stages]
+  uint64_t* k_empty = k_full + kAtStages;     // [stages]
+  uint64_t* v_full = k_empty + kAtStages;     // [stages]
+  uint64_t* v_empty = v_full + kAtStages;     // [stages]
+  uint64_t* s_full = v_empty + kAtStages;     // [2]
   uint64_t* s_free = s_full + 2;              // [2]
   uint64_t* p_full = s_free + 2;              // [2]
   uint64_t* pv_done = p_full + 2;             // [2]
@@ -94,7 +100,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int qblk = static_cast<int>(gridDim.x - 1 - blockIdx.x), h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.Hq / p.Hkv);
   const int q0 = qblk * kAtBQ;
   // keys this block can see: [0, kv_end)
@@ -108,8 +114,10 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kAtStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -139,35 +147,44 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    int issued = 0;
+    int k_issued = 0, v_issued = 0;
     bool ok = true;
+    // one K or V block copy into stage j % kAtStages of its ring
+    auto copy = [&](bool is_v, int j) -> bool {
+      const int st = j % kAtStages;
+      uint64_t* empty = is_v ? v_empty : k_empty;
+      uint64_t* full = is_v ? v_full : k_full;
+      if (!mbar_wait_warp(&empty[st], ((j / kAtStages) & 1) ^ 1, abort_flag, is_v ? 0x70a : 0x701)) return false;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&full[st], S::kTile);
+        tma_load_5d((is_v ? vring : kring) + st * S::kTile, is_v ? &p.tv : &p.tk, &full[st], 0, j * kAtBK, 0, kvh,
+                    b);
+      }
+      __syncwarp();
+      ++(is_v ? v_issued : k_issued);
+      return true;
+    };
     if (nb > 0) {
       if (elect_one()) {
         mbar_arrive_expect_tx(q_full, S::kQ);
         tma_load_5d(sq, &p.tq, q_full, 0, q0, 0, h, b);
       }
       __syncwarp();
-      for (int j = 0; j < nb; ++j) {
-        const int st = j % kAtStages;
-        if (!mbar_wait_warp(&kv_empty[st], ((j / kAtStages) & 1) ^ 1, abort_flag, 0x701)) {
+      ok = copy(false, 0);
+      for (int j = 0; j < nb && ok; ++j) {
+        if (j + 1 < nb && !copy(false, j + 1)) {
           ok = false;
           break;
         }
-        if (elect_one()) {
-          uint8_t* kd = ring + st * S::kStage;
-          mbar_arrive_expect_tx(&kv_full[st], S::kStage);
-          tma_load_5d(kd, &p.tk, &kv_full[st], 0, j * kAtBK, 0, kvh, b);
-          tma_load_5d(kd + S::kTile, &p.tv, &kv_full[st], 0, j * kAtBK, 0, kvh, b);
-        }
-        __syncwarp();
-        ++issued;
+        ok = copy(true, j);
       }
     }
     if (!ok) {
       mbar_wait_drain(q_full, 0, 200000000ull);
-      const int first = issued > kAtStages ? issued - kAtStages : 0;
-      for (int i = first; i < issued; ++i)
-        mbar_wait_drain(&kv_full[i % kAtStages], static_cast<uint32_t>((i / kAtStages) & 1), 200000000ull);
+      for (int i = (k_issued > kAtStages ? k_issued - kAtStages : 0); i < k_issued; ++i)
+        mbar_wait_drain(&k_full[i % kAtStages], static_cast<uint32_t>((i / kAtStages) & 1), 200000000ull);
+      for (int i = (v_issued > kAtStages ? v_issued - kAtStages : 0); i < v_issued; ++i)
+        mbar_wait_drain(&v_full[i % kAtStages], static_cast<uint32_t>((i / kAtStages) & 1), 200000000ull);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -188,10 +205,10 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
     bool issued_any = false;
     auto issue_s = [&](int j) -> bool {
       const int st = j % kAtStages, sb = j & 1;
-      if (!mbar_wait_warp(&kv_full[st], (j / kAtStages) & 1, abort_flag, 0x703)) return false;
+      if (!mbar_wait_warp(&k_full[st], (j / kAtStages) & 1, abort_flag, 0x703)) return false;
       if (!mbar_wait_warp(&s_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, 0x704)) return false;
       tc_fence_after();
-      const uint64_t kdesc = smem_desc_k_sw128(smem_addr(ring + st * S::kStage));
+      const uint64_t kdesc = smem_desc_k_sw128(smem_addr(kring + st * S::kTile));
       if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -199,6 +216,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
           tc_mma_ss(tmem + kAtColS + sb * kAtBK, qdesc + off, kdesc + off, id_s, kk > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[sb]);
+        tc_commit(&k_empty[st]);
       }
       __syncwarp();
       issued_any = true;
@@ -211,18 +229,19 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
         break;
       }
       const int st = j % kAtStages, pb = j & 1;
-      if (!mbar_wait_warp(&p_full[pb], (j >> 1) & 1, abort_flag, 0x705)) {
+      if (!mbar_wait_warp(&v_full[st], (j / kAtStages) & 1, abort_flag, 0x70b) ||
+          !mbar_wait_warp(&p_full[pb], (j >> 1) & 1, abort_flag, 0x705)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t vaddr = smem_addr(ring + st * S::kStage + S::kTile);
+      const uint32_t vaddr = smem_addr(vring + st * S::kTile);
       if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < kAtBK / 16; ++kk)
           tc_mma_ts(tmem + kAtColO, tmem + kAtColP + pb * 64 + kk * 8, vdesc_of(vaddr + kk * 2048), id_pv,
                     (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&kv_empty[st]);
+        tc_commit(&v_empty[st]);
         tc_commit(&pv_done[pb]);
       }
       __syncwarp();
@@ -249,15 +268,16 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
         break;
       }
       tc_fence_after();
+      // the row's 128 scores: four loads in flight, one wait
       float sv[kAtBK];
+      uint32_t r[kAtBK / 32][32];
 #pragma unroll
-      for (int c = 0; c < kAtBK / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_off + kAtColS + sb * kAtBK + c * 32, r);
-        tmem_wait_ld();
+      for (int c = 0; c < kAtBK / 32; ++c) tmem_ld32(tmem + lane_off + kAtColS + sb * kAtBK + c * 32, r[c]);
+      tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
-      }
+      for (int c = 0; c < kAtBK / 32; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[c][i]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
