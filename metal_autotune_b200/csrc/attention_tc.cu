@@ -283,22 +283,24 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
       if (lane == 0) mbar_arrive(&s_free[sb]);
       const int k0 = j * kAtBK;
       const bool edge = k0 + kAtBK > p.Lk || (p.causal && k0 + kAtBK - 1 > p.q_offset + q0);
-      float mx = -INFINITY;
       if (edge) {
 #pragma unroll
         for (int i = 0; i < kAtBK; ++i) {
           const int64_t key = k0 + i;
           const bool vis = key < p.Lk && (!p.causal || key <= qpos);
-          sv[i] = vis ? sv[i] * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, sv[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kAtBK; ++i) {
-          sv[i] *= p.scale_log2;
-          mx = fmaxf(mx, sv[i]);
+          if (!vis) sv[i] = -INFINITY;
         }
       }
+      // the block's maximum of the raw scores in 8 independent chains (one
+      // warp per scheduler: a single chain of 128 would expose each step's
+      // latency); scale > 0, so it scales to the maximum of the scaled scores
+      float mxk[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mxk[u] = sv[u];
+#pragma unroll
+      for (int i = 8; i < kAtBK; ++i) mxk[i & 7] = fmaxf(mxk[i & 7], sv[i]);
+      const float mx = fmaxf(fmaxf(fmaxf(mxk[0], mxk[1]), fmaxf(mxk[2], mxk[3])),
+                             fmaxf(fmaxf(mxk[4], mxk[5]), fmaxf(mxk[6], mxk[7]))) * p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       const bool need = j > 0 && m_new > m_run + kAtRescale;
       if (j == 0) {
@@ -331,21 +333,26 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
         ok = false;
         break;
       }
-      float rs = 0.f;
+      // p = 2^(s * scale - m), the scale folded into one FMA; the row sum in
+      // 8 independent chains
+      float rsk[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) rsk[u] = 0.f;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float e0 = ex2_approx(sv[c * 64 + 2 * i] - m_run);
-          const float e1 = ex2_approx(sv[c * 64 + 2 * i + 1] - m_run);
-          rs += e0 + e1;
+          const float e0 = ex2_approx(fmaf(sv[c * 64 + 2 * i], p.scale_log2, -m_run));
+          const float e1 = ex2_approx(fmaf(sv[c * 64 + 2 * i + 1], p.scale_log2, -m_run));
+          rsk[(2 * i) & 7] += e0;
+          rsk[(2 * i + 1) & 7] += e1;
           typename Elem<DT>::T2 t2 = Elem<DT>::pack2(e0, e1);
           pk[i] = *reinterpret_cast<uint32_t*>(&t2);
         }
         tmem_st32(tmem + lane_off + kAtColP + sb * 64 + c * 32, pk);
       }
-      l_run += rs;
+      l_run += ((rsk[0] + rsk[1]) + (rsk[2] + rsk[3])) + ((rsk[4] + rsk[5]) + (rsk[6] + rsk[7]));
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -411,6 +418,7 @@ int attn_tc_run(const void* q, const void* k, const void* v, void* o, int64_t B,
                 int64_t qs_l, int64_t ks_b, int64_t ks_h, int64_t ks_l, int64_t vs_b, int64_t vs_h, int64_t vs_l,
                 int64_t os_b, int64_t os_h, int64_t os_l, int dtype, cudaStream_t stream) {
   if ((D != 64 && D != 128) || (dtype != MT_BF16 && dtype != MT_F16)) return MT_ERR_UNSUPPORTED;
+  if (!(scale > 0.f)) return MT_ERR_UNSUPPORTED;  // the kernel folds a positive scale into its exponent
   const int64_t st[9] = {qs_b, qs_h, qs_l, ks_b, ks_h, ks_l, vs_b, vs_h, vs_l};
   for (int64_t s : st)
     if (s <= 0 || s % 8 != 0) return MT_ERR_UNSUPPORTED;
