@@ -2,7 +2,9 @@
 // (flash attention forward: tcgen05.mma with tensor-memory accumulators,
 // TMA-staged Q/K/V, online softmax).
 //
-// One CTA = 128 query rows of one (batch, head); KV blocks of 128 keys.
+// Work item = 128 query rows of one (batch, head); KV blocks of 128 keys. A
+// persistent grid (one CTA per SM) walks the items heaviest first, so the
+// next item's Q copy and first S = Q K^T overlap this item's O store.
 //   S_j = Q K_j^T        tcgen05.mma, A = Q and B = K_j from shared memory
 //                        (K-major, 128-byte swizzle), fp32 S in tensor memory
 //                        (two buffers, so S_{j+1} is computed while the
@@ -34,9 +36,7 @@
 // from one elected lane, warps 2-5 run the softmax, the O rescaling and the
 // final normalisation and store. Every mbarrier wait is bounded (2 s); on
 // expiry the CTA records a site code in the device status word, drains its
-// in-flight copies and MMAs (bounded) and frees its tensor memory. Query
-// blocks run last-first, so under the causal mask the CTAs with the most key
-// blocks start first.
+// in-flight copies and MMAs (bounded) and frees its tensor memory.
 #include "mt_common.cuh"
 #include "mt_tma.h"
 
@@ -58,6 +58,7 @@ struct AttnTcParams {
   int64_t q_offset;
   float scale_log2;
   int causal, vec;
+  int B, nq, tiles;  // batch, query blocks per (batch, head), work items = nq * Hq * B
 };
 
 template <int D>
@@ -76,6 +77,30 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Work item `id` of the persistent grid: query block, head, batch and the
+// number of key blocks it sees. Items run heaviest first: the last query
+// block of every (head, batch) before the one before it, and so on.
+struct AtTile {
+  int q0, h, b, kvh, nb;
+};
+__device__ __forceinline__ AtTile at_tile(const AttnTcParams& p, int id) {
+  const int hb = p.Hq * p.B;
+  const int qi = id / hb;
+  const int r = id - qi * hb;
+  AtTile t;
+  t.q0 = (p.nq - 1 - qi) * kAtBQ;
+  t.h = r % p.Hq;
+  t.b = r / p.Hq;
+  t.kvh = t.h / (p.Hq / p.Hkv);
+  int64_t kv_end = p.Lk;  // keys this block can see: [0, kv_end)
+  if (p.causal) {
+    const int64_t lim = p.q_offset + t.q0 + kAtBQ;
+    if (lim < kv_end) kv_end = lim < 0 ? 0 : lim;
+  }
+  t.nb = static_cast<int>((kv_end + kAtBK - 1) / kAtBK);
+  return t;
+}
+
 template <int DT, int D>
 __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_constant__ AttnTcParams p) {
   using T = typename Elem<DT>::T;
@@ -87,7 +112,9 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
   uint8_t* vring = kring + kAtStages * S::kTile;
   uint64_t* bars = reinterpret_cast<uint64_t*>(vring + kAtStages * S::kTile);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;                // [stages]
+  uint64_t* q_empty = bars + 1;               // Q read by the tile's last S
+  uint64_t* o_free = bars + 2;                // O read out by the softmax warps
+  uint64_t* k_full = bars + 3;                // [stages]
   uint64_t* k_empty = k_full + kAtStages;     // [stages]
   uint64_t* v_full = k_empty + kAtStages;     // [stages]
   uint64_t* v_empty = v_full + kAtStages;     // [stages]
@@ -100,19 +127,10 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qblk = static_cast<int>(gridDim.x - 1 - blockIdx.x), h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / (p.Hq / p.Hkv);
-  const int q0 = qblk * kAtBQ;
-  // keys this block can see: [0, kv_end)
-  int64_t kv_end = p.Lk;
-  if (p.causal) {
-    const int64_t lim = p.q_offset + q0 + kAtBQ;
-    if (lim < kv_end) kv_end = lim < 0 ? 0 : lim;
-  }
-  const int nb = static_cast<int>((kv_end + kAtBK - 1) / kAtBK);
-
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_free, 4);
     for (int s = 0; s < kAtStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -145,45 +163,56 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
   griddep_wait();
   griddep_launch();
 
+  // Counters shared by all roles, over the work items with at least one key
+  // block: qt counts items, g counts key blocks (ring stage g % kAtStages,
+  // S / P buffer g & 1).
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    int k_issued = 0, v_issued = 0;
+    int qt = 0, kc = 0, vc = 0;
     bool ok = true;
-    // one K or V block copy into stage j % kAtStages of its ring
-    auto copy = [&](bool is_v, int j) -> bool {
-      const int st = j % kAtStages;
+    // one K or V block copy into the next stage of its ring
+    auto copy = [&](bool is_v, const AtTile& t, int j) -> bool {
+      int& c = is_v ? vc : kc;
+      const int st = c % kAtStages;
       uint64_t* empty = is_v ? v_empty : k_empty;
       uint64_t* full = is_v ? v_full : k_full;
-      if (!mbar_wait_warp(&empty[st], ((j / kAtStages) & 1) ^ 1, abort_flag, is_v ? 0x70a : 0x701)) return false;
+      if (!mbar_wait_warp(&empty[st], ((c / kAtStages) & 1) ^ 1, abort_flag, is_v ? 0x70a : 0x701)) return false;
       if (elect_one()) {
         mbar_arrive_expect_tx(&full[st], S::kTile);
-        tma_load_5d((is_v ? vring : kring) + st * S::kTile, is_v ? &p.tv : &p.tk, &full[st], 0, j * kAtBK, 0, kvh,
-                    b);
+        tma_load_5d((is_v ? vring : kring) + st * S::kTile, is_v ? &p.tv : &p.tk, &full[st], 0, j * kAtBK, 0, t.kvh,
+                    t.b);
       }
       __syncwarp();
-      ++(is_v ? v_issued : k_issued);
+      ++c;
       return true;
     };
-    if (nb > 0) {
+    for (int id = blockIdx.x; id < p.tiles && ok; id += gridDim.x) {
+      const AtTile t = at_tile(p, id);
+      if (t.nb == 0) continue;
+      if (!mbar_wait_warp(q_empty, (qt & 1) ^ 1, abort_flag, 0x70c)) {
+        ok = false;
+        break;
+      }
       if (elect_one()) {
         mbar_arrive_expect_tx(q_full, S::kQ);
-        tma_load_5d(sq, &p.tq, q_full, 0, q0, 0, h, b);
+        tma_load_5d(sq, &p.tq, q_full, 0, t.q0, 0, t.h, t.b);
       }
       __syncwarp();
-      ok = copy(false, 0);
-      for (int j = 0; j < nb && ok; ++j) {
-        if (j + 1 < nb && !copy(false, j + 1)) {
+      ++qt;
+      ok = copy(false, t, 0);
+      for (int j = 0; j < t.nb && ok; ++j) {
+        if (j + 1 < t.nb && !copy(false, t, j + 1)) {
           ok = false;
           break;
         }
-        ok = copy(true, j);
+        ok = copy(true, t, j);
       }
     }
     if (!ok) {
-      mbar_wait_drain(q_full, 0, 200000000ull);
-      for (int i = (k_issued > kAtStages ? k_issued - kAtStages : 0); i < k_issued; ++i)
+      if (qt > 0) mbar_wait_drain(q_full, static_cast<uint32_t>((qt - 1) & 1), 200000000ull);
+      for (int i = (kc > kAtStages ? kc - kAtStages : 0); i < kc; ++i)
         mbar_wait_drain(&k_full[i % kAtStages], static_cast<uint32_t>((i / kAtStages) & 1), 200000000ull);
-      for (int i = (v_issued > kAtStages ? v_issued - kAtStages : 0); i < v_issued; ++i)
+      for (int i = (vc > kAtStages ? vc - kAtStages : 0); i < vc; ++i)
         mbar_wait_drain(&v_full[i % kAtStages], static_cast<uint32_t>((i / kAtStages) & 1), 200000000ull);
     }
   } else if (warp == 1) {
@@ -201,12 +230,13 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
       d |= static_cast<uint64_t>(2) << 61;
       return d;
     };
-    bool ok = nb > 0 && mbar_wait_warp(q_full, 0, abort_flag, 0x702);
-    bool issued_any = false;
-    auto issue_s = [&](int j) -> bool {
-      const int st = j % kAtStages, sb = j & 1;
-      if (!mbar_wait_warp(&k_full[st], (j / kAtStages) & 1, abort_flag, 0x703)) return false;
-      if (!mbar_wait_warp(&s_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, 0x704)) return false;
+    bool ok = true, issued_any = false;
+    int qt = 0, gs = 0, gp = 0;  // items, S blocks and P V blocks issued
+    // S = Q K^T of the next key block; after the item's last one, Q is free
+    auto issue_s = [&](bool last) -> bool {
+      const int st = gs % kAtStages, sb = gs & 1;
+      if (!mbar_wait_warp(&k_full[st], (gs / kAtStages) & 1, abort_flag, 0x703)) return false;
+      if (!mbar_wait_warp(&s_free[sb], ((gs >> 1) & 1) ^ 1, abort_flag, 0x704)) return false;
       tc_fence_after();
       const uint64_t kdesc = smem_desc_k_sw128(smem_addr(kring + st * S::kTile));
       if (elect_one()) {
@@ -217,34 +247,48 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
         }
         tc_commit(&s_full[sb]);
         tc_commit(&k_empty[st]);
+        if (last) tc_commit(q_empty);
       }
       __syncwarp();
       issued_any = true;
+      ++gs;
       return true;
     };
-    if (ok) ok = issue_s(0);
-    for (int j = 0; j < nb && ok; ++j) {
-      if (j + 1 < nb && !issue_s(j + 1)) {
+    for (int id = blockIdx.x; id < p.tiles && ok; id += gridDim.x) {
+      const AtTile t = at_tile(p, id);
+      if (t.nb == 0) continue;
+      if (!mbar_wait_warp(q_full, qt & 1, abort_flag, 0x702)) {
         ok = false;
         break;
       }
-      const int st = j % kAtStages, pb = j & 1;
-      if (!mbar_wait_warp(&v_full[st], (j / kAtStages) & 1, abort_flag, 0x70b) ||
-          !mbar_wait_warp(&p_full[pb], (j >> 1) & 1, abort_flag, 0x705)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t vaddr = smem_addr(vring + st * S::kTile);
-      if (elect_one()) {
+      ok = issue_s(t.nb == 1);
+      for (int j = 0; j < t.nb && ok; ++j) {
+        if (j + 1 < t.nb && !issue_s(j + 2 == t.nb)) {
+          ok = false;
+          break;
+        }
+        const int st = gp % kAtStages, pb = gp & 1;
+        // the item's first P V overwrites O: the previous item's O must have been read out
+        if ((j == 0 && !mbar_wait_warp(o_free, (qt & 1) ^ 1, abort_flag, 0x70d)) ||
+            !mbar_wait_warp(&v_full[st], (gp / kAtStages) & 1, abort_flag, 0x70b) ||
+            !mbar_wait_warp(&p_full[pb], (gp >> 1) & 1, abort_flag, 0x705)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t vaddr = smem_addr(vring + st * S::kTile);
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kAtBK / 16; ++kk)
-          tc_mma_ts(tmem + kAtColO, tmem + kAtColP + pb * 64 + kk * 8, vdesc_of(vaddr + kk * 2048), id_pv,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&v_empty[st]);
-        tc_commit(&pv_done[pb]);
+          for (int kk = 0; kk < kAtBK / 16; ++kk)
+            tc_mma_ts(tmem + kAtColO, tmem + kAtColP + pb * 64 + kk * 8, vdesc_of(vaddr + kk * 2048), id_pv,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&v_empty[st]);
+          tc_commit(&pv_done[pb]);
+        }
+        __syncwarp();
+        ++gp;
       }
-      __syncwarp();
+      ++qt;
     }
     if (__any_sync(0xffffffffu, *abort_flag != 0) && issued_any) {
       if (elect_one()) {
@@ -257,116 +301,130 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
     // ------------------------------------------------------------ softmax / correction / store
     const int quad = warp & 3;                 // tensor-memory lanes [32*quad, +32)
     const int row = quad * 32 + lane;          // query row within the block
-    const int64_t qpos = p.q_offset + q0 + row;  // absolute position (causal limit)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < nb; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, abort_flag, 0x706)) {
-        ok = false;
-        break;
+    int g = 0;  // key blocks consumed
+    for (int id = blockIdx.x; id < p.tiles && ok; id += gridDim.x) {
+      const AtTile t = at_tile(p, id);
+      T* o = static_cast<T*>(p.o) + t.b * p.os_b + t.h * p.os_h + static_cast<int64_t>(t.q0 + row) * p.os_l;
+      const bool live = t.q0 + row < p.Lq;
+      if (t.nb == 0) {
+        // no visible key (only possible with a negative q_offset): zeros, as the oracle writes
+        if (live)
+          for (int i = 0; i < D; ++i) o[i] = Elem<DT>::from_f(0.f);
+        continue;
       }
-      tc_fence_after();
-      // the row's 128 scores: four loads in flight, one wait
-      float sv[kAtBK];
-      uint32_t r[kAtBK / 32][32];
-#pragma unroll
-      for (int c = 0; c < kAtBK / 32; ++c) tmem_ld32(tmem + lane_off + kAtColS + sb * kAtBK + c * 32, r[c]);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < kAtBK / 32; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[c][i]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
-      const int k0 = j * kAtBK;
-      const bool edge = k0 + kAtBK > p.Lk || (p.causal && k0 + kAtBK - 1 > p.q_offset + q0);
-      if (edge) {
-#pragma unroll
-        for (int i = 0; i < kAtBK; ++i) {
-          const int64_t key = k0 + i;
-          const bool vis = key < p.Lk && (!p.causal || key <= qpos);
-          if (!vis) sv[i] = -INFINITY;
-        }
-      }
-      // the block's maximum of the raw scores in 8 independent chains (one
-      // warp per scheduler: a single chain of 128 would expose each step's
-      // latency); scale > 0, so it scales to the maximum of the scaled scores
-      float mxk[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) mxk[u] = sv[u];
-#pragma unroll
-      for (int i = 8; i < kAtBK; ++i) mxk[i & 7] = fmaxf(mxk[i & 7], sv[i]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxk[0], mxk[1]), fmaxf(mxk[2], mxk[3])),
-                             fmaxf(fmaxf(mxk[4], mxk[5]), fmaxf(mxk[6], mxk[7]))) * p.scale_log2;
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = j > 0 && m_new > m_run + kAtRescale;
-      if (j == 0) {
-        m_run = m_new;
-      } else if (__any_sync(0xffffffffu, need)) {
-        // the previous P V must have landed in O before O is rescaled
-        if (!mbar_wait_warp(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 0x707)) {
+      const int64_t qpos = p.q_offset + t.q0 + row;  // absolute position (causal limit)
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < t.nb; ++j, ++g) {
+        const int sb = g & 1;
+        if (!mbar_wait_warp(&s_full[sb], (g >> 1) & 1, abort_flag, 0x706)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float alpha = need ? exp2f(m_run - m_new) : 1.0f;
-        if (need) {
-          m_run = m_new;
-          l_run *= alpha;
-        }
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_off + kAtColO + c * 32, r);
-          tmem_wait_ld();
+        // the row's 128 scores: four loads in flight, one wait
+        float sv[kAtBK];
+        uint32_t r[kAtBK / 32][32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(tmem + lane_off + kAtColO + c * 32, r);
+        for (int c = 0; c < kAtBK / 32; ++c) tmem_ld32(tmem + lane_off + kAtColS + sb * kAtBK + c * 32, r[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < kAtBK / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[c][i]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);
+        const int k0 = j * kAtBK;
+        const bool edge = k0 + kAtBK > p.Lk || (p.causal && k0 + kAtBK - 1 > p.q_offset + t.q0);
+        if (edge) {
+#pragma unroll
+          for (int i = 0; i < kAtBK; ++i) {
+            const int64_t key = k0 + i;
+            const bool vis = key < p.Lk && (!p.causal || key <= qpos);
+            if (!vis) sv[i] = -INFINITY;
+          }
         }
+        // the block's maximum of the raw scores in 8 independent chains (one
+        // warp per scheduler: a single chain of 128 would expose each step's
+        // latency); scale > 0, so it scales to the maximum of the scaled scores
+        float mxk[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mxk[u] = sv[u];
+#pragma unroll
+        for (int i = 8; i < kAtBK; ++i) mxk[i & 7] = fmaxf(mxk[i & 7], sv[i]);
+        const float mx = fmaxf(fmaxf(fmaxf(mxk[0], mxk[1]), fmaxf(mxk[2], mxk[3])),
+                               fmaxf(fmaxf(mxk[4], mxk[5]), fmaxf(mxk[6], mxk[7]))) * p.scale_log2;
+        const float m_new = fmaxf(m_run, mx);
+        const bool need = j > 0 && m_new > m_run + kAtRescale;
+        if (j == 0) {
+          m_run = m_new;
+        } else if (__any_sync(0xffffffffu, need)) {
+          // the previous P V must have landed in O before O is rescaled
+          if (!mbar_wait_warp(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, abort_flag, 0x707)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float alpha = need ? exp2f(m_run - m_new) : 1.0f;
+          if (need) {
+            m_run = m_new;
+            l_run *= alpha;
+          }
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t ro[32];
+            tmem_ld32(tmem + lane_off + kAtColO + c * 32, ro);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ro[i] = __float_as_uint(__uint_as_float(ro[i]) * alpha);
+            tmem_st32(tmem + lane_off + kAtColO + c * 32, ro);
+          }
+          tmem_wait_st();
+        }
+        // P buffer g % 2 was last read by the P V of key block g - 2
+        if (g >= 2 && !mbar_wait_warp(&pv_done[sb], ((g - 2) >> 1) & 1, abort_flag, 0x708)) {
+          ok = false;
+          break;
+        }
+        // p = 2^(s * scale - m), the scale folded into one FMA; the row sum in
+        // 8 independent chains. A row that sees no key yet (m = -inf, only
+        // with a negative q_offset) gets p = 0 and, at the end, zeros.
+        const float m_use = m_run == -INFINITY ? 0.f : m_run;
+        float rsk[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) rsk[u] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float e0 = ex2_approx(fmaf(sv[c * 64 + 2 * i], p.scale_log2, -m_use));
+            const float e1 = ex2_approx(fmaf(sv[c * 64 + 2 * i + 1], p.scale_log2, -m_use));
+            rsk[(2 * i) & 7] += e0;
+            rsk[(2 * i + 1) & 7] += e1;
+            typename Elem<DT>::T2 t2 = Elem<DT>::pack2(e0, e1);
+            pk[i] = *reinterpret_cast<uint32_t*>(&t2);
+          }
+          tmem_st32(tmem + lane_off + kAtColP + sb * 64 + c * 32, pk);
+        }
+        l_run += ((rsk[0] + rsk[1]) + (rsk[2] + rsk[3])) + ((rsk[4] + rsk[5]) + (rsk[6] + rsk[7]));
         tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[sb]);
       }
-      // P buffer j%2 was last read by P V of block j-2
-      if (j >= 2 && !mbar_wait_warp(&pv_done[sb], ((j - 2) >> 1) & 1, abort_flag, 0x708)) {
+      if (!ok || !mbar_wait_warp(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, abort_flag, 0x709)) {
         ok = false;
         break;
       }
-      // p = 2^(s * scale - m), the scale folded into one FMA; the row sum in
-      // 8 independent chains
-      float rsk[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) rsk[u] = 0.f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e0 = ex2_approx(fmaf(sv[c * 64 + 2 * i], p.scale_log2, -m_run));
-          const float e1 = ex2_approx(fmaf(sv[c * 64 + 2 * i + 1], p.scale_log2, -m_run));
-          rsk[(2 * i) & 7] += e0;
-          rsk[(2 * i + 1) & 7] += e1;
-          typename Elem<DT>::T2 t2 = Elem<DT>::pack2(e0, e1);
-          pk[i] = *reinterpret_cast<uint32_t*>(&t2);
-        }
-        tmem_st32(tmem + lane_off + kAtColP + sb * 64 + c * 32, pk);
-      }
-      l_run += ((rsk[0] + rsk[1]) + (rsk[2] + rsk[3])) + ((rsk[4] + rsk[5]) + (rsk[6] + rsk[7]));
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
-    }
-    if (ok && nb > 0 && mbar_wait_warp(&pv_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, abort_flag, 0x709)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      T* o = static_cast<T*>(p.o) + b * p.os_b + h * p.os_h + static_cast<int64_t>(q0 + row) * p.os_l;
-      const bool live = q0 + row < p.Lq;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_off + kAtColO + c * 32, r);
+        uint32_t ro[32];
+        tmem_ld32(tmem + lane_off + kAtColO + c * 32, ro);
         tmem_wait_ld();
         if (live) {
           if (p.vec) {
@@ -376,22 +434,21 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tc_kernel(const __grid_con
               typename Elem<DT>::T2* hh = reinterpret_cast<typename Elem<DT>::T2*>(&u);
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                hh[e] = Elem<DT>::pack2(__uint_as_float(r[8 * q + 2 * e]) * inv,
-                                        __uint_as_float(r[8 * q + 2 * e + 1]) * inv);
+                hh[e] = Elem<DT>::pack2(__uint_as_float(ro[8 * q + 2 * e]) * inv,
+                                        __uint_as_float(ro[8 * q + 2 * e + 1]) * inv);
               *reinterpret_cast<uint4*>(o + c * 32 + 8 * q) = u;
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[c * 32 + i] = Elem<DT>::from_f(__uint_as_float(r[i]) * inv);
+            for (int i = 0; i < 32; ++i) o[c * 32 + i] = Elem<DT>::from_f(__uint_as_float(ro[i]) * inv);
           }
         }
         __syncwarp();
       }
-    } else if (nb == 0) {
-      // no visible key (only possible with a negative q_offset): zeros, as the oracle writes
-      T* o = static_cast<T*>(p.o) + b * p.os_b + h * p.os_h + static_cast<int64_t>(q0 + row) * p.os_l;
-      if (q0 + row < p.Lq)
-        for (int i = 0; i < D; ++i) o[i] = Elem<DT>::from_f(0.f);
+      // O is read out: the next item's first P V may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);
     }
   }
   tc_fence_before();
@@ -442,8 +499,15 @@ int attn_tc_run(const void* q, const void* k, const void* v, void* o, int64_t B,
   p.scale_log2 = scale * 1.44269504088896341f;
   p.causal = causal;
   p.vec = aligned(o, 16) && os_l % 8 == 0 && os_h % 8 == 0 && os_b % 8 == 0;
-  const dim3 grid(static_cast<unsigned>((Lq + kAtBQ - 1) / kAtBQ), static_cast<unsigned>(Hq),
-                  static_cast<unsigned>(B));
+  p.B = static_cast<int>(B);
+  p.nq = static_cast<int>((Lq + kAtBQ - 1) / kAtBQ);
+  const int64_t tiles = static_cast<int64_t>(p.nq) * Hq * B;
+  if (tiles >= (int64_t(1) << 31)) return MT_ERR_UNSUPPORTED;
+  p.tiles = static_cast<int>(tiles);
+  int sms = 148;
+  if (int e = device_sm_count(&sms)) return e;
+  // persistent: one CTA per SM (each holds all 512 tensor-memory columns)
+  const dim3 grid(static_cast<unsigned>(p.tiles < sms ? p.tiles : sms));
   auto run = [&](auto kern, size_t smem) -> int {
     if (int e = ensure_smem(kern, smem)) return e;
     return launch(kern, grid, dim3(kAtThreads), smem, stream, p);

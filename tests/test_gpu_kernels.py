@@ -225,6 +225,20 @@ def test_sdpa(cuda, oracle, B, Hq, Hkv, Lq, Lk, D, causal):
     assert torch.equal(o2.transpose(1, 2), o)
 
 
+def test_sdpa_rows_before_every_key(cuda, oracle):
+    """q_offset < 0 on the tcgen05 path: the first query blocks see no key at
+    all (zeros, as the oracle writes) and sit in the persistent grid's walk
+    between blocks that do."""
+    B, Hq, Hkv, Lq, Lk, D, off = 1, 4, 2, 400, 384, 128, -200
+    q = oracle.round_to(rng.standard_normal((B, Hq, Lq, D)).astype(np.float32), "bfloat16")
+    k = oracle.round_to(rng.standard_normal((B, Hkv, Lk, D)).astype(np.float32), "bfloat16")
+    v = oracle.round_to(rng.standard_normal((B, Hkv, Lk, D)).astype(np.float32), "bfloat16")
+    o = lib.sdpa(t(q), t(k), t(v), scale=1 / math.sqrt(D), causal=True, q_offset=off)
+    ref = oracle.sdpa(q, k, v, 1 / math.sqrt(D), True, off)
+    assert not np.any(n(o)[:, :, :-off])  # rows 0..199 see no key
+    assert np.abs(n(o) - ref).max() <= 2 ** -7 * np.abs(ref).max() + 4e-3 * np.abs(v).max()
+
+
 # --------------------------------------------------------------- elementwise / gather
 def test_swiglu(cuda, oracle):
     g = oracle.round_to(rng.standard_normal(10001).astype(np.float32) * 4, "bfloat16")
