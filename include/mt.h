@@ -435,7 +435,11 @@ int mt_diff_reduce_noalloc(const void* a, const void* b, int64_t n, int dtype,
  * fp32 sums with the bias added before the one rounding (mx.addmm) and GELU
  * rounded after it (not bit-reproducible: the sums run in tiles). The 16-bit
  * path runs on the tcgen05 GEMM (tensor memory accumulators, TMA-staged
- * operands) when K is a multiple of 8.
+ * operands) when K is a multiple of 8: on pairs of SMs (cta_group::2,
+ * 256 x 256 tiles) once there are at least as many such tiles as SM pairs,
+ * else one SM per 128 x 256 tile; both give the same bits. The environment
+ * variable MT_GEMM_PAIR=0 / 1 forces the choice (this and mt_conv1d,
+ * mt_linear_residual and the quantized matmul from 1024 rows).
  */
 int mt_linear(const void* x, const void* w, const void* bias, void* y,
               int64_t M, int64_t N, int64_t K, int act, int dtype,
