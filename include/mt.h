@@ -218,10 +218,11 @@ int mt_rms_norm_quantized_matmul_swiglu(
  * Bytes of workspace the quantized-matmul entry points need for this shape.
  * `n_total` is the summed N over all sets (2N for the SwiGLU pair);
  * `kind` is 0 (plain/residual/multi) or 1 (SwiGLU pair). From M = 1024 rows
- * up it includes room for one set's dequantised weights (n_total*K elements)
- * and, for the SwiGLU pair, its two [M, N] products: those shapes dequantise
- * the weights once and multiply on the tcgen05 GEMM. Given less than this,
- * they run the fused kernel instead.
+ * up it includes room for one set's dequantised weights (n_total*K elements;
+ * for the SwiGLU pair 256*ceil(N/128)*K: gate and up rows interleaved in
+ * blocks of 128, one GEMM with SwiGLU in its epilogue): those shapes
+ * dequantise the weights once and multiply on the tcgen05 GEMM. Given less
+ * than this, they run the fused kernel instead.
  */
 size_t mt_qmm_workspace_bytes(int64_t M, int64_t n_total, int64_t K, int bits,
                               int kind);
