@@ -5,7 +5,8 @@ sequence on the dequantised weights (every op of the CUDA path rounds to
 bf16, the restatement does not: relative-norm tolerance below); tp = 2 and
 tp = 4, with all shards in this process and the partial sums added in shard
 order, are checked against tp = 1, which they match up to the rounding of
-each shard's partial to bf16 before the sum."""
+each shard's partial to bf16 before the sum; at 384 tokens (the fused
+quantized matmul) and at 1024 (weights dequantised once, tcgen05 GEMM)."""
 from __future__ import annotations
 
 import math
@@ -92,6 +93,24 @@ def test_sharded_matches_tp1(tp1, tp):
     assert _rel(got, ref) < 1e-2
     # the shards are slices of the one seeded model
     assert torch.equal(torch.cat([s.lm_head[0] for s in sharded.shards]), tp1.shards[0].lm_head[0])
+
+
+@pytest.mark.parametrize("tp", [1, 2, 4])
+def test_many_rows_forward(tp1, tp):
+    """1024 tokens: every projection takes the many-rows form (weights
+    dequantised once, tcgen05 GEMM, SwiGLU in the GEMM epilogue) at each
+    shard's widths; tp = 1 against the fp32 restatement, tp > 1 against tp = 1."""
+    tok = _tokens(2, 512)
+    ref = tp1(tok)
+    torch.cuda.synchronize()
+    if tp == 1:
+        assert _rel(ref, _restated(tp1, tok)) < REL_TOL
+        return
+    sharded = llama_tp.LlamaTP(CFG, tp, range(tp), llama_tp.LocalComm(), seed=5)
+    got = sharded(tok)
+    torch.cuda.synchronize()
+    assert lib.device_status(clear=True) == 0
+    assert _rel(got, ref) < 1e-2
 
 
 def test_forward_is_deterministic(tp1):
